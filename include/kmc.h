@@ -1,0 +1,152 @@
+/*
+ * kmc.h -- C ABI of the B200 Lloyd-pass library (libkmc.so, sm_100a).
+ *
+ * Drop-in boundary for the hot path of kakollu/mlx-kmeans.  The reference has no C/FFI layer: its
+ * boundary is three Python functions in mlx_kmeans/core.py, and each entry point below names the one
+ * it replaces.  A ctypes binding (mlx_kmeans_b200/_lib.py) puts the same Python signatures back on top.
+ *
+ * Conventions
+ *   - Every pointer marked (device) is a device pointer on the current CUDA device; (host) pointers are
+ *     ordinary host memory.  `stream` is a cudaStream_t passed as void* (0 = legacy default stream).
+ *   - Calls only enqueue work on `stream`; none synchronises, except kmc_stats_read which copies the
+ *     statistics back and waits for them.
+ *   - Every call returns KMC_OK (0) or an error code; nothing is thrown across the ABI.  The message of
+ *     the last failure on the calling thread is kmc_last_error().
+ *   - The library allocates nothing on its own for these calls: the caller passes device workspaces
+ *     (256-byte aligned) of the sizes the *_workspace_bytes functions give.
+ *
+ * Numeric contract (the reference's, see core.py:218-219 and tests/accuracy.py:31-51):
+ *   label = the center with the smallest float64 distance sum_j ((double)x_j - (double)c_j)^2 (NumPy's
+ *   pairwise summation order), lowest index on exact ties; best = the float32 distance to that center,
+ *   each square and add rounded on its own; totals are exact and independent of summation order.
+ */
+#ifndef KMC_H
+#define KMC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum kmc_status {
+    KMC_OK = 0,
+    KMC_ERR_INVALID = 1,      /* bad shape, null pointer, workspace too small (ValueError in Python) */
+    KMC_ERR_CUDA = 2,         /* a CUDA call failed (RuntimeError in Python) */
+    KMC_ERR_UNSUPPORTED = 3,  /* shape outside what the library handles (d > KMC_MAX_DIMS) */
+};
+
+#define KMC_MAX_DIMS 4096
+
+/* Flags of kmc_pass. */
+#define KMC_PASS_ACCUMULATE 1u   /* add into `totals` instead of overwriting them (data held in slices) */
+#define KMC_PASS_GENERIC 2u      /* force the any-shape kernel (tests compare the specialised kernels to it) */
+
+/* Device statistics of one Lloyd step, as kmc_finish leaves them (layout fixed, 64 bytes). */
+typedef struct kmc_stats {
+    double inertia;        /* sum of best over all rows, for the centers the pass started from */
+    int64_t n_empty;       /* clusters that received no row */
+    int64_t n_relocated;   /* clusters given a far row by the relocation rule */
+    int64_t needs_reloc;   /* 1: clusters emptied and no candidate rows were given; C_new not written */
+    int64_t flags;         /* 1 = non-finite data, centers or distance */
+    int64_t rescored;      /* rows whose label was decided in float64 (diagnostic) */
+    int64_t reserved[2];
+} kmc_stats;
+
+/* ---------------------------------------------------------------- library */
+
+int kmc_version(void);
+const char *kmc_last_error(void);
+/* Number of streaming multiprocessors of the current device (grid sizing of the caller's own work). */
+int kmc_num_sms(void);
+
+/* ---------------------------------------------------------------- workspace */
+
+/* Bytes of device workspace kmc_pass, kmc_finish and kmc_totals_unpack need for d dims and k centers.
+ * kmc_finish and kmc_totals_unpack read the constants kmc_pass left there, so a Lloyd step uses one
+ * workspace throughout. */
+size_t kmc_workspace_bytes(int d, int k);
+/* Bytes of device workspace kmc_far_rows needs for `cand_rows` candidates (a separate buffer). */
+size_t kmc_far_workspace_bytes(int64_t cand_rows);
+
+/* ---------------------------------------------------------------- Lloyd step
+ * Replaces core.py:2209-2242 `lloyd_step(parts, C)` and core.py:2200-2206 `assign_mlx(parts, C)`:
+ *   kmc_colmax      once per dataset (the fixed-point grid of the totals),
+ *   kmc_pass        per slice: nearest center + accumulation into totals,
+ *   [ranks > 1: the caller sums totals over ranks, int64 sum -- exact, order-free]
+ *   kmc_finish      center divide, empty-cluster relocation, still-empty rule, statistics.
+ */
+
+/* Per-column max |x| of X (n x d, device) into colmax (d uint32 float bits, device).  Accumulates
+ * (atomic max) into colmax; zero it first with KMC_PASS_ACCUMULATE clear (flags & 1 == 0). */
+int kmc_colmax(const float *X, int64_t n, int d, uint32_t *colmax, unsigned flags, void *stream);
+
+/* One assignment pass over X (n x d, device) against C (k x d, device).
+ * totals (device, k x (d+2) int64): per cluster [count, sum of best, sum of x_j ...] in fixed point.
+ * labels (device, n int32) and best (device, n float32) are optional (NULL to skip).
+ * colmax: the GLOBAL per-column maxima (all slices, all ranks); n_total: the GLOBAL row count.
+ * Replaces core.py:2018-2197 `_gpu_pass`. */
+int kmc_pass(const float *X, int64_t n, int d, const float *C, int k, const uint32_t *colmax, int64_t n_total,
+             int64_t *totals, int32_t *labels, float *best, unsigned flags, void *workspace, size_t ws_bytes,
+             void *stream);
+
+/* Local relocation candidates: the `cand_rows` rows of X with the largest best (lower row index on
+ * ties), as records of (d + 4) 32-bit words [best, global row lo, global row hi, label, x_0 .. x_{d-1}],
+ * farthest first, padded with best = -1.  row0 = global index of local row 0.
+ * Replaces the far-row selection of core.py:2225-2230. */
+int kmc_far_rows(const float *X, int64_t n, int d, const int32_t *labels, const float *best, int64_t row0,
+                 int64_t cand_rows, uint32_t *cands, void *workspace, size_t ws_bytes, void *stream);
+
+/* Finish a Lloyd step from the (global) totals, on the workspace of the kmc_pass that made them (its
+ * fixed-point grid lives there): relocation of empty clusters to the farthest rows (candidate lists of
+ * `ranks` ranks, each from kmc_far_rows, concatenated; NULL when none were gathered), then
+ * C_new = sums / counts rounded to float32, a still-empty cluster takes the largest cluster's center,
+ * and kmc_stats.  totals are updated in place by the relocation.  C_new (device, k x d).
+ * Replaces core.py:2223-2241. */
+int kmc_finish(int64_t *totals, int k, int d, const uint32_t *cands, int64_t cand_rows, int ranks, float *C_new,
+               kmc_stats *stats, void *workspace, size_t ws_bytes, void *stream);
+
+/* Copy the device statistics to the host and wait for them (the one synchronising call). */
+int kmc_stats_read(const kmc_stats *stats_dev, kmc_stats *stats_host, void *stream);
+
+/* Convert totals to float64 sums (k x d), int64 counts (k) and the inertia (all device), as
+ * core.py:2200-2206 `assign_mlx` returns them; same workspace as the kmc_pass that made the totals. */
+int kmc_totals_unpack(const int64_t *totals, int k, int d, double *sums, int64_t *counts, double *inertia,
+                      void *workspace, size_t ws_bytes, void *stream);
+
+/* ---------------------------------------------------------------- k-means++
+ * Replaces core.py:153-192 `kmeans_pp_init(parts, rows, k, rng, sample)` after the host has drawn the
+ * sample rows and gathered them into S (m x d, device): greedy k-means++ with 2 + floor(ln k) candidates
+ * per round by the Gumbel-max trick (Philox4x32-10 with key seeds[r]), the candidate lowering the total
+ * d2 the most kept.  first = sample row of the first center; seeds (device, k-1 uint64);
+ * picks (device, k int64) = chosen sample rows; C_out (device, k x d). */
+size_t kmc_pp_workspace_bytes(int64_t m, int d, int k);
+int kmc_pp_init(const float *S, int64_t m, int d, int k, int64_t first, const uint64_t *seeds, int64_t *picks,
+                float *C_out, void *workspace, size_t ws_bytes, void *stream);
+
+/* ---------------------------------------------------------------- data generation
+ * Synthetic inputs of the benchmark configurations, generated on the device from the global row index
+ * (Philox4x32-10, key = seed), so any split of rows over GPUs yields the same rows.  Replaces
+ * core.py:111-129 `make_data_mlx` (which draws from a splitmix64 hash instead).
+ *   kind 0: uniform [0, 1)                           (params unused)
+ *   kind 1: Gaussian mixture: component uniform over `ncomp`, x = means[c] + sds[c] * N(0,1),
+ *           means/sds (device, ncomp x d); clipped to [lo, hi] when lo < hi
+ *   kind 2: kind 1 then each row scaled to unit L2 norm (float64 norm)
+ */
+int kmc_gen(int kind, float *X, int64_t n, int d, int64_t row0, uint64_t seed, const float *means,
+            const float *sds, int ncomp, float lo, float hi, void *stream);
+
+/* Column sums of X and of X^2 in exact fixed point (grid from colmax, n_total), accumulated into
+ * sums (device, 2 x d int64); and the in-place standardisation X = (X - mean) / std with mean/std
+ * (device, 2 x d float64) derived from those sums.  Used by the 96M-row configuration (standardised
+ * per column in float64, README.md:90 of the reference). */
+int kmc_colsums(const float *X, int64_t n, int d, const uint32_t *colmax, int64_t n_total, int64_t *sums,
+                void *stream);
+int kmc_standardize(float *X, int64_t n, int d, const int64_t *sums, const uint32_t *colmax, int64_t n_total,
+                    double *mean_std, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KMC_H */

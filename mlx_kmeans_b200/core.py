@@ -1,0 +1,404 @@
+"""Host side of the Lloyd hot path: the functions of the reference's mlx_kmeans/core.py that sit on the
+path, with the same names, arguments, return values and errors, running on libkmc.so.
+
+    lloyd_step(parts, C)            core.py:2209-2242
+    assign_mlx(parts, C, ...)       core.py:2200-2206
+    kmeans_pp_init(parts, rows, k, rng, sample=None)   core.py:153-192
+    kmeans(parts, rows, k, ...)     core.py:2247-2273
+    take_rows, slice_rows, make_data_numpy               core.py:19-40, 132-143
+
+`parts` are float32 (rows, dims) CUDA tensors (torch is the device-memory plumbing), NumPy arrays (copied to
+the device once per call), or a Dataset, which keeps the per-dataset state (column maxima, workspaces) between
+passes the way the reference keeps its per-array caches (core.py:548-578). Multi-GPU: a Dataset built with a
+torch.distributed process group holds this rank's contiguous row shard; the per-cluster totals are summed over
+ranks with one all-reduce per pass (int64, exact).
+"""
+import weakref
+
+import numpy as np
+import torch
+
+from . import _lib
+
+SLICE_ROWS = 100_000_000            # kept for API parity: the kernels use 64-bit offsets, so slices are optional
+PART_MAX_ELEMENTS = 2**62           # no 32-bit addressing limit here (core.py:19-20 has 2**32 - 1)
+
+EXACT_METHODS = ("auto", "rows", "pairs", "tiles", "tiles1", "cascade", "onehot", "fused", "generic")
+ACCUMULATE_METHODS = ("auto", "blocks", "sorted", "lanes", "atomic")
+
+
+def slice_rows(dims):
+    """Rows per slice (core.py:23-25). Kept for callers that slice; the library needs no slicing."""
+    return SLICE_ROWS
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+# ---------------------------------------------------------------- data
+
+def make_data_numpy(rows, dims, k, seed):
+    """Points scattered around k hidden centers (the reference's make_data_numpy, core.py:30-40, same draws)."""
+    rng = np.random.default_rng(seed)
+    true_centers = rng.uniform(-10, 10, size=(k, dims)).astype(np.float32)
+    X = np.empty((rows, dims), dtype=np.float32)
+    chunk = 10_000_000
+    for s in range(0, rows, chunk):
+        e = min(s + chunk, rows)
+        labels = rng.integers(0, k, size=e - s)
+        X[s:e] = true_centers[labels] + rng.standard_normal((e - s, dims), dtype=np.float32)
+    return [X]
+
+
+def _as_part(p, device):
+    """One slice as a contiguous float32 CUDA tensor, with the reference's shape errors (core.py:2022-2027)."""
+    if isinstance(p, torch.Tensor):
+        if p.ndim != 2:
+            raise ValueError(f"each part must be 2-D (rows, dims), got {p.ndim}-D")
+        t = p
+        if t.device.type != "cuda":
+            t = t.to(device)
+        if t.dtype != torch.float32:
+            t = t.float()
+        return t.contiguous()
+    a = np.asarray(p.to_numpy() if hasattr(p, "to_numpy") else p)
+    if a.ndim != 2:
+        raise ValueError(f"each part must be 2-D (rows, dims), got {a.ndim}-D")
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(device)
+
+
+class Dataset:
+    """Device-resident rows plus the state one Lloyd pass after another reuses.
+
+    parts: list of (n_i, d) float32 CUDA tensors held by reference (never modified).
+    group: torch.distributed process group when the rows are sharded over ranks (this rank's parts are a
+    contiguous block of rows starting at global row `row0`); None on one GPU.
+    """
+
+    def __init__(self, parts, group=None, device=None):
+        if isinstance(parts, (torch.Tensor, np.ndarray)) or not isinstance(parts, (list, tuple)):
+            parts = [parts]
+        if not parts:
+            raise ValueError("expected a nonempty 2-D (rows, dims) array")
+        self.device = torch.device(device) if device is not None else (
+            parts[0].device if isinstance(parts[0], torch.Tensor) and parts[0].is_cuda
+            else torch.device("cuda", torch.cuda.current_device()))
+        self.parts = [_as_part(p, self.device) for p in parts]
+        d = self.parts[0].shape[1]
+        for p in self.parts:
+            if p.shape[1] != d:
+                raise ValueError(f"data has {p.shape[1]} columns but the first slice has {d}")
+        if d > _lib.KMC_MAX_DIMS:
+            raise ValueError(f"{d} dims is above the supported maximum {_lib.KMC_MAX_DIMS}")
+        self.d = d
+        self.group = group
+        self.n_local = sum(p.shape[0] for p in self.parts)
+        if group is not None:
+            import torch.distributed as dist
+            self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+            counts = torch.tensor([self.n_local], dtype=torch.int64, device=self.device)
+            allc = [torch.zeros_like(counts) for _ in range(self.world)]
+            dist.all_gather(allc, counts, group=group)
+            allc = [int(c.item()) for c in allc]
+            self.row0 = sum(allc[:self.rank])
+            self.n_total = sum(allc)
+        else:
+            self.rank, self.world, self.row0, self.n_total = 0, 1, 0, self.n_local
+        self._ws = {}
+        self._colmax = None
+
+    # -- per-dataset state
+    @property
+    def colmax(self):
+        """Global per-column max |x| (float32 bits as int32): the fixed-point grid of the totals."""
+        if self._colmax is None:
+            cm = torch.zeros(self.d, dtype=torch.int32, device=self.device)
+            flags = 0
+            for p in self.parts:
+                _lib.call("kmc_colmax", _ptr(p), p.shape[0], self.d, _ptr(cm), flags, _stream())
+                flags = _lib.KMC_PASS_ACCUMULATE
+            if self.group is not None:
+                import torch.distributed as dist
+                dist.all_reduce(cm, op=dist.ReduceOp.MAX, group=self.group)
+            self._colmax = cm
+        return self._colmax
+
+    def absmax(self):
+        """max |x| over all rows and columns (host float; NaN / inf if the data holds them)."""
+        bits = self.colmax.cpu().numpy().astype(np.uint32)
+        vals = bits.view(np.float32)
+        if (bits > 0x7F800000).any():
+            return float("nan")
+        return float(vals.max())
+
+    def buffers(self, k):
+        """Workspace, totals, stats and C_new buffers for k centers (reused across passes)."""
+        b = self._ws.get(k)
+        if b is None:
+            L = _lib.load()
+            wsb = int(L.kmc_workspace_bytes(self.d, k))
+            b = dict(
+                ws=torch.empty(wsb, dtype=torch.uint8, device=self.device), wsb=wsb,
+                totals=torch.zeros((k, self.d + 2), dtype=torch.int64, device=self.device),
+                stats=torch.zeros(_lib.STATS_BYTES, dtype=torch.uint8, device=self.device),
+                C_new=torch.empty((k, self.d), dtype=torch.float32, device=self.device),
+                labels=None, best=None)
+            self._ws[k] = b
+        return b
+
+    def _label_buffers(self, b):
+        if b["labels"] is None:
+            b["labels"] = [torch.empty(p.shape[0], dtype=torch.int32, device=self.device) for p in self.parts]
+            b["best"] = [torch.empty(p.shape[0], dtype=torch.float32, device=self.device) for p in self.parts]
+        return b["labels"], b["best"]
+
+    # -- one pass
+    def run_pass(self, C, labels=False, generic=False):
+        """kmc_pass over every local slice, then the all-reduce of the totals. C: (k, d) float32 CUDA."""
+        k = C.shape[0]
+        b = self.buffers(k)
+        lab, bst = self._label_buffers(b) if labels else (None, None)
+        cm = self.colmax
+        flags = _lib.KMC_PASS_GENERIC if generic else 0
+        st = _stream()
+        for i, p in enumerate(self.parts):
+            _lib.call("kmc_pass", _ptr(p), p.shape[0], self.d, _ptr(C), k, _ptr(cm), self.n_total,
+                      _ptr(b["totals"]), _ptr(lab[i]) if labels else None, _ptr(bst[i]) if labels else None,
+                      flags, _ptr(b["ws"]), b["wsb"], st)
+            flags |= _lib.KMC_PASS_ACCUMULATE
+        if self.group is not None:
+            import torch.distributed as dist
+            dist.all_reduce(b["totals"], op=dist.ReduceOp.SUM, group=self.group)
+        return b
+
+    def read_stats(self, b):
+        host = np.zeros(8, dtype=np.int64)
+        _lib.call("kmc_stats_read", _ptr(b["stats"]), host.ctypes.data, _stream())
+        return dict(inertia=float(host[:1].view(np.float64)[0]), n_empty=int(host[1]), n_relocated=int(host[2]),
+                    needs_reloc=int(host[3]), flags=int(host[4]), rescored=int(host[5]))
+
+    def step(self, C, generic=False):
+        """One Lloyd iteration on the device: C (k, d) CUDA -> (C_new CUDA tensor (a buffer reused by the
+        next step with the same k; copy it to keep it), stats dict)."""
+        k = C.shape[0]
+        b = self.run_pass(C, generic=generic)
+        _lib.call("kmc_finish", _ptr(b["totals"]), k, self.d, None, 0, 1, _ptr(b["C_new"]), _ptr(b["stats"]),
+                  _ptr(b["ws"]), b["wsb"], _stream())
+        s = self.read_stats(b)
+        if s["needs_reloc"]:
+            s = self._relocate(C, b, s["n_empty"], generic)
+        return b["C_new"], s
+
+    def _relocate(self, C, b, n_empty, generic):
+        """Empty clusters: recompute the pass with labels and best, gather the farthest rows of every slice
+        and rank, and finish again with them (core.py:2224-2236)."""
+        k = C.shape[0]
+        b = self.run_pass(C, labels=True, generic=generic)
+        E = int(n_empty)
+        R = self.d + 4
+        fwb = int(_lib.load().kmc_far_workspace_bytes(E))
+        fws = torch.empty(fwb, dtype=torch.uint8, device=self.device)
+        lists = []
+        for i, p in enumerate(self.parts):
+            cand = torch.empty((E, R), dtype=torch.int32, device=self.device)
+            row0 = self.row0 + sum(q.shape[0] for q in self.parts[:i])
+            _lib.call("kmc_far_rows", _ptr(p), p.shape[0], self.d, _ptr(b["labels"][i]), _ptr(b["best"][i]),
+                      row0, E, _ptr(cand), _ptr(fws), fwb, _stream())
+            lists.append(cand)
+        local = torch.cat(lists, 0) if len(lists) > 1 else lists[0]
+        nlists = len(lists)
+        if self.group is not None:
+            import torch.distributed as dist
+            if len(self.parts) != 1:
+                raise ValueError("a sharded Dataset holds one slice per rank")
+            gathered = [torch.empty_like(local) for _ in range(self.world)]
+            dist.all_gather(gathered, local, group=self.group)
+            local = torch.cat(gathered, 0)
+            nlists = self.world
+        _lib.call("kmc_finish", _ptr(b["totals"]), k, self.d, _ptr(local), E, nlists, _ptr(b["C_new"]),
+                  _ptr(b["stats"]), _ptr(b["ws"]), b["wsb"], _stream())
+        return self.read_stats(b)
+
+    def assign(self, C, return_labels=False, generic=False):
+        """One pass -> (sums float64 (k, d), counts int64 (k), inertia float[, labels int64 (n_local)])."""
+        k = C.shape[0]
+        b = self.run_pass(C, labels=return_labels, generic=generic)
+        sums = torch.empty((k, self.d), dtype=torch.float64, device=self.device)
+        counts = torch.empty(k, dtype=torch.int64, device=self.device)
+        inertia = torch.empty(1, dtype=torch.float64, device=self.device)
+        _lib.call("kmc_totals_unpack", _ptr(b["totals"]), k, self.d, _ptr(sums), _ptr(counts), _ptr(inertia),
+                  _ptr(b["ws"]), b["wsb"], _stream())
+        out = (sums.cpu().numpy(), counts.cpu().numpy(), float(inertia.item()))
+        if return_labels:
+            out += (torch.cat(b["labels"]).to(torch.int64).cpu().numpy(),)
+        return out
+
+
+# identity cache, like core.py:548-578: a second array never sees the first one's state
+_datasets = {}
+
+
+def _dataset(parts):
+    if isinstance(parts, Dataset):
+        return parts
+    if isinstance(parts, (torch.Tensor, np.ndarray)) or not isinstance(parts, (list, tuple)):
+        parts = [parts]
+    if all(isinstance(p, torch.Tensor) and p.is_cuda and p.dtype == torch.float32 and p.is_contiguous()
+           and p.ndim == 2 for p in parts):
+        key = tuple((id(p), p.data_ptr(), tuple(p.shape), p._version) for p in parts)
+        hit = _datasets.get(key)
+        if hit is not None:
+            ds, refs = hit
+            if all(r() is p for r, p in zip(refs, parts)):
+                return ds
+        ds = Dataset(list(parts))
+        refs = [weakref.ref(p) for p in parts]
+
+        def gone(_r, key=key):
+            _datasets.pop(key, None)
+        for p in parts:
+            weakref.finalize(p, gone, None)
+        _datasets[key] = (ds, refs)
+        return ds
+    return Dataset(list(parts))
+
+
+def _check_method(method, accumulate, k, d):
+    if method not in EXACT_METHODS + ("approx",):
+        raise ValueError(f"unknown method {method!r}")
+    if accumulate not in ACCUMULATE_METHODS:
+        raise ValueError(f"unknown accumulate {accumulate!r}")
+    if method == "tiles" and (k % 8 or d % 8):
+        raise ValueError(f"method='tiles' needs k and dims to be multiples of 8 (got k={k}, dims={d}); 'auto' picks it "
+                         f"only where it applies")
+
+
+def _centers(C, ds):
+    C = np.ascontiguousarray(C, dtype=np.float32) if not isinstance(C, torch.Tensor) else C
+    if C.ndim != 2:
+        raise ValueError(f"centers must be 2-D (k, dims), got {C.ndim}-D")
+    if C.shape[1] != ds.d:
+        raise ValueError(f"data has {ds.d} columns but the centers have {C.shape[1]}; fit and predict need the "
+                         f"same features")
+    if isinstance(C, torch.Tensor):
+        return C.to(ds.device, torch.float32).contiguous()
+    return torch.from_numpy(C).to(ds.device)
+
+
+# ---------------------------------------------------------------- the reference's entry points
+
+def lloyd_step(parts, C, method="auto", accumulate="auto"):
+    """One exact Lloyd iteration on the GPU -> (new centers float32, inertia, number of empty clusters).
+
+    core.py:2209-2242: the inertia belongs to the centers the step started from; empty clusters take the
+    farthest rows (farthest first, lower row index on ties), a cluster still empty takes the largest
+    cluster's center. Everything but the statistics stays on the device."""
+    ds = _dataset(parts)
+    Cd = _centers(C, ds)
+    _check_method(method, accumulate, Cd.shape[0], ds.d)
+    C_new, s = ds.step(Cd, generic=(method == "generic"))
+    inertia = float("nan") if s["flags"] & 1 else s["inertia"]
+    return C_new.cpu().numpy(), inertia, s["n_empty"]
+
+
+def assign_mlx(parts, C, method="auto", return_labels=False, accumulate="auto"):
+    """One pass -> (per-cluster sums float64, counts int64, inertia[, labels int64]) (core.py:2200-2206)."""
+    ds = _dataset(parts)
+    Cd = _centers(C, ds)
+    _check_method(method, accumulate, Cd.shape[0], ds.d)
+    out = ds.assign(Cd, return_labels=return_labels, generic=(method == "generic"))
+    return out
+
+
+assign = assign_mlx
+
+
+def take_rows(parts, idx):
+    """Gather global row indices from a list of slices -> float32 numpy array (core.py:132-143)."""
+    ds = _dataset(parts)
+    idx = np.asarray(idx, dtype=np.int64)
+    out = np.empty((len(idx), ds.d), dtype=np.float32)
+    off = 0
+    for p in ds.parts:
+        m = (idx >= off) & (idx < off + p.shape[0])
+        if m.any():
+            local = torch.from_numpy(idx[m] - off).to(p.device)
+            out[m] = p.index_select(0, local).cpu().numpy()
+        off += p.shape[0]
+    return out
+
+
+def kmeans_pp_init(parts, rows, k, rng, sample=None):
+    """k-means++ seeding on a random subsample (core.py:153-192).
+
+    The sample rows and the first center come from `rng` exactly as the reference draws them
+    (core.py:170-181); the k-1 greedy rounds then run on the device (kmc_pp_init) with no host round trip."""
+    ds = _dataset(parts)
+    if sample is None:
+        sample = min(200_000, max(20_000, 20 * k))
+    idx = np.sort(rng.choice(rows, size=min(sample, rows), replace=False))
+    S = _gather_rows(ds, idx)
+    m, d = S.shape
+    first = int(rng.integers(m))
+    seeds = rng.integers(2**63 - 1, size=max(k - 1, 0)).astype(np.uint64)
+    return pp_init_device(S, k, first, seeds).cpu().numpy()
+
+
+def _gather_rows(ds, idx):
+    """Rows idx (sorted global indices, all on this rank) gathered on the device -> (m, d) tensor."""
+    outs = []
+    off = 0
+    for p in ds.parts:
+        lo, hi = np.searchsorted(idx, [off, off + p.shape[0]])
+        if hi > lo:
+            outs.append(p.index_select(0, torch.from_numpy(idx[lo:hi] - off).to(p.device)))
+        off += p.shape[0]
+    return torch.cat(outs, 0).contiguous()
+
+
+def pp_init_device(S, k, first, seeds):
+    """kmc_pp_init on a device sample S (m, d) -> (k, d) CUDA tensor."""
+    m, d = S.shape
+    if k > m:
+        raise ValueError(f"k={k} exceeds the {m} sample rows")
+    L = _lib.load()
+    wsb = int(L.kmc_pp_workspace_bytes(m, d, k))
+    ws = torch.empty(max(wsb, 256), dtype=torch.uint8, device=S.device)
+    seeds_d = torch.from_numpy(np.asarray(seeds, dtype=np.uint64).view(np.int64)).to(S.device)
+    picks = torch.empty(k, dtype=torch.int64, device=S.device)
+    C = torch.empty((k, d), dtype=torch.float32, device=S.device)
+    _lib.call("kmc_pp_init", _ptr(S), m, d, k, int(first), _ptr(seeds_d) if k > 1 else None, _ptr(picks), _ptr(C),
+              _ptr(ws), wsb, _stream())
+    pp_init_device.last_picks = picks
+    return C
+
+
+def kmeans(parts, rows, k, max_iter, tol, seed, verbose=True):
+    """The reference's synthetic driver (core.py:2247-2273, MLX backend branch) on the device."""
+    import time
+    ds = _dataset(parts)
+    rng = np.random.default_rng(seed)
+    C = kmeans_pp_init(ds, rows, k, rng)
+    prev = None
+    Cd = torch.from_numpy(C).to(ds.device)
+    for it in range(1, max_iter + 1):
+        t = time.perf_counter()
+        newC, s = ds.step(Cd)
+        newC = newC.clone()
+        shift = float(torch.sqrt(((newC - Cd) ** 2).sum(1)).max())
+        Cd = newC
+        inertia = s["inertia"]
+        if verbose:
+            note = f"  ({s['n_empty']} empty clusters relocated)" if s["n_empty"] else ""
+            print(f"iter {it:3d}  inertia {inertia:.6e}  max_center_shift {shift:.5f}  "
+                  f"{time.perf_counter() - t:.3f}s{note}")
+        if prev is not None and abs(prev - inertia) <= tol * prev:
+            break
+        prev = inertia
+    inertia = ds.assign(Cd)[2]
+    return Cd.cpu().numpy(), inertia

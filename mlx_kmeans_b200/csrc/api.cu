@@ -1,0 +1,246 @@
+// api.cu -- the C ABI of libkmc.so (declared in include/kmc.h).  Argument checks, workspace carve-up,
+// dispatch to the kernels, and the error reporting: every entry point returns a status and records a
+// message for kmc_last_error(); nothing is thrown across the ABI.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/kmc.h"
+#include "kmc_internal.h"
+
+namespace kmc {
+
+namespace {
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+    return fail(KMC_ERR_CUDA, "%s: %s", where, cudaGetErrorString(e));
+}
+
+size_t a256(size_t v) { return (v + 255) & ~size_t(255); }
+
+int check_shape(int64_t n, int d, int k) {
+    if (n < 0) return fail(KMC_ERR_INVALID, "n must be >= 0, got %lld", (long long)n);
+    if (d < 1) return fail(KMC_ERR_INVALID, "dims must be >= 1, got %d", d);
+    if (d > KMC_MAX_DIMS) return fail(KMC_ERR_UNSUPPORTED, "dims %d above the supported maximum %d", d, KMC_MAX_DIMS);
+    if (k < 1) return fail(KMC_ERR_INVALID, "k must be >= 1, got %d", k);
+    return KMC_OK;
+}
+}  // namespace
+
+int num_sms() {
+    static thread_local int dev = -1, sms = 0;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    if (cur != dev || sms == 0) {
+        dev = cur;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cur) != cudaSuccess || sms <= 0) sms = 148;
+    }
+    return sms;
+}
+
+Workspace carve(void* base, int d, int k) {
+    Workspace w;
+    char* p = static_cast<char*>(base);
+    size_t off = 0;
+    auto take = [&](size_t bytes) { char* q = p ? p + off : nullptr; off += a256(bytes); return q; };
+    w.prep = reinterpret_cast<Prep*>(take(sizeof(Prep)));
+    w.counters = reinterpret_cast<long long*>(take(sizeof(long long) * 8));
+    w.scale_x = reinterpret_cast<double*>(take(sizeof(double) * d));
+    w.hc = reinterpret_cast<float*>(take(sizeof(float) * k));
+    w.reloc = reinterpret_cast<int*>(take(sizeof(int) * k));
+    w.empty = reinterpret_cast<long long*>(take(sizeof(long long) * k));
+    w.bytes = off;
+    return w;
+}
+
+FarWorkspace carve_far(void* base, int64_t cand_rows) {
+    FarWorkspace w;
+    char* p = static_cast<char*>(base);
+    size_t off = 0;
+    auto take = [&](size_t bytes) { char* q = p ? p + off : nullptr; off += a256(bytes); return q; };
+    w.rs = reinterpret_cast<unsigned long long*>(take(sizeof(unsigned long long) * 8));
+    w.hist = reinterpret_cast<unsigned int*>(take(sizeof(unsigned int) * 256));
+    w.keys = reinterpret_cast<unsigned long long*>(take(sizeof(unsigned long long) * (cand_rows > 0 ? cand_rows : 1)));
+    w.bytes = off;
+    return w;
+}
+
+}  // namespace kmc
+
+using namespace kmc;
+
+extern "C" {
+
+int kmc_version(void) { return 1; }
+
+const char* kmc_last_error(void) { return g_err.c_str(); }
+
+int kmc_num_sms(void) { return num_sms(); }
+
+size_t kmc_workspace_bytes(int d, int k) { return carve(nullptr, d, k).bytes; }
+
+size_t kmc_far_workspace_bytes(int64_t cand_rows) { return carve_far(nullptr, cand_rows).bytes; }
+
+int kmc_colmax(const float* X, int64_t n, int d, uint32_t* colmax, unsigned flags, void* stream) {
+    if (int s = check_shape(n, d, 1)) return s;
+    if (!colmax || (n > 0 && !X)) return fail(KMC_ERR_INVALID, "kmc_colmax: null pointer");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (!(flags & KMC_PASS_ACCUMULATE)) {
+        cudaError_t e = cudaMemsetAsync(colmax, 0, sizeof(uint32_t) * d, st);
+        if (e != cudaSuccess) return cuda_fail(e, "kmc_colmax");
+    }
+    if (n == 0) return KMC_OK;
+    cudaError_t e = launch_colmax(X, n, d, colmax, st);
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_colmax");
+    return KMC_OK;
+}
+
+int kmc_pass(const float* X, int64_t n, int d, const float* C, int k, const uint32_t* colmax, int64_t n_total,
+             int64_t* totals, int32_t* labels, float* best, unsigned flags, void* workspace, size_t ws_bytes,
+             void* stream) {
+    if (int s = check_shape(n, d, k)) return s;
+    if (!C || !colmax || !totals || !workspace || (n > 0 && !X))
+        return fail(KMC_ERR_INVALID, "kmc_pass: null pointer");
+    if (n_total < n) return fail(KMC_ERR_INVALID, "kmc_pass: n_total %lld < n %lld", (long long)n_total, (long long)n);
+    Workspace ws = carve(workspace, d, k);
+    if (ws_bytes < ws.bytes) return fail(KMC_ERR_INVALID, "kmc_pass: workspace of %zu bytes, need %zu", ws_bytes, ws.bytes);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    if (!(flags & KMC_PASS_ACCUMULATE)) {
+        e = cudaMemsetAsync(totals, 0, sizeof(int64_t) * (size_t)k * (d + 2), st);
+        if (e != cudaSuccess) return cuda_fail(e, "kmc_pass: clear totals");
+        e = cudaMemsetAsync(ws.counters, 0, sizeof(long long) * 8, st);
+        if (e != cudaSuccess) return cuda_fail(e, "kmc_pass: clear counters");
+    }
+    e = launch_prepare(C, k, d, colmax, n_total, ws.prep, ws.scale_x, ws.hc, st);
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_pass: prepare");
+    if (n == 0) return KMC_OK;
+    PassArgs a;
+    a.X = X;
+    a.n = n;
+    a.d = d;
+    a.k = k;
+    a.C = C;
+    a.hc = ws.hc;
+    a.scale_x = ws.scale_x;
+    a.prep = ws.prep;
+    a.totals = reinterpret_cast<long long*>(totals);
+    a.labels = labels;
+    a.best = best;
+    a.counters = ws.counters;
+    a.smem_acc = 0;
+    a.ctile = 0;
+    e = cudaErrorNotSupported;
+    if (!(flags & KMC_PASS_GENERIC)) e = launch_pass_lowd(a, st);
+    if (e == cudaErrorNotSupported) e = launch_pass_generic(a, st);
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_pass");
+    return KMC_OK;
+}
+
+int kmc_far_rows(const float* X, int64_t n, int d, const int32_t* labels, const float* best, int64_t row0,
+                 int64_t cand_rows, uint32_t* cands, void* workspace, size_t ws_bytes, void* stream) {
+    if (int s = check_shape(n, d, 1)) return s;
+    if (cand_rows < 1) return fail(KMC_ERR_INVALID, "kmc_far_rows: cand_rows must be >= 1");
+    if (!cands || !workspace || (n > 0 && (!X || !labels || !best)))
+        return fail(KMC_ERR_INVALID, "kmc_far_rows: null pointer");
+    if (n > 0xffffffffll) return fail(KMC_ERR_UNSUPPORTED, "kmc_far_rows: more than 2^32 rows on one GPU");
+    FarWorkspace ws = carve_far(workspace, cand_rows);
+    if (ws_bytes < ws.bytes) return fail(KMC_ERR_INVALID, "kmc_far_rows: workspace of %zu bytes, need %zu", ws_bytes, ws.bytes);
+    cudaError_t e = launch_far_rows(X, n, d, labels, best, row0, cand_rows, cands, ws, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_far_rows");
+    return KMC_OK;
+}
+
+int kmc_finish(int64_t* totals, int k, int d, const uint32_t* cands, int64_t cand_rows, int ranks, float* C_new,
+               kmc_stats* stats, void* workspace, size_t ws_bytes, void* stream) {
+    if (int s = check_shape(0, d, k)) return s;
+    if (!totals || !C_new || !stats || !workspace) return fail(KMC_ERR_INVALID, "kmc_finish: null pointer");
+    if (cands && (cand_rows < 1 || ranks < 1 || ranks > 64))
+        return fail(KMC_ERR_INVALID, "kmc_finish: cand_rows %lld / ranks %d", (long long)cand_rows, ranks);
+    Workspace ws = carve(workspace, d, k);
+    if (ws_bytes < ws.bytes) return fail(KMC_ERR_INVALID, "kmc_finish: workspace of %zu bytes, need %zu", ws_bytes, ws.bytes);
+    cudaError_t e = launch_finish(reinterpret_cast<long long*>(totals), k, d, cands, cand_rows, ranks, C_new, stats, ws,
+                                  static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_finish");
+    return KMC_OK;
+}
+
+int kmc_stats_read(const kmc_stats* stats_dev, kmc_stats* stats_host, void* stream) {
+    if (!stats_dev || !stats_host) return fail(KMC_ERR_INVALID, "kmc_stats_read: null pointer");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(stats_host, stats_dev, sizeof(kmc_stats), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_stats_read");
+    return KMC_OK;
+}
+
+int kmc_totals_unpack(const int64_t* totals, int k, int d, double* sums, int64_t* counts, double* inertia,
+                      void* workspace, size_t ws_bytes, void* stream) {
+    if (int s = check_shape(0, d, k)) return s;
+    if (!totals || !sums || !counts || !inertia || !workspace) return fail(KMC_ERR_INVALID, "kmc_totals_unpack: null pointer");
+    Workspace ws = carve(workspace, d, k);
+    if (ws_bytes < ws.bytes) return fail(KMC_ERR_INVALID, "kmc_totals_unpack: workspace of %zu bytes, need %zu", ws_bytes, ws.bytes);
+    cudaError_t e = launch_unpack(reinterpret_cast<const long long*>(totals), k, d, ws.scale_x, ws.prep, ws.counters, sums, counts,
+                                  inertia, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_totals_unpack");
+    return KMC_OK;
+}
+
+size_t kmc_pp_workspace_bytes(int64_t m, int d, int k) { return pp_workspace_bytes(m, d, k); }
+
+int kmc_pp_init(const float* S, int64_t m, int d, int k, int64_t first, const uint64_t* seeds, int64_t* picks,
+                float* C_out, void* workspace, size_t ws_bytes, void* stream) {
+    if (int s = check_shape(m, d, k)) return s;
+    if (m < 1) return fail(KMC_ERR_INVALID, "kmc_pp_init: empty sample");
+    if (first < 0 || first >= m) return fail(KMC_ERR_INVALID, "kmc_pp_init: first row %lld outside the sample", (long long)first);
+    if (!S || !picks || !C_out || !workspace || (k > 1 && !seeds)) return fail(KMC_ERR_INVALID, "kmc_pp_init: null pointer");
+    if (ws_bytes < pp_workspace_bytes(m, d, k)) return fail(KMC_ERR_INVALID, "kmc_pp_init: workspace too small");
+    cudaError_t e = launch_pp_init(S, m, d, k, first, seeds, picks, C_out, workspace, ws_bytes, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_pp_init");
+    return KMC_OK;
+}
+
+int kmc_gen(int kind, float* X, int64_t n, int d, int64_t row0, uint64_t seed, const float* means, const float* sds,
+            int ncomp, float lo, float hi, void* stream) {
+    if (int s = check_shape(n, d, 1)) return s;
+    if (n > 0 && !X) return fail(KMC_ERR_INVALID, "kmc_gen: null pointer");
+    if (kind < 0 || kind > 2) return fail(KMC_ERR_INVALID, "kmc_gen: unknown kind %d", kind);
+    if (kind > 0 && (!means || !sds || ncomp < 1)) return fail(KMC_ERR_INVALID, "kmc_gen: mixture needs means, sds, ncomp");
+    cudaError_t e = launch_gen(kind, X, n, d, row0, seed, means, sds, ncomp, lo, hi, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_gen");
+    return KMC_OK;
+}
+
+int kmc_colsums(const float* X, int64_t n, int d, const uint32_t* colmax, int64_t n_total, int64_t* sums, void* stream) {
+    if (int s = check_shape(n, d, 1)) return s;
+    if (!colmax || !sums || (n > 0 && !X)) return fail(KMC_ERR_INVALID, "kmc_colsums: null pointer");
+    cudaError_t e = launch_colsums(X, n, d, colmax, n_total, reinterpret_cast<long long*>(sums), static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_colsums");
+    return KMC_OK;
+}
+
+int kmc_standardize(float* X, int64_t n, int d, const int64_t* sums, const uint32_t* colmax, int64_t n_total,
+                    double* mean_std, void* stream) {
+    if (int s = check_shape(n, d, 1)) return s;
+    if (!colmax || !sums || !mean_std || (n > 0 && !X)) return fail(KMC_ERR_INVALID, "kmc_standardize: null pointer");
+    if (n_total < 1) return fail(KMC_ERR_INVALID, "kmc_standardize: n_total must be >= 1");
+    cudaError_t e = launch_standardize(X, n, d, reinterpret_cast<const long long*>(sums), colmax, n_total, mean_std,
+                                       static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_standardize");
+    return KMC_OK;
+}
+
+}  // extern "C"

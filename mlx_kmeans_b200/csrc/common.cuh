@@ -1,0 +1,192 @@
+// common.cuh -- device helpers shared by the kmc kernels (sm_100a).
+//
+// Numeric contract of every pass (mirrors the reference's, kakollu/mlx-kmeans):
+//   label(x)  = argmin_c D64(x, c), lowest index on exact ties, where D64 is the float64 distance of
+//               the reference's test oracle (tests/accuracy.py:31-51): (double)x_j - (double)c_j,
+//               squared, summed in NumPy's pairwise order.  A float32 screen picks the label and only
+//               rows whose two best screen scores lie inside a proven error window are re-scored with
+//               D64, so the screen never decides a label it cannot prove.
+//   best(x)   = float32 distance to the chosen center, s = s + (x_j - c_j)^2 in order with every
+//               operation rounded on its own (core.py:248-257 keeps the same quantity as `best`).
+//   totals    = per cluster [count, sum of best, sum of x_j ...] (core.py:236-237 layout), held as
+//               exact int64 fixed point: every value is rounded once to a per-column power-of-two grid
+//               and the integers are summed, so totals do not depend on summation order, thread
+//               schedule, or how rows are split across blocks and GPUs.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace kmc {
+
+constexpr int kMaxDims = 4096;     // largest d the pass kernels accept
+
+// Per-pass constants, computed on device by k_prepare (no host round trip).
+struct Prep {
+    double inv_scale_i;     // 2^-si
+    double scale_i;         // 2^si: inertia fixed point
+    float cmax2;            // max_c |c|^2 (float32, rounded up)
+    float win_coef;         // screen window = win_coef * (|x|^2 + cmax2) + win_abs
+    float win_abs;
+    int si;
+    int flags;              // kFlag* below
+    int pad;
+};
+
+enum : int {
+    kFlagNonFinite = 1,     // data or centers hold NaN / inf, or a distance overflowed float32
+};
+
+// Device statistics written by the finish kernel; read by the host once per pass.
+struct Stats {
+    double inertia;         // sum of best over all rows (of the centers the pass started from)
+    int64_t n_empty;        // clusters with no rows after the pass (before relocation)
+    int64_t n_relocated;    // clusters given a far row by the relocation rule
+    int64_t needs_reloc;    // 1: empties exist and the finish had no candidate rows -> centers not written
+    int64_t flags;          // kFlag*
+    int64_t rescored;       // rows re-scored in float64 by the pass kernels (diagnostic)
+    int64_t pad[2];
+};
+
+// ---------------------------------------------------------------- fixed point
+
+// smallest e with |v| <= 2^e (v finite, > 0)
+__host__ __device__ inline int ceil_log2(double v) {
+    int e;
+    double m = frexp(v, &e);
+    return m == 0.5 ? e - 1 : e;
+}
+
+// The grid a column is summed on: |v| <= absmax and n rows -> sum of n quantised values < 2^61.
+__host__ __device__ inline int column_shift(float absmax, int64_t n_total) {
+    double m = absmax > 0.0f ? (double)absmax : 1.1754943508222875e-38;   // FLT_MIN
+    int L = ceil_log2((double)(n_total > 0 ? n_total : 1));
+    int s = 61 - L - ceil_log2(m);
+    return s > 1000 ? 1000 : (s < -1000 ? -1000 : s);
+}
+
+__device__ __forceinline__ long long quantize(float v, double scale) {
+    return __double2ll_rn(__dmul_rn((double)v, scale));
+}
+
+// ---------------------------------------------------------------- distances
+
+// float32 distance with every operation rounded separately (no contraction): the `best` value.
+__device__ __forceinline__ float best32_term(float s, float x, float c) {
+    float q = __fsub_rn(x, c);
+    return __fadd_rn(s, __fmul_rn(q, q));
+}
+
+// NumPy's pairwise sum of the float64 terms t_j = ((double)x_j - (double)c_j)^2, j in [lo, lo + n).
+// Fewer than 8 terms: in order; up to 128: eight running partials + tail; longer: split at n/2 rounded
+// down to a multiple of 8 (the same tree NumPy builds for a reduction over a contiguous axis).
+__device__ __forceinline__ double d64_term(const float* x, const float* c, int j) {
+    double q = __dsub_rn((double)x[j], (double)c[j]);
+    return __dmul_rn(q, q);
+}
+
+__device__ inline double d64_leaf(const float* x, const float* c, int lo, int n) {
+    if (n < 8) {
+        double r = 0.0;
+        for (int i = 0; i < n; i++) r = __dadd_rn(r, d64_term(x, c, lo + i));
+        return r;
+    }
+    double r0 = d64_term(x, c, lo + 0), r1 = d64_term(x, c, lo + 1), r2 = d64_term(x, c, lo + 2),
+           r3 = d64_term(x, c, lo + 3), r4 = d64_term(x, c, lo + 4), r5 = d64_term(x, c, lo + 5),
+           r6 = d64_term(x, c, lo + 6), r7 = d64_term(x, c, lo + 7);
+    int i = 8;
+    for (; i < n - (n % 8); i += 8) {
+        r0 = __dadd_rn(r0, d64_term(x, c, lo + i + 0));
+        r1 = __dadd_rn(r1, d64_term(x, c, lo + i + 1));
+        r2 = __dadd_rn(r2, d64_term(x, c, lo + i + 2));
+        r3 = __dadd_rn(r3, d64_term(x, c, lo + i + 3));
+        r4 = __dadd_rn(r4, d64_term(x, c, lo + i + 4));
+        r5 = __dadd_rn(r5, d64_term(x, c, lo + i + 5));
+        r6 = __dadd_rn(r6, d64_term(x, c, lo + i + 6));
+        r7 = __dadd_rn(r7, d64_term(x, c, lo + i + 7));
+    }
+    double res = __dadd_rn(__dadd_rn(__dadd_rn(r0, r1), __dadd_rn(r2, r3)),
+                           __dadd_rn(__dadd_rn(r4, r5), __dadd_rn(r6, r7)));
+    for (; i < n; i++) res = __dadd_rn(res, d64_term(x, c, lo + i));
+    return res;
+}
+
+// Iterative form of the recursive split (no device recursion): a post-order walk with an explicit
+// stack; depth <= log2(kMaxDims / 128) + 2.
+__device__ inline double d64_pairwise(const float* x, const float* c, int d) {
+    if (d <= 128) return __dadd_rn(0.0, d64_leaf(x, c, 0, d));
+    struct Frame { int lo, n, state; double left; };
+    Frame st[16];
+    int sp = 0;
+    st[0] = {0, d, 0, 0.0};
+    double ret = 0.0;
+    while (true) {
+        Frame& f = st[sp];
+        if (f.n <= 128) {
+            ret = d64_leaf(x, c, f.lo, f.n);
+            if (sp == 0) break;
+            sp--;
+            continue;
+        }
+        int n2 = f.n / 2;
+        n2 -= n2 % 8;
+        if (f.state == 0) {            // descend left
+            f.state = 1;
+            st[++sp] = {f.lo, n2, 0, 0.0};
+        } else if (f.state == 1) {     // left done -> descend right
+            f.left = ret;
+            f.state = 2;
+            st[++sp] = {f.lo + n2, f.n - n2, 0, 0.0};
+        } else {                       // right done
+            ret = __dadd_rn(f.left, ret);
+            if (sp == 0) break;
+            sp--;
+        }
+    }
+    return __dadd_rn(0.0, ret);
+}
+
+// ---------------------------------------------------------------- Philox4x32-10
+
+// Salmon, Moraes, Dror, Shaw, SC'11: ten rounds of two 32x32->64 multiplies with a Weyl key schedule.
+__host__ __device__ inline void philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1) {
+#pragma unroll
+    for (int r = 0; r < 10; r++) {
+        uint64_t p0 = (uint64_t)0xD2511F53u * c[0], p1 = (uint64_t)0xCD9E8D57u * c[2];
+        uint32_t n0 = (uint32_t)(p1 >> 32) ^ c[1] ^ k0;
+        uint32_t n1 = (uint32_t)p1;
+        uint32_t n2 = (uint32_t)(p0 >> 32) ^ c[3] ^ k1;
+        uint32_t n3 = (uint32_t)p0;
+        c[0] = n0; c[1] = n1; c[2] = n2; c[3] = n3;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+}
+
+// Natural log in (0, inf) from log(m 2^e) = e ln2 + 2 atanh((m-1)/(m+1)), m in [sqrt(1/2), sqrt(2)),
+// every operation an IEEE double op rounded on its own, so host and device agree bit for bit.
+__host__ __device__ inline double kmc_log(double v) {
+    int e = 0;
+    double m = frexp(v, &e);
+    if (m < 0.70710678118654752440) { m = m * 2.0; e -= 1; }
+#ifdef __CUDA_ARCH__
+    double s = __ddiv_rn(__dsub_rn(m, 1.0), __dadd_rn(m, 1.0));
+    double s2 = __dmul_rn(s, s);
+    double term = s, sum = 0.0;
+    for (int i = 0; i < 40; i++) {
+        sum = __dadd_rn(sum, __ddiv_rn(term, (double)(2 * i + 1)));
+        term = __dmul_rn(term, s2);
+    }
+    return __dadd_rn(__dmul_rn((double)e, 0.69314718055994530942), __dmul_rn(2.0, sum));
+#else
+    double s = (m - 1.0) / (m + 1.0);
+    double s2 = s * s;
+    double term = s, sum = 0.0;
+    for (int i = 0; i < 40; i++) {
+        sum = sum + term / (double)(2 * i + 1);
+        term = term * s2;
+    }
+    return (double)e * 0.69314718055994530942 + 2.0 * sum;
+#endif
+}
+
+}  // namespace kmc

@@ -1,0 +1,77 @@
+// kmc_internal.h -- shared declarations of the kmc CUDA library (not part of the public ABI).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace kmc {
+
+int num_sms();
+
+// Arguments of the pass kernels.
+struct PassArgs {
+    const float* X;
+    int64_t n;
+    int d, k;
+    const float* C;
+    const float* hc;          // k: |c|^2 / 2 (float32)
+    const double* scale_x;    // d: 2^shift per column
+    const Prep* prep;
+    long long* totals;        // k x (d+2)
+    int32_t* labels;          // optional
+    float* best;              // optional
+    long long* counters;      // [0] rows re-scored, [1] flags
+    int smem_acc;             // generic kernel: accumulate in shared memory
+    int ctile;                // generic kernel: centers per shared tile
+};
+
+// Pass workspace carve-up (256-byte aligned pieces): kmc_pass writes prep/scale_x/hc/counters,
+// kmc_finish and kmc_totals_unpack read them.
+struct Workspace {
+    Prep* prep;
+    long long* counters;      // 8: [0] rows re-scored, [1] flags
+    double* scale_x;          // d
+    float* hc;                // k
+    int* reloc;               // k: candidate slot relocated into cluster c, or -1
+    long long* empty;         // k: empty cluster list
+    size_t bytes;
+};
+Workspace carve(void* base, int d, int k);
+
+// Far-rows workspace.
+struct FarWorkspace {
+    unsigned long long* rs;   // radix-select state: [0] prefix [1] mask [2] remaining [3] take-all [4] collected
+    unsigned int* hist;       // 256
+    unsigned long long* keys; // cand_rows collected keys
+    size_t bytes;
+};
+FarWorkspace carve_far(void* base, int64_t cand_rows);
+
+cudaError_t launch_colmax(const float* X, int64_t n, int d, unsigned int* colmax, cudaStream_t st);
+cudaError_t launch_prepare(const float* C, int k, int d, const unsigned int* colmax, int64_t n_total, Prep* prep,
+                           double* scale_x, float* hc, cudaStream_t st);
+cudaError_t launch_pass_generic(PassArgs a, cudaStream_t st);
+// Specialised low-dimensional fused pass; returns cudaErrorNotSupported when (d, k) has no instance.
+cudaError_t launch_pass_lowd(PassArgs a, cudaStream_t st);
+
+cudaError_t launch_far_rows(const float* X, int64_t n, int d, const int32_t* labels, const float* best, int64_t row0,
+                            int64_t cand_rows, uint32_t* cands, const FarWorkspace& ws, cudaStream_t st);
+cudaError_t launch_finish(long long* totals, int k, int d, const uint32_t* cands, int64_t cand_rows, int ranks,
+                          float* C_new, void* stats, const Workspace& ws, cudaStream_t st);
+cudaError_t launch_unpack(const long long* totals, int k, int d, const double* scale_x, const Prep* prep,
+                          const long long* counters, double* sums, int64_t* counts, double* inertia, cudaStream_t st);
+
+cudaError_t launch_pp_init(const float* S, int64_t m, int d, int k, int64_t first, const uint64_t* seeds,
+                           int64_t* picks, float* C_out, void* ws, size_t ws_bytes, cudaStream_t st);
+size_t pp_workspace_bytes(int64_t m, int d, int k);
+
+cudaError_t launch_gen(int kind, float* X, int64_t n, int d, int64_t row0, uint64_t seed, const float* means,
+                       const float* sds, int ncomp, float lo, float hi, cudaStream_t st);
+cudaError_t launch_colsums(const float* X, int64_t n, int d, const unsigned int* colmax, int64_t n_total,
+                           long long* sums, cudaStream_t st);
+cudaError_t launch_standardize(float* X, int64_t n, int d, const long long* sums, const unsigned int* colmax,
+                               int64_t n_total, double* mean_std, cudaStream_t st);
+
+}  // namespace kmc

@@ -1,0 +1,240 @@
+// pass_generic.cu -- column maxima, per-pass constants, and the any-shape assignment pass.
+//
+// Reference: core.py:2018-2197 (_gpu_pass) with the rows kernel of core.py:263-274 as its label
+// semantics, and the accumulation of core.py:236-243 ([count, inertia, sums...] per cluster).
+// This is the path for shapes no specialised kernel covers; it is exact for every (n, d, k) and
+// every input, and the specialised kernels are checked against it as well as against the oracle.
+#include "common.cuh"
+#include "kmc_internal.h"
+
+namespace kmc {
+
+// ---------------------------------------------------------------- column maxima
+// Per-column max |x| as float bits (|x| bits order like the values; NaN bits sort above inf).
+// The grid stride is a multiple of d, so each thread always reads the same column.
+__global__ void k_colmax(const float* __restrict__ X, int64_t total, int d, int64_t stride,
+                         unsigned int* __restrict__ colmax) {
+    extern __shared__ unsigned int smax[];
+    for (int j = threadIdx.x; j < d; j += blockDim.x) smax[j] = 0u;
+    __syncthreads();
+    int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < stride) {
+        unsigned int m = 0u;
+        for (int64_t e = t; e < total; e += stride) {
+            unsigned int b = __float_as_uint(X[e]) & 0x7fffffffu;
+            m = b > m ? b : m;
+        }
+        atomicMax(&smax[(int)(t % d)], m);
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < d; j += blockDim.x)
+        if (smax[j]) atomicMax(&colmax[j], smax[j]);
+}
+
+// ---------------------------------------------------------------- per-pass constants
+// One CTA.  Screen constants per center, the fixed-point grids, and the window of the float32 screen.
+//
+// Screen: score_c = |c|^2/2 - x.c, an fma chain of d steps from h_c = |c|^2/2 (itself d fmas).
+// |score_c(fp32) - score_c| <= 1.5 gamma_{d+1} (|x|^2 + |c|^2), gamma_n = n u / (1 - n u), u = 2^-24,
+// and D(c) - D(c') = 2 (score_c - score_c').  When the best two screen scores are further apart than
+// twice that bound (taken with max |c|^2, a 4/3 margin, and the float64 rounding of D64 added) the
+// float32 winner is the float64 winner; otherwise the row is re-scored in float64.
+__global__ void k_prepare(const float* __restrict__ C, int k, int d, const unsigned int* __restrict__ colmax,
+                          int64_t n_total, Prep* __restrict__ prep, double* __restrict__ scale_x,
+                          float* __restrict__ hc) {
+    __shared__ float s_max[32];
+    __shared__ float s_cmax2[32];
+    __shared__ int s_bad;
+    if (threadIdx.x == 0) s_bad = 0;
+    __syncthreads();
+    float mx = 0.0f, cm2 = 0.0f;
+    int bad = 0;
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+        unsigned int b = colmax[j];
+        if (b >= 0x7f800000u) bad = 1;
+        float v = __uint_as_float(b);
+        mx = fmaxf(mx, v);
+        scale_x[j] = ldexp(1.0, column_shift(v, n_total));
+    }
+    for (int c = threadIdx.x; c < k; c += blockDim.x) {
+        float s = 0.0f;
+        for (int j = 0; j < d; j++) {
+            float v = C[(int64_t)c * d + j];
+            if (!isfinite(v)) bad = 1;
+            mx = fmaxf(mx, fabsf(v));
+            s = __fmaf_rn(v, v, s);
+        }
+        hc[c] = 0.5f * s;
+        cm2 = fmaxf(cm2, s);
+    }
+    for (int o = 16; o; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        cm2 = fmaxf(cm2, __shfl_xor_sync(0xffffffffu, cm2, o));
+    }
+    if (bad) atomicOr(&s_bad, 1);
+    if ((threadIdx.x & 31) == 0) { s_max[threadIdx.x >> 5] = mx; s_cmax2[threadIdx.x >> 5] = cm2; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) { mx = fmaxf(mx, s_max[w]); cm2 = fmaxf(cm2, s_cmax2[w]); }
+        Prep p;
+        double M = mx > 0.0f ? (double)mx : 1.1754943508222875e-38;
+        double bound = 4.0 * (double)d * M * M * (1.0 + 1.0 / 1048576.0);     // >= any best32
+        int L = ceil_log2((double)(n_total > 0 ? n_total : 1));
+        int si = 61 - L - ceil_log2(bound);
+        si = si > 1000 ? 1000 : (si < -1000 ? -1000 : si);
+        p.si = si;
+        p.scale_i = ldexp(1.0, si);
+        p.inv_scale_i = ldexp(1.0, -si);
+        p.cmax2 = cm2 * (1.0f + 1.0f / 1048576.0f);
+        p.win_coef = (float)(4.0 * (d + 2) / 16777216.0 + (double)d / 281474976710656.0);
+        p.win_abs = (float)((d + 2) * 7.174648137343064e-43);               // (d+2) 2^-140
+        p.flags = (s_bad || bound > 3.0e38) ? kFlagNonFinite : 0;
+        p.pad = 0;
+        *prep = p;
+    }
+}
+
+// ---------------------------------------------------------------- the any-shape pass
+// One thread per row.  DMAX > 0: the row is held in registers (d <= DMAX); DMAX == 0: read from L1.
+// Centers stream through shared memory in tiles.  Accumulators: shared int64 slots when k*(d+2) fits,
+// else the global totals directly.
+template <int DMAX>
+__global__ void __launch_bounds__(256) k_pass_generic(PassArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int d = a.d, k = a.k;
+    const int W = d + 2;
+    long long* sacc = reinterpret_cast<long long*>(smem_raw);
+    const int nslots = a.smem_acc ? k * W : 0;
+    float* ctile = reinterpret_cast<float*>(smem_raw + (size_t)nslots * 8);
+    float* htile = ctile + (size_t)a.ctile * d;
+    for (int s = threadIdx.x; s < nslots; s += blockDim.x) sacc[s] = 0;
+    const Prep prep = *a.prep;
+    const double scale_i = prep.scale_i;
+    int rescored = 0, bad = 0;
+
+    const int64_t rows_per_cta = (a.n + gridDim.x - 1) / gridDim.x;
+    const int64_t r_begin = (int64_t)blockIdx.x * rows_per_cta;
+    const int64_t r_end = min(a.n, r_begin + rows_per_cta);
+    for (int64_t base = r_begin; base < r_end; base += blockDim.x) {
+        const int64_t i = base + threadIdx.x;
+        const bool live = i < r_end;
+        const float* xr = a.X + (live ? i : r_begin) * (int64_t)d;
+        float xreg[DMAX > 0 ? DMAX : 1];
+        float x2 = 0.0f;
+        if (DMAX > 0) {
+#pragma unroll
+            for (int j = 0; j < (DMAX > 0 ? DMAX : 1); j++) {
+                xreg[j] = j < d ? xr[j] : 0.0f;
+                x2 = __fmaf_rn(xreg[j], xreg[j], x2);
+            }
+        } else {
+            for (int j = 0; j < d; j++) x2 = __fmaf_rn(xr[j], xr[j], x2);
+        }
+        float s1 = INFINITY, s2 = INFINITY;
+        int l1 = 0;
+        for (int c0 = 0; c0 < k; c0 += a.ctile) {
+            const int ct = min(a.ctile, k - c0);
+            __syncthreads();
+            for (int e = threadIdx.x; e < ct * d; e += blockDim.x) ctile[e] = a.C[(int64_t)c0 * d + e];
+            for (int e = threadIdx.x; e < ct; e += blockDim.x) htile[e] = a.hc[c0 + e];
+            __syncthreads();
+            for (int cc = 0; cc < ct; cc++) {
+                const float* cr = ctile + (size_t)cc * d;
+                float s = htile[cc];
+                if (DMAX > 0) {
+#pragma unroll
+                    for (int j = 0; j < (DMAX > 0 ? DMAX : 1); j++)
+                        if (j < d) s = __fmaf_rn(-xreg[j], cr[j], s);
+                } else {
+                    for (int j = 0; j < d; j++) s = __fmaf_rn(-xr[j], cr[j], s);
+                }
+                if (s < s1) { s2 = s1; s1 = s; l1 = c0 + cc; }
+                else if (s < s2) s2 = s;
+            }
+        }
+        if (!live) continue;
+        int l = l1;
+        const float win = __fmaf_rn(prep.win_coef, x2 + prep.cmax2, prep.win_abs);
+        if (!(s2 - s1 > win)) {             // inside the window (or not finite): decide in float64
+            double bd = INFINITY;
+            int bl = 0;
+            for (int c = 0; c < k; c++) {
+                double v = d64_pairwise(xr, a.C + (int64_t)c * d, d);
+                if (v < bd) { bd = v; bl = c; }
+            }
+            l = bl;
+            rescored++;
+        }
+        const float* cl = a.C + (int64_t)l * d;
+        float b = 0.0f;
+        for (int j = 0; j < d; j++) b = best32_term(b, xr[j], cl[j]);
+        if (!isfinite(b)) bad = 1;
+        if (a.labels) a.labels[i] = l;
+        if (a.best) a.best[i] = b;
+        long long* acc = a.smem_acc ? sacc + (size_t)l * W : a.totals + (size_t)l * W;
+        atomicAdd(reinterpret_cast<unsigned long long*>(acc), 1ull);
+        atomicAdd(reinterpret_cast<unsigned long long*>(acc + 1), (unsigned long long)quantize(b, scale_i));
+        for (int j = 0; j < d; j++)
+            atomicAdd(reinterpret_cast<unsigned long long*>(acc + 2 + j),
+                      (unsigned long long)quantize(xr[j], a.scale_x[j]));
+    }
+    __syncthreads();
+    for (int s = threadIdx.x; s < nslots; s += blockDim.x)
+        if (sacc[s]) atomicAdd(reinterpret_cast<unsigned long long*>(a.totals + s), (unsigned long long)sacc[s]);
+    if (rescored) atomicAdd(reinterpret_cast<unsigned long long*>(&a.counters[0]), (unsigned long long)rescored);
+    if (bad) atomicOr(reinterpret_cast<unsigned long long*>(&a.counters[1]), (unsigned long long)kFlagNonFinite);
+}
+
+// ---------------------------------------------------------------- launchers
+
+cudaError_t launch_colmax(const float* X, int64_t n, int d, unsigned int* colmax, cudaStream_t st) {
+    const int threads = 256;
+    int64_t total = n * (int64_t)d;
+    int64_t want = (int64_t)num_sms() * 8 * threads;
+    int64_t stride = (want / d) * d;
+    if (stride < d) stride = d;
+    if (stride > total) stride = ((total + d - 1) / d) * d;
+    int blocks = (int)((stride + threads - 1) / threads);
+    k_colmax<<<blocks, threads, sizeof(unsigned int) * d, st>>>(X, total, d, stride, colmax);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prepare(const float* C, int k, int d, const unsigned int* colmax, int64_t n_total, Prep* prep,
+                           double* scale_x, float* hc, cudaStream_t st) {
+    k_prepare<<<1, 1024, 0, st>>>(C, k, d, colmax, n_total, prep, scale_x, hc);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pass_generic(PassArgs a, cudaStream_t st) {
+    const int W = a.d + 2;
+    const size_t budget = 200 * 1024;
+    a.smem_acc = (size_t)a.k * W * 8 <= 96 * 1024 ? 1 : 0;
+    size_t acc_bytes = a.smem_acc ? (size_t)a.k * W * 8 : 0;
+    size_t per_center = (size_t)(a.d + 1) * 4;
+    size_t room = budget - acc_bytes;
+    int ct = (int)(room / per_center);
+    if (ct > a.k) ct = a.k;
+    if (ct > 1024) ct = 1024;
+    if (ct < 1) return cudaErrorInvalidValue;
+    a.ctile = ct;
+    size_t smem = acc_bytes + (size_t)ct * per_center;
+    const int threads = 256;
+    int64_t blocks64 = (a.n + threads - 1) / threads;
+    int cap = num_sms() * (a.smem_acc ? 2 : 4);
+    int blocks = (int)(blocks64 < cap ? blocks64 : cap);
+    if (blocks < 1) blocks = 1;
+    cudaError_t e;
+#define KMC_GENERIC_CASE(DM)                                                                            \
+    e = cudaFuncSetAttribute(k_pass_generic<DM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    if (e != cudaSuccess) return e;                                                                     \
+    k_pass_generic<DM><<<blocks, threads, smem, st>>>(a);
+    if (a.d <= 8) { KMC_GENERIC_CASE(8) }
+    else if (a.d <= 16) { KMC_GENERIC_CASE(16) }
+    else if (a.d <= 32) { KMC_GENERIC_CASE(32) }
+    else if (a.d <= 64) { KMC_GENERIC_CASE(64) }
+    else { KMC_GENERIC_CASE(0) }
+#undef KMC_GENERIC_CASE
+    return cudaGetLastError();
+}
+
+}  // namespace kmc

@@ -1,0 +1,167 @@
+"""scikit-learn-shaped KMeans on the B200 Lloyd path (the reference's mlx_kmeans/estimator.py API).
+
+    KMeans(n_clusters=64).fit(X).cluster_centers_
+
+Same constructor, attributes and errors as the reference (estimator.py:52-65, 180-230): n_clusters, n_init,
+max_iter, tol (relative inertia change), random_state, verbose, spherical, accumulate, exact, plus the
+reference's e-means options, which this build does not offer (algorithm must be "lloyd"). The Lloyd loop keeps
+its centers on the device; each step reads back one 64-byte statistics record for the tol test.
+"""
+import numpy as np
+import torch
+
+from . import core
+
+
+class KMeans:
+    """Exact k-means on B200 GPUs: every label is the float64-nearest center, lowest index on ties.
+
+    exact=False is accepted for API parity and runs the exact path (the reference ignores it as well below
+    its crossover dims; the approximate kernel is not part of this build yet). accumulate="atomic" also runs the
+    deterministic accumulation: totals here are exact integers, so there is no faster non-deterministic mode to
+    opt into.
+    """
+
+    def __init__(self, n_clusters=8, n_init=1, max_iter=300, tol=1e-4, random_state=None, verbose=False,
+                 spherical=False, accumulate="auto", exact=True, algorithm="lloyd", epochs=3, batch_size=None):
+        self.n_clusters = n_clusters
+        self.n_init = n_init
+        self.max_iter = max_iter
+        self.tol = tol
+        self.random_state = random_state
+        self.verbose = verbose
+        self.spherical = spherical
+        self.accumulate = accumulate
+        self.exact = exact
+        self.algorithm = algorithm
+        self.epochs = epochs
+        self.batch_size = batch_size
+
+    @property
+    def _method(self):
+        return "auto" if self.exact else "approx"
+
+    @classmethod
+    def from_centers(cls, centers, **kwargs):
+        """A fitted model from centers saved earlier (estimator.py:71-79)."""
+        centers = np.ascontiguousarray(centers, dtype=np.float32)
+        if not np.isfinite(centers).all():
+            raise ValueError("centers contain NaN or infinity")
+        model = cls(n_clusters=len(centers), **kwargs)
+        model.cluster_centers_ = centers
+        return model
+
+    @staticmethod
+    def _explain_nonfinite(ds):
+        """Say why a pass came back non-finite, then raise (estimator.py:81-106)."""
+        peak = ds.absmax()
+        if not np.isfinite(peak):
+            raise ValueError(
+                "input contains NaN or infinity, which would produce nan centers rather than an error. "
+                "Drop or impute those rows first (the file workflow's missing='drop' does this).")
+        limit = float(np.sqrt(np.finfo(np.float32).max / (4.0 * ds.d)))
+        if peak > limit:
+            raise ValueError(
+                f"largest coordinate is {peak:.3e}, above the {limit:.3e} this many dimensions allow: "
+                f"a squared distance would overflow float32 and return nan. Standardise the features "
+                f"(see the README) or rescale before fitting.")
+        raise ValueError("clustering produced a non-finite result, but the input values look usable; "
+                         "please report this with the data shape and dtype.")
+
+    @staticmethod
+    def _parts(X):
+        """-> a core.Dataset (device-resident rows), from NumPy, pandas, lists, CUDA tensors or a Dataset."""
+        if isinstance(X, core.Dataset):
+            return X
+        if isinstance(X, list) and X and isinstance(X[0], torch.Tensor):
+            return core.Dataset(X)
+        if isinstance(X, torch.Tensor):
+            if X.ndim != 2 or not all(X.shape):
+                raise ValueError(f"expected a nonempty 2-D (rows, dims) array, got shape {tuple(X.shape)}")
+            return core.Dataset([X])
+        if not isinstance(X, np.ndarray):
+            X = np.asarray(X.to_numpy() if hasattr(X, "to_numpy") else X)
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        if X.ndim != 2 or not all(X.shape):
+            raise ValueError(f"expected a nonempty 2-D (rows, dims) array, got shape {X.shape}")
+        return core.Dataset([X])
+
+    @staticmethod
+    def _normalise(C):
+        n = torch.linalg.vector_norm(C.double(), dim=1, keepdim=True)
+        return (C.double() / torch.where(n > 0, n, torch.ones_like(n))).float()
+
+    def _one_run(self, ds, rows, seed):
+        """estimator.py:132-150 with the centers kept on the device between steps."""
+        rng = np.random.default_rng(seed)
+        C = torch.from_numpy(core.kmeans_pp_init(ds, rows, self.n_clusters, rng)).to(ds.device)
+        if self.spherical:
+            C = self._normalise(C)
+        prev = None
+        inertia = float("nan")
+        it = 0
+        generic = self._method == "generic"
+        for it in range(self.max_iter):
+            C_new, s = ds.step(C, generic=generic)
+            C = C_new.clone()
+            inertia = s["inertia"]
+            if s["flags"] & 1 or not np.isfinite(inertia):
+                self._explain_nonfinite(ds)
+            if self.spherical:
+                C = self._normalise(C)
+            if self.verbose:
+                n_empty = s["n_empty"]
+                print(f"iter {it + 1}: inertia {inertia:.6e}" + (f", {n_empty} empty relocated" if n_empty else ""))
+            if prev is not None and abs(prev - inertia) <= self.tol * prev:
+                break
+            prev = inertia
+        return C, inertia, it + 1
+
+    def _check_algorithm(self):
+        algorithm = getattr(self, "algorithm", "lloyd")
+        if algorithm not in ("lloyd", "emeans"):
+            raise ValueError(f"algorithm must be 'lloyd' or 'emeans', got {algorithm!r}")
+        if algorithm == "emeans":
+            raise ValueError("algorithm='emeans' is not part of this build (the Lloyd path is)")
+
+    def fit(self, X, y=None):
+        for name in ['n_clusters', 'n_init', 'max_iter']:
+            value = getattr(self, name)
+            if isinstance(value, bool) or not isinstance(value, (int, np.integer)) or value < 1:
+                raise ValueError(f'{name} must be a positive integer')
+        if not np.isfinite(self.tol) or self.tol < 0:
+            raise ValueError('tol must be finite and nonnegative')
+        self._check_algorithm()
+        if self.accumulate not in core.ACCUMULATE_METHODS:
+            raise ValueError(f"unknown accumulate {self.accumulate!r}")
+        ds = self._parts(X)
+        rows = ds.n_total
+        if rows < self.n_clusters:
+            raise ValueError('n_clusters cannot exceed the number of rows')
+        best = None
+        for run in range(self.n_init):                  # restarts reuse the data already on the GPU
+            seed = None if self.random_state is None else self.random_state + run
+            C, inertia, iters = self._one_run(ds, rows, seed)
+            # A Lloyd step reports inertia before its center update: score the final centers (estimator.py:201-204)
+            _, _, inertia, labels = ds.assign(C, return_labels=True)
+            if self.verbose and self.n_init > 1:
+                print(f"start {run + 1}/{self.n_init}: inertia {inertia:.6e} after {iters} iterations")
+            if best is None or inertia < best[1]:
+                best = (C.cpu().numpy(), inertia, iters, labels)
+        self.cluster_centers_, self.inertia_, self.n_iter_, self.labels_ = best
+        return self
+
+    def predict(self, X):
+        """Cluster index for every row of X (any array-like)."""
+        ds = self._parts(X)
+        if ds.d != self.cluster_centers_.shape[1]:
+            raise ValueError(f"X has {ds.d} features but this model was fitted with "
+                             f"{self.cluster_centers_.shape[1]}")
+        C = torch.from_numpy(np.ascontiguousarray(self.cluster_centers_, dtype=np.float32)).to(ds.device)
+        _, _, inertia, labels = ds.assign(C, return_labels=True)
+        if not np.isfinite(inertia):
+            self._explain_nonfinite(ds)
+        return labels
+
+    def fit_predict(self, X, y=None):
+        return self.fit(X).labels_

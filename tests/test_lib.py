@@ -1,0 +1,56 @@
+"""libkmc.so: it builds for sm_100a, loads, and exports every entry point include/kmc.h declares (CPU tier:
+no compute call is made without a GPU)."""
+import os
+import re
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "kmc.h")
+
+
+def declared():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(kmc_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_boundary():
+    names = declared()
+    for n in ["kmc_pass", "kmc_finish", "kmc_far_rows", "kmc_colmax", "kmc_pp_init", "kmc_gen", "kmc_stats_read",
+              "kmc_totals_unpack", "kmc_workspace_bytes"]:
+        assert n in names
+
+
+def test_library_builds_and_exports_every_declared_symbol():
+    from mlx_kmeans_b200 import build
+    lib = build.build()
+    out = subprocess.run(["nm", "-D", "--defined-only", lib], capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r" T (kmc_\w+)", out))
+    missing = [n for n in declared() if n not in exported]
+    assert not missing, f"declared in kmc.h but not exported: {missing}"
+
+
+def test_ctypes_binding_covers_the_header():
+    from mlx_kmeans_b200 import _lib
+    assert sorted(_lib.SIGNATURES) == declared()
+    L = _lib.load()
+    assert L.kmc_version() >= 1
+    # size queries need no device
+    assert L.kmc_workspace_bytes(4, 16) > 0
+    assert L.kmc_far_workspace_bytes(8) > 0
+    assert L.kmc_pp_workspace_bytes(1000, 4, 16) > 0
+
+
+def test_invalid_arguments_are_reported_not_thrown():
+    from mlx_kmeans_b200 import _lib
+    L = _lib.load()
+    # null pointers / bad shapes fail in the argument checks, before any CUDA call
+    assert L.kmc_pass(None, 10, 0, None, 4, None, 10, None, None, None, 0, None, 0, None) == _lib.KMC_ERR_INVALID
+    assert b"dims" in L.kmc_last_error()
+    assert L.kmc_pass(None, 10, 5000, None, 4, None, 10, None, None, None, 0, None, 0, None) == _lib.KMC_ERR_UNSUPPORTED
+    assert L.kmc_finish(None, 4, 4, None, 0, 1, None, None, None, 0, None) == _lib.KMC_ERR_INVALID
+    with pytest.raises(ValueError):
+        _lib.call("kmc_pass", None, 10, 0, None, 4, None, 10, None, None, None, 0, None, 0, None)
