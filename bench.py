@@ -42,6 +42,7 @@ def parse():
     p.add_argument("--steps", type=int, default=400)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--config", type=int, default=3)
+    p.add_argument("--rows", type=int, default=None, help="override the configuration's row count (profiling)")
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--no-cpu", action="store_true")
@@ -200,7 +201,9 @@ def main():
         group = dist.group.WORLD
 
     cfg = args.config
-    c = CONFIGS[cfg]
+    c = dict(CONFIGS[cfg])
+    if args.rows:
+        c["rows"] = args.rows
     n_total, d, k = c["rows"], c["dims"], c["k"]
     lo, hi = shard_range(n_total, rank, world)
     X = generate(cfg, lo, hi - lo, dev, rows_total=n_total, group=group)
@@ -309,7 +312,9 @@ def main():
         "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": DESCRIPTION[cfg], "rows": n_total, "dims": d, "k": k,
+        "config": {"workload": DESCRIPTION[cfg] + ("" if n_total == CONFIGS[cfg]["rows"] else
+                                                   f" (rows overridden: {n_total})"),
+                   "rows": n_total, "dims": d, "k": k,
                    "parallelism": f"rows sharded dp{world}, int64 totals all-reduced (NCCL)",
                    "l2": "inputs larger than L2 (%.2f GB per GPU), no flush" % (bytes_per_launch / 1e9),
                    "relocation_steps_in_timed_region": reloc_steps,

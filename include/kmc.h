@@ -60,6 +60,9 @@ int kmc_version(void);
 const char *kmc_last_error(void);
 /* Number of streaming multiprocessors of the current device (grid sizing of the caller's own work). */
 int kmc_num_sms(void);
+/* Row granularity of the pass kernels' fixed blocks: when every shard / slice starts at a global row that
+ * is a multiple of this, the totals are bit-identical however the rows are split over slices and GPUs. */
+int64_t kmc_row_block(void);
 
 /* ---------------------------------------------------------------- workspace */
 

@@ -90,6 +90,8 @@ const char* kmc_last_error(void) { return g_err.c_str(); }
 
 int kmc_num_sms(void) { return num_sms(); }
 
+int64_t kmc_row_block(void) { return lowd_block_rows(); }
+
 size_t kmc_workspace_bytes(int d, int k) { return carve(nullptr, d, k).bytes; }
 
 size_t kmc_far_workspace_bytes(int64_t cand_rows) { return carve_far(nullptr, cand_rows).bytes; }

@@ -55,6 +55,7 @@ cudaError_t launch_prepare(const float* C, int k, int d, const unsigned int* col
 cudaError_t launch_pass_generic(PassArgs a, cudaStream_t st);
 // Specialised low-dimensional fused pass; returns cudaErrorNotSupported when (d, k) has no instance.
 cudaError_t launch_pass_lowd(PassArgs a, cudaStream_t st);
+int64_t lowd_block_rows();
 
 cudaError_t launch_far_rows(const float* X, int64_t n, int d, const int32_t* labels, const float* best, int64_t row0,
                             int64_t cand_rows, uint32_t* cands, const FarWorkspace& ws, cudaStream_t st);

@@ -56,9 +56,15 @@ def mixture_params(cfg):
     raise ValueError(f"unknown configuration {cfg}")
 
 
-def shard_range(n_total, rank, world):
-    """Contiguous rows [lo, hi) of rank `rank` of `world`."""
-    return n_total * rank // world, n_total * (rank + 1) // world
+def shard_range(n_total, rank, world, align=None):
+    """Contiguous rows [lo, hi) of rank `rank` of `world`; every boundary a multiple of `align` (default: the
+    library's row block, so the totals are bit-identical for any number of GPUs)."""
+    if align is None:
+        align = int(_lib.load().kmc_row_block())
+    blocks = (n_total + align - 1) // align
+    lo = min(n_total, (blocks * rank // world) * align)
+    hi = min(n_total, (blocks * (rank + 1) // world) * align)
+    return lo, hi
 
 
 def generate(cfg, row0, n, device, rows_total=None, group=None):

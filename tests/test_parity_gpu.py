@@ -152,3 +152,77 @@ def test_errors_match_the_reference(cuda_device):
         km.KMeans(n_clusters=4, max_iter=2, random_state=0).fit(huge)
     with pytest.raises(ValueError, match="n_clusters"):
         km.KMeans(n_clusters=50).fit(rng.standard_normal((10, 3)).astype(np.float32))
+
+
+# ---------------------------------------------------------------- the fused low-dimensional kernel
+
+def _oracle_totals(X, labels, k):
+    sums = np.zeros((k, X.shape[1]))
+    np.add.at(sums, labels, X.astype(np.float64))
+    return sums, np.bincount(labels, minlength=k)
+
+
+def test_config1_full_fused_vs_generic_vs_oracle(cuda_device):
+    import mlx_kmeans_b200 as km
+    from mlx_kmeans_b200.data import generate
+    torch = _torch()
+    X = generate(1, 0, 100_000, cuda_device)
+    Xh = X.cpu().numpy()
+    C = Xh[np.random.default_rng(0).choice(len(Xh), 8, replace=False)].copy()
+    ds = km.Dataset([X])
+    Cd = torch.from_numpy(C).to(cuda_device)
+    fused = ds.assign(Cd, return_labels=True)
+    generic = ds.assign(Cd, return_labels=True, generic=True)
+    ref_labels, _, best = O.assign(Xh, C)
+    _check_assign(Xh, C, fused, ref_labels)
+    _check_assign(Xh, C, generic, ref_labels)
+    assert np.array_equal(fused[1], generic[1])
+
+
+def test_config3_slice_matches_oracle(cuda_device):
+    """2M rows of the 96M-row configuration (same generator, standardised over the slice)."""
+    import mlx_kmeans_b200 as km
+    from mlx_kmeans_b200.data import generate
+    torch = _torch()
+    X = generate(3, 0, 2_000_000, cuda_device, rows_total=2_000_000)
+    Xh = X.cpu().numpy()
+    C = Xh[np.random.default_rng(3).choice(len(Xh), 16, replace=False)].copy()
+    ds = km.Dataset([X])
+    b = ds.run_pass(torch.from_numpy(C).to(cuda_device), labels=True)
+    labels = b["labels"][0].cpu().numpy()
+    best = b["best"][0].cpu().numpy()
+    ref_labels, _, ref_best = O.assign(Xh, C)
+    assert np.array_equal(labels, ref_labels)
+    assert np.array_equal(best.view(np.uint32), ref_best.view(np.uint32)), "best must be bit-exact"
+    out = ds.assign(torch.from_numpy(C).to(cuda_device), return_labels=True)
+    _check_assign(Xh, C, out, ref_labels)
+
+
+def test_fused_is_deterministic_and_block_split_invariant(cuda_device):
+    import mlx_kmeans_b200 as km
+    from mlx_kmeans_b200 import _lib
+    from mlx_kmeans_b200.data import generate
+    torch = _torch()
+    blk = int(_lib.load().kmc_row_block())
+    n = 37 * blk + 1234
+    X = generate(3, 0, n, cuda_device, rows_total=n)
+    C = X[torch.arange(0, 16, device=cuda_device) * 997].contiguous()
+    a = km.Dataset([X]).assign(C, return_labels=True)
+    b = km.Dataset([X]).assign(C, return_labels=True)
+    cuts = [0, 5 * blk, 21 * blk, n]
+    c = km.Dataset([X[lo:hi] for lo, hi in zip(cuts[:-1], cuts[1:])]).assign(C, return_labels=True)
+    for u, v, w in zip(a, b, c):
+        assert np.array_equal(np.asarray(u), np.asarray(v))
+        assert np.array_equal(np.asarray(u), np.asarray(w))
+
+
+def test_window_rows_are_rescored(cuda_device):
+    """Exact float64 ties (integer grid, mirrored centers) must reach the float64 re-scoring."""
+    import mlx_kmeans_b200 as km
+    g = load_golden("integer_grid_ties_d6_k12")
+    ds = _ds(g["X"], cuda_device)
+    C = _torch().from_numpy(g["C"]).to(cuda_device)
+    _, s = ds.step(C)
+    assert s["rescored"] > 50
+    labels = ds.assign(C, return_labels=True)[3]
+    assert np.array_equal(labels, g["labels"])
