@@ -3,7 +3,7 @@
 Bars (the reference's tests/accuracy.py:86-99, tightened where the design allows):
   labels   bit-exact to the float64 oracle (lowest index on exact ties)
   counts   exact
-  sums     within 1e-9 of the float64 sums, relative to |data| RMS x count (reference bar: 1e-6 for centers)
+  sums     within 1e-7 of the float64 sums, relative to |data| RMS x count (reference bar: 1e-6 for centers)
   inertia  within 1e-6 relative of sum over rows of the float32 `best` in float64
   centers  (Lloyd step) within 1e-6 relative to the data RMS; relocated clusters bit-equal to their row
 """
@@ -43,7 +43,7 @@ def _check_assign(X, C, out, labels_ref):
     np.add.at(ref_sums, labels_ref, X.astype(np.float64))
     rms = float(np.sqrt((X.astype(np.float64) ** 2).mean())) or 1.0
     err = np.abs(sums - ref_sums) / (rms * np.maximum(ref_counts, 1)[:, None])
-    assert err.max() <= 1e-9
+    assert err.max() <= 1e-7
     _, _, best = O.assign(X, C)
     ref_inertia = float(best.astype(np.float64).sum())
     assert abs(inertia - ref_inertia) <= 1e-6 * max(ref_inertia, 1e-30)
