@@ -261,6 +261,7 @@ def main():
     pass_ms = statistics.mean(a.elapsed_time(z) for a, z in ev)
     st_host = stats.cpu().numpy().view(np.int64).reshape(K, 8)
     reloc_steps = int((st_host[:, 3] != 0).sum())
+    rescored = float(st_host[:, 5].mean())
     if world > 1:
         t = torch.tensor([total_ms, pass_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
@@ -318,6 +319,7 @@ def main():
                    "parallelism": f"rows sharded dp{world}, int64 totals all-reduced (NCCL)",
                    "l2": "inputs larger than L2 (%.2f GB per GPU), no flush" % (bytes_per_launch / 1e9),
                    "relocation_steps_in_timed_region": reloc_steps,
+                   "rows_rescored_in_float64_per_pass": rescored,
                    "kernel": "generic" if args.generic else "auto"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / pk["hbm_gbs"], "traffic": traffic,

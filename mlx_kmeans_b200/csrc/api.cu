@@ -145,6 +145,7 @@ int kmc_pass(const float* X, int64_t n, int d, const float* C, int k, const uint
     a.counters = ws.counters;
     a.smem_acc = 0;
     a.ctile = 0;
+    a.key_keep = 0;
     e = cudaErrorNotSupported;
     if (!(flags & KMC_PASS_GENERIC)) e = launch_pass_lowd(a, st);
     if (e == cudaErrorNotSupported) e = launch_pass_generic(a, st);

@@ -25,6 +25,7 @@ struct PassArgs {
     long long* counters;      // [0] rows re-scored, [1] flags
     int smem_acc;             // generic kernel: accumulate in shared memory
     int ctile;                // generic kernel: centers per shared tile
+    unsigned key_keep;        // fused low-d kernel: ~(center index bits) of a key
 };
 
 // Pass workspace carve-up (256-byte aligned pieces): kmc_pass writes prep/scale_x/hc/counters,

@@ -31,8 +31,8 @@ namespace {
 constexpr int kThreads = 128;          // 4 warps per CTA
 constexpr int kWarps = kThreads / 32;
 constexpr int kStages = 8;             // ring slots per thread (power of two)
-constexpr int kRowsPerLane = 64;       // rows per lane between folds (a multiple of kStages, < 256)
-constexpr int kBlockRows = kThreads * kRowsPerLane;   // 8192 rows per block
+constexpr int kRowsPerLane = 128;      // rows per lane between folds (a multiple of kStages, < 256)
+constexpr int kBlockRows = kThreads * kRowsPerLane;   // 16384 rows per block
 static_assert(kRowsPerLane % kStages == 0 && kRowsPerLane < 256, "block layout");
 
 __device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
@@ -44,6 +44,11 @@ __device__ __forceinline__ float hi_of(unsigned long long v) { return __uint_as_
 __device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned long long c) {
     unsigned long long d;
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
 __device__ __forceinline__ unsigned long long sub2(unsigned long long a, unsigned long long b) {
@@ -62,18 +67,53 @@ __device__ __forceinline__ float min3(float a, float b, float c) {
     return d;
 }
 
-// key = score with its low mantissa bits replaced by the center index
-template <unsigned MASK>
-__device__ __forceinline__ float keyed(float s, unsigned idx) {
-    return __uint_as_float((__float_as_uint(s) & ~MASK) | idx);
+// key = distance with its low mantissa bits replaced by the center index: (s & keep) | IDX in one lop3, the
+// index an immediate and keep (~index mask) a register
+template <unsigned IDX>
+__device__ __forceinline__ float keyed_imm(float s, unsigned keep) {
+    unsigned d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEC;" : "=r"(d) : "r"(__float_as_uint(s)), "n"(IDX), "r"(keep));
+    return __uint_as_float(d);
 }
 
-// add to a shared-memory word only this thread touches (program order => deterministic)
-__device__ __forceinline__ void red_add(float* p, float v) {
-    asm volatile("red.shared.add.f32 [%0], %1;" ::"r"((unsigned)__cvta_generic_to_shared(p)), "f"(v) : "memory");
+__host__ __device__ constexpr unsigned idx_bits(int k) { return k <= 2 ? 1 : k <= 4 ? 2 : k <= 8 ? 3 : k <= 16 ? 4 : 5; }
+
+// s[0..D) += t in shared memory (a slot only this thread touches, so a plain read-modify-write), in
+// 16- / 8-byte pieces where D allows
+template <int D>
+__device__ __forceinline__ void add_row(unsigned saddr, const float (&t)[D]) {
+    if constexpr (D % 4 == 0) {
+#pragma unroll
+        for (int q = 0; q < D / 4; q++) {
+            float a0, a1, a2, a3;
+            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(a0), "=f"(a1), "=f"(a2), "=f"(a3) : "r"(saddr + 16 * q));
+            unsigned long long lo = add2(pack2(a0, a1), pack2(t[4 * q], t[4 * q + 1]));
+            unsigned long long hi = add2(pack2(a2, a3), pack2(t[4 * q + 2], t[4 * q + 3]));
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(saddr + 16 * q), "f"(lo_of(lo)), "f"(hi_of(lo)),
+                         "f"(lo_of(hi)), "f"(hi_of(hi)) : "memory");
+        }
+    } else if constexpr (D % 2 == 0) {
+#pragma unroll
+        for (int q = 0; q < D / 2; q++) {
+            float a0, a1;
+            asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(a0), "=f"(a1) : "r"(saddr + 8 * q));
+            unsigned long long s = add2(pack2(a0, a1), pack2(t[2 * q], t[2 * q + 1]));
+            asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(saddr + 8 * q), "f"(lo_of(s)), "f"(hi_of(s)) : "memory");
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < D; j++) {
+            float a;
+            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(a) : "r"(saddr + 4 * j));
+            asm volatile("st.shared.f32 [%0], %1;" ::"r"(saddr + 4 * j), "f"(__fadd_rn(a, t[j])) : "memory");
+        }
+    }
 }
-__device__ __forceinline__ void red_add(unsigned* p, unsigned v) {
-    asm volatile("red.shared.add.u32 [%0], %1;" ::"r"((unsigned)__cvta_generic_to_shared(p)), "r"(v) : "memory");
+
+__device__ __forceinline__ void add_u32(unsigned saddr, unsigned v) {
+    unsigned a;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(a) : "r"(saddr));
+    asm volatile("st.shared.u32 [%0], %1;" ::"r"(saddr), "r"(a + v) : "memory");
 }
 
 template <int BYTES>
@@ -119,24 +159,53 @@ __device__ __forceinline__ double d64_regs(const float* x, const float* c) {
     }
 }
 
+// D floats from shared memory (32-bit shared-window address), in 16- or 8-byte pieces where D allows;
+// the caller guarantees the alignment (rows and centers start at multiples of D floats, the buffers at 16 B)
 template <int D>
-__device__ __forceinline__ void load_row(float (&x)[D], const float* src) {
+__device__ __forceinline__ void load_row(float (&x)[D], unsigned saddr) {
     if constexpr (D % 4 == 0) {
 #pragma unroll
-        for (int q = 0; q < D / 4; q++) {
-            float4 v = reinterpret_cast<const float4*>(src)[q];
-            x[4 * q] = v.x; x[4 * q + 1] = v.y; x[4 * q + 2] = v.z; x[4 * q + 3] = v.w;
-        }
+        for (int q = 0; q < D / 4; q++)
+            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(x[4 * q]), "=f"(x[4 * q + 1]), "=f"(x[4 * q + 2]), "=f"(x[4 * q + 3])
+                         : "r"(saddr + 16 * q));
     } else if constexpr (D % 2 == 0) {
 #pragma unroll
-        for (int q = 0; q < D / 2; q++) {
-            float2 v = reinterpret_cast<const float2*>(src)[q];
-            x[2 * q] = v.x; x[2 * q + 1] = v.y;
-        }
+        for (int q = 0; q < D / 2; q++)
+            asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(x[2 * q]), "=f"(x[2 * q + 1]) : "r"(saddr + 8 * q));
     } else {
 #pragma unroll
-        for (int j = 0; j < D; j++) x[j] = src[j];
+        for (int j = 0; j < D; j++) asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x[j]) : "r"(saddr + 4 * j));
     }
+}
+
+template <int D>
+struct RowVec {
+    float v[D];
+};
+
+// Decide the warp's rows flagged in `fm` in float64, one center per lane, lowest index on exact ties; returns
+// the label of the calling lane's row (`l` when its row is not flagged).  Out of line: it runs for a few rows
+// per million and would otherwise take registers from the row loop.
+template <int D>
+__device__ __noinline__ int rescore_rows(unsigned fm, RowVec<D> x, const float* cs, int k, int lane, int l) {
+    while (fm) {
+        const int src = __ffs(fm) - 1;
+        fm &= fm - 1;
+        float xs[D];
+#pragma unroll
+        for (int j = 0; j < D; j++) xs[j] = __shfl_sync(0xffffffffu, x.v[j], src);
+        double v = lane < k ? d64_regs<D>(xs, cs + lane * D) : INFINITY;
+        int vi = lane;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            double ov = __shfl_xor_sync(0xffffffffu, v, o);
+            int oi = __shfl_xor_sync(0xffffffffu, vi, o);
+            if (ov < v || (ov == v && oi < vi)) { v = ov; vi = oi; }
+        }
+        if (lane == src) l = vi;
+    }
+    return l;
 }
 
 }  // namespace
@@ -159,14 +228,34 @@ template <int D, int K>
 struct LowdRow {
     unsigned long long cp2[K / 2][D];   // -c, two centers per register pair
     unsigned long long hp2[K / 2];      // |c|^2 / 2
-    float coef, cmax2, wabs;
+    float coef, slack, cmax2, wabs;
+    unsigned keep;                      // ~(index mask), a launch argument so it stays in a register
     const float* cs;                    // shared copy of the centers (zero padded to 32 rows)
-    float* sums;                        // this warp's sums slots
-    unsigned* cnts;                     // this warp's packed counts
+    unsigned cs_s;                      // its shared-window address
+    float* sums;                        // this warp's sums slots: [cluster][lane][D]
+    unsigned* cnts;                     // this warp's packed 8-bit counts: [cluster / 4][lane]
+    unsigned sums_s, cnts_s;            // their shared-window addresses
     int lane, k;
     double inert;
     long long rescored;
     int bad;
+
+    // keys of centers 2P and 2P+1: one packed distance chain, then one lop3 each inserting the index
+    template <int P>
+    __device__ __forceinline__ void pair(const unsigned long long (&xx)[D], unsigned long long xh2, float (&t1)[K / 2],
+                                         float (&t2)[K / 2]) {
+        unsigned long long s = add2(xh2, hp2[P]);
+#pragma unroll
+        for (int j = 0; j < D; j++) s = fma2(xx[j], cp2[P][j], s);
+        const float ka = keyed_imm<2 * P>(lo_of(s), keep), kb = keyed_imm<2 * P + 1>(hi_of(s), keep);
+        t1[P] = fminf(ka, kb);
+        t2[P] = fmaxf(ka, kb);
+    }
+    template <int... P>
+    __device__ __forceinline__ void pairs(std::integer_sequence<int, P...>, const unsigned long long (&xx)[D],
+                                          unsigned long long xh2, float (&t1)[K / 2], float (&t2)[K / 2]) {
+        (pair<P>(xx, xh2, t1, t2), ...);
+    }
 
     template <bool CHECK, bool OUT>
     __device__ __forceinline__ void row(const float (&x)[D], int64_t row, int64_t n, int32_t* labels, float* best) {
@@ -181,16 +270,12 @@ struct LowdRow {
             xx[j] = pack2(x[j], x[j]);
             x2 = __fmaf_rn(x[j], x[j], x2);
         }
+        // half squared distance |x|^2/2 + |c|^2/2 - x.c: near the winner it is small, so are the index
+        // bits' perturbations of the keys
+        const float xh = 0.5f * x2;
+        const unsigned long long xh2 = pack2(xh, xh);
         float t1[K / 2], t2[K / 2];
-#pragma unroll
-        for (int p = 0; p < K / 2; p++) {
-            unsigned long long s = hp2[p];
-#pragma unroll
-            for (int j = 0; j < D; j++) s = fma2(xx[j], cp2[p][j], s);
-            const float ka = keyed<MASK>(lo_of(s), 2u * p), kb = keyed<MASK>(hi_of(s), 2u * p + 1u);
-            t1[p] = fminf(ka, kb);
-            t2[p] = fmaxf(ka, kb);
-        }
+        pairs(std::make_integer_sequence<int, K / 2>{}, xx, xh2, t1, t2);
 #pragma unroll
         for (int w = K / 4; w >= 1; w >>= 1) {
 #pragma unroll
@@ -202,35 +287,23 @@ struct LowdRow {
         }
         const float m1 = t1[0], m2 = t2[0];
         int l = (int)(__float_as_uint(m1) & MASK);
-        const float win = __fmaf_rn(coef, x2 + cmax2, wabs);
+        const float win = __fmaf_rn(coef, x2 + cmax2, wabs) + slack * (fabsf(m1) + fabsf(m2));
         const bool flag = valid && !(m2 - m1 > win);
 
         // ---- rows inside the window: float64, one center per lane, lowest index on ties
         unsigned fm = __ballot_sync(0xffffffffu, flag);
         if (fm) {
             rescored += flag ? 1 : 0;
-            while (fm) {
-                const int src = __ffs(fm) - 1;
-                fm &= fm - 1;
-                float xs[D];
+            RowVec<D> xv;
 #pragma unroll
-                for (int j = 0; j < D; j++) xs[j] = __shfl_sync(0xffffffffu, x[j], src);
-                double v = lane < k ? d64_regs<D>(xs, cs + lane * D) : INFINITY;
-                int vi = lane;
-#pragma unroll
-                for (int o = 16; o; o >>= 1) {
-                    double ov = __shfl_xor_sync(0xffffffffu, v, o);
-                    int oi = __shfl_xor_sync(0xffffffffu, vi, o);
-                    if (ov < v || (ov == v && oi < vi)) { v = ov; vi = oi; }
-                }
-                if (lane == src) l = vi;
-            }
+            for (int j = 0; j < D; j++) xv.v[j] = x[j];
+            l = rescore_rows<D>(fm, xv, cs, k, lane, l);
         }
         if (!valid) return;
 
         // ---- residual t = x - c_l and best = sum t^2 (each op rounded on its own, in column order)
         float c[D];
-        load_row<D>(c, cs + l * D);
+        load_row<D>(c, cs_s + (unsigned)(l * D * 4));
         float t[D], q[D];
         if constexpr (D % 2 == 0) {
 #pragma unroll
@@ -250,21 +323,30 @@ struct LowdRow {
         float b = q[0];                    // 0 + q0 == q0 exactly
 #pragma unroll
         for (int j = 1; j < D; j++) b = __fadd_rn(b, q[j]);
-        float* sl = sums + l * (D * 32) + lane;
-#pragma unroll
-        for (int j = 0; j < D; j++) red_add(sl + j * 32, t[j]);
-        red_add(cnts + (l >> 2) * 32 + lane, 1u << ((l & 3) * 8));
-        inert = __dadd_rn(inert, (double)b);
+        // this lane's slot of cluster l (plain read-modify-write: nobody else touches it)
+        add_row<D>(sums_s + (unsigned)((l * 32 + lane) * D * 4), t);
+        add_u32(cnts_s + (unsigned)(((l >> 2) * 32 + lane) * 4), 1u << ((l & 3) * 8));
+        ichunk = __fadd_rn(ichunk, b);     // float32 over at most kStages rows, then float64
         if (OUT) {
             if (labels) labels[row] = l;
             if (best) best[row] = b;
         }
-        if (!(b <= 3.0e38f)) bad = 1;
     }
+
+    // end of a chunk of kStages rows: the float32 partial of the inertia joins the float64 one
+    __device__ __forceinline__ void chunk_done() {
+        inert = __dadd_rn(inert, (double)ichunk);
+        ichunk = 0.0f;
+    }
+    float ichunk;
 };
 
+#ifndef KMC_LOWD_MIN_BLOCKS
+#define KMC_LOWD_MIN_BLOCKS 4
+#endif
+
 template <int D, int K, bool OUT>
-__global__ void __launch_bounds__(kThreads, 4) k_pass_lowd(PassArgs a) {
+__global__ void __launch_bounds__(kThreads, KMC_LOWD_MIN_BLOCKS) k_pass_lowd(PassArgs a) {
     static_assert(K % 2 == 0 && K <= 32, "K even, at most 32");
     constexpr int CPB = (D % 4 == 0) ? 16 : ((D % 2 == 0) ? 8 : 4);   // bytes per cp.async
     constexpr int NCP = D * 4 / CPB;
@@ -300,75 +382,95 @@ __global__ void __launch_bounds__(kThreads, 4) k_pass_lowd(PassArgs a) {
     }
     const Prep prep = *a.prep;
     // both keys' index bits move them by < 2^(IDXBITS-23) |key| <= 2^(IDXBITS-23) (|x|^2 + max|c|^2)
-    st.coef = prep.win_coef + 1.0f / (float)(1u << (21 - IDXBITS));
+    // Window of the screen.  With u = 2^-24 and g = D u / (1 - D u), the computed half distance of every
+    // center is within (2 g + u / 2)(|x|^2 + |c|^2) of the exact one (|x|^2 and |c|^2 each carry g, the add
+    // that joins them u, the fma chain g on |x|^2/2 + |c|^2/2 + |x||c|), so two centers within
+    // (4 g + u)(|x|^2 + max|c|^2) -- taken with a 2^-10 margin plus D 2^-48 for the float64 rounding of
+    // D64 -- may be misordered.  The index bits move a key by less than 2^(IDXBITS-23) of itself; every key
+    // above the second smallest is at least that key less that share, hence slack = 2^(IDXBITS-22) on
+    // |m1| + |m2| (a factor two to spare).
+    st.coef = (float)(((4.0 * D + 2.0) / 16777216.0) * (1.0 + 1.0 / 1024.0) + (double)D / 281474976710656.0);
+    st.slack = 1.0f / (float)(1u << (22 - IDXBITS));
+    st.keep = a.key_keep;
     st.cmax2 = prep.cmax2;
     st.wabs = prep.win_abs;
     st.cs = cs;
+    st.cs_s = (unsigned)__cvta_generic_to_shared(cs);
     st.sums = sums_all + (size_t)warp * L::kSums;
     st.cnts = cnts_all + (size_t)warp * L::kCnts;
+    st.sums_s = (unsigned)__cvta_generic_to_shared(st.sums);
+    st.cnts_s = (unsigned)__cvta_generic_to_shared(st.cnts);
     st.lane = lane;
     st.k = k;
     st.inert = 0.0;
+    st.ichunk = 0.0f;
     st.rescored = 0;
     st.bad = 0;
 
     // Row of thread tid at step r of block b: b * kBlockRows + r * kThreads + tid.  Ring slot r % kStages
     // holds step r; the prefetch of step r + kStages - 1 is issued at step r into the slot read at step
-    // r - 1, so this thread's reads of that slot have completed.
+    // r - 1, so this thread's reads of that slot have completed.  The prefetch walks a pointer (and, near
+    // the end of the rows, a row index) kStages - 1 steps ahead of the reads, jumping to the CTA's next
+    // block when it leaves the current one.
     const int64_t nblk = (n + kBlockRows - 1) / kBlockRows;
     float* myring = ring + (size_t)tid * D;
+    const unsigned myring_s = (unsigned)__cvta_generic_to_shared(myring);
     constexpr int SLOT = kThreads * D;
-    auto fetch = [&](int slot, int64_t row) {
-        if (row < n) {
-            const float* src = a.X + row * D;
+    constexpr int STEP = kThreads * D;                 // floats between a thread's consecutive rows
+    const float* pf = a.X + ((int64_t)blockIdx.x * kBlockRows + tid) * D;
+    int64_t pf_row = (int64_t)blockIdx.x * kBlockRows + tid;
+    auto fetch = [&](int slot, bool ok) {
+        if (ok) {
             float* dst = myring + slot * SLOT;
 #pragma unroll
-            for (int q = 0; q < NCP; q++) cp_async<CPB>(dst + q * (CPB / 4), src + q * (CPB / 4));
+            for (int q = 0; q < NCP; q++) cp_async<CPB>(dst + q * (CPB / 4), pf + q * (CPB / 4));
         }
         cp_commit();
+        pf += STEP;
+        pf_row += kThreads;
     };
-    {
-        const int64_t base0 = (int64_t)blockIdx.x * kBlockRows + tid;
 #pragma unroll
-        for (int s = 0; s < kStages - 1; s++) fetch(s, base0 + (int64_t)s * kThreads);
-    }
+    for (int s = 0; s < kStages - 1; s++) fetch(s, pf_row < n);
 
     for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
         const int64_t base = blk * kBlockRows + tid;
         const int64_t next = (blk + gridDim.x) * kBlockRows + tid;
-        const bool full = (blk + 1) * kBlockRows <= n;
+        // checks are needed only while this block or the prefetched part of the next one is ragged
+        const bool clean = (blk + gridDim.x + 1) * kBlockRows <= n;
         auto steps = [&](auto check) {
             constexpr bool CHECK = decltype(check)::value;
             for (int ch = 0; ch < kRowsPerLane / kStages; ch++) {
 #pragma unroll
                 for (int s = 0; s < kStages; s++) {
                     const int r = ch * kStages + s;
-                    const int pr = r + kStages - 1;
-                    fetch((s + kStages - 1) & (kStages - 1),
-                          pr < kRowsPerLane ? base + (int64_t)pr * kThreads
-                                            : next + (int64_t)(pr - kRowsPerLane) * kThreads);
+                    if (s == 1 && ch == kRowsPerLane / kStages - 1) {   // step r + kStages - 1 == kRowsPerLane
+                        pf = a.X + next * D;
+                        pf_row = next;
+                    }
+                    fetch((s + kStages - 1) & (kStages - 1), !CHECK || pf_row < n);
                     cp_wait<kStages - 1>();
                     float x[D];
-                    load_row<D>(x, myring + s * SLOT);
+                    load_row<D>(x, myring_s + (unsigned)(s * SLOT * 4));
                     st.template row<CHECK, OUT>(x, base + (int64_t)r * kThreads, n, a.labels, a.best);
                 }
+                st.chunk_done();
             }
         };
-        if (full) steps(std::integral_constant<bool, false>{});
+        if (clean) steps(std::integral_constant<bool, false>{});
         else steps(std::integral_constant<bool, true>{});
 
         // ---- fold the lanes' slots into the CTA's int64 totals (fixed order => deterministic)
         __syncwarp();
         float* sums = st.sums;
         unsigned* cnts = st.cnts;
+        // slot (c, lane) holds D floats at sums[(c * 32 + lane) * D]; lane L folds columns s = c * D + j
         for (int s = lane; s < K * D; s += 32) {
-            float* col = sums + (size_t)s * 32;
+            float* col = sums + (size_t)(s / D) * 32 * D + (s % D);
             double sum = 0.0;
 #pragma unroll 8
             for (int i = 0; i < 32; i++) {
                 const int li = (i + lane) & 31;
-                sum = __dadd_rn(sum, (double)col[li]);
-                col[li] = 0.0f;
+                sum = __dadd_rn(sum, (double)col[li * D]);
             }
             fold[(s / D) * (D + 1) + (s % D)] = sum;
         }
@@ -382,6 +484,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_pass_lowd(PassArgs a) {
         }
         __syncwarp();
         for (int e = lane; e < L::kCnts; e += 32) cnts[e] = 0u;
+        for (int e = lane; e < L::kSums; e += 32) sums[e] = 0.0f;
         for (int s = lane; s < K * (D + 1); s += 32) {
             const int c = s / (D + 1), j = s % (D + 1);
             if (c >= k) continue;
@@ -399,7 +502,8 @@ __global__ void __launch_bounds__(kThreads, 4) k_pass_lowd(PassArgs a) {
         double inert = st.inert;
 #pragma unroll
         for (int o = 16; o; o >>= 1) inert = __dadd_rn(inert, __shfl_xor_sync(0xffffffffu, inert, o));
-        if (lane == 0 && inert != 0.0)
+        if (!(inert <= 1.0e300)) st.bad = 1;            // a non-finite distance anywhere in the block
+        else if (lane == 0 && inert != 0.0)
             atomicAdd(reinterpret_cast<unsigned long long*>(&acc[1]),
                       (unsigned long long)__double2ll_rn(__dmul_rn(inert, prep.scale_i)));
         st.inert = 0.0;
@@ -440,6 +544,7 @@ cudaError_t run(PassArgs a, cudaStream_t st) {
     int64_t grid = (int64_t)num_sms() * per_sm;
     if (grid > nblk) grid = nblk;
     if (grid < 1) grid = 1;
+    a.key_keep = ~((1u << idx_bits(K)) - 1u);
     k_pass_lowd<D, K, OUT><<<(int)grid, kThreads, smem, st>>>(a);
     return cudaGetLastError();
 }
