@@ -94,6 +94,20 @@ int kmc_pass(const float *X, int64_t n, int d, const float *C, int k, const uint
              int64_t *totals, int32_t *labels, float *best, unsigned flags, void *workspace, size_t ws_bytes,
              void *stream);
 
+/* kmc_pass without a caller workspace.  No counterpart in the reference: it exists for callers that cannot
+ * allocate device memory -- a host runtime that owns every device allocation through its own pool, or a
+ * phase of a program in which calling an allocator is not allowed -- and so cannot provide the workspace
+ * kmc_pass asks for.  Its scratch is a file-scope device array of KMC_STATIC_SCRATCH_BYTES per GPU, held from
+ * the library's load until the process exits; shapes needing more (kmc_workspace_bytes(d, k) above it, e.g.
+ * k above ~4000 at d = 64) are refused with KMC_ERR_UNSUPPORTED.  It calls no allocator.  The first call on a
+ * device looks up that device's copy of the array (cudaGetSymbolAddress); make that first call before any
+ * stream capture.  All calls share the one array and it keeps the last call's contents: calls whose work
+ * overlaps on the GPU race, so issue them in one stream (or order them).  The pass clears what must start at
+ * zero itself (totals and counters, unless KMC_PASS_ACCUMULATE).  Arguments, outputs and errors as kmc_pass. */
+#define KMC_STATIC_SCRATCH_BYTES (64 * 1024)
+int kmc_pass_static(const float *X, int64_t n, int d, const float *C, int k, const uint32_t *colmax,
+                    int64_t n_total, int64_t *totals, int32_t *labels, float *best, unsigned flags, void *stream);
+
 /* Local relocation candidates: the `cand_rows` rows of X with the largest best (lower row index on
  * ties), as records of (d + 4) 32-bit words [best, global row lo, global row hi, label, x_0 .. x_{d-1}],
  * farthest first, padded with best = -1.  row0 = global index of local row 0.

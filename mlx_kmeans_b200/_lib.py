@@ -33,6 +33,7 @@ SIGNATURES = {
     "kmc_far_workspace_bytes": (_sz, [_i64]),
     "kmc_colmax": (_int, [_vp, _i64, _int, _vp, _u, _vp]),
     "kmc_pass": (_int, [_vp, _i64, _int, _vp, _int, _vp, _i64, _vp, _vp, _vp, _u, _vp, _sz, _vp]),
+    "kmc_pass_static": (_int, [_vp, _i64, _int, _vp, _int, _vp, _i64, _vp, _vp, _vp, _u, _vp]),
     "kmc_far_rows": (_int, [_vp, _i64, _int, _vp, _vp, _i64, _i64, _vp, _vp, _sz, _vp]),
     "kmc_finish": (_int, [_vp, _int, _int, _vp, _i64, _int, _vp, _vp, _vp, _sz, _vp]),
     "kmc_stats_read": (_int, [_vp, _vp, _vp]),

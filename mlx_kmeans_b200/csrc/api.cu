@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/kmc.h"
@@ -244,6 +245,47 @@ int kmc_standardize(float* X, int64_t n, int d, const int64_t* sums, const uint3
                                        static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "kmc_standardize");
     return KMC_OK;
+}
+
+
+// ---------------------------------------------------------------- kmc_pass_static
+// The pass with its scratch in a file-scope device array instead of a caller buffer, for callers that
+// cannot allocate device memory.  Every GPU that loads the library holds one copy (KMC_STATIC_SCRATCH_BYTES)
+// until the process exits.  Host code cannot hand the array's name to a kernel (on the host it is only a
+// stand-in symbol), so each device's address is looked up once with cudaGetSymbolAddress, with that device
+// current, and cached.
+static __device__ __align__(256) unsigned char g_static_scratch[KMC_STATIC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_static_mu;
+void* g_static_addr[256] = {};
+}  // namespace
+
+int kmc_pass_static(const float* X, int64_t n, int d, const float* C, int k, const uint32_t* colmax, int64_t n_total,
+                    int64_t* totals, int32_t* labels, float* best, unsigned flags, void* stream) {
+    if (int s = check_shape(n, d, k)) return s;
+    const size_t need = carve(nullptr, d, k).bytes;
+    if (need > (size_t)KMC_STATIC_SCRATCH_BYTES)
+        return fail(KMC_ERR_UNSUPPORTED,
+                    "kmc_pass_static: d=%d, k=%d need %zu bytes of scratch, above the fixed %d bytes; "
+                    "use kmc_pass with a caller workspace", d, k, need, (int)KMC_STATIC_SCRATCH_BYTES);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_pass_static: cudaGetDevice");
+    if (dev < 0 || dev >= 256) return fail(KMC_ERR_UNSUPPORTED, "kmc_pass_static: device ordinal %d", dev);
+    void* ws = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_static_mu);
+        if (!g_static_addr[dev]) {
+            void* p = nullptr;
+            e = cudaGetSymbolAddress(&p, g_static_scratch);
+            if (e != cudaSuccess || p == nullptr) return cuda_fail(e, "kmc_pass_static: cudaGetSymbolAddress");
+            g_static_addr[dev] = p;
+        }
+        ws = g_static_addr[dev];
+    }
+    return kmc_pass(X, n, d, C, k, colmax, n_total, totals, labels, best, flags, ws, (size_t)KMC_STATIC_SCRATCH_BYTES,
+                    stream);
 }
 
 }  // extern "C"
