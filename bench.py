@@ -136,6 +136,8 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    from threadpoolctl import threadpool_limits
+    threadpool_limits(os.cpu_count())          # torchrun sets OMP_NUM_THREADS=1; the baseline uses every core
     from mlx_kmeans_b200.data import CONFIGS, DESCRIPTION, host_sample
     from oracle.assign_numpy_port import cpu_lloyd_pass
     cfg = args.config
