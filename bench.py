@@ -48,6 +48,7 @@ def parse():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--generic", action="store_true", help="force the any-shape kernel (diagnostic)")
+    p.add_argument("--no-bounds", action="store_true", help="compare every row with every center each pass")
     return p.parse_args()
 
 
@@ -221,7 +222,7 @@ def main():
 
     # warm-up: full Lloyd steps (relocation handled)
     for _ in range(max(args.warmup, 3)):
-        C_new, s = ds.step(C, generic=args.generic)
+        C_new, s = ds.step(C, generic=args.generic, bounded=not args.no_bounds)
         C = C_new.clone()
 
     L = _lib.load()
@@ -232,6 +233,9 @@ def main():
     K = args.steps
     stats = torch.zeros((K, _lib.STATS_BYTES), dtype=torch.uint8, device=dev)
     Cs = [C.clone(), torch.empty_like(C)]
+    # per-row bounds carried over from the warm-up steps (the fit's own state)
+    bounded = not args.no_bounds and not args.generic
+    bb, bbytes = ds.bounds(k)[0] if bounded else (None, 0)
     flags = _lib.KMC_PASS_GENERIC if args.generic else 0
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -247,8 +251,13 @@ def main():
     for i in range(K):
         Cin, Cout = Cs[i % 2], Cs[(i + 1) % 2]
         ev[i][0].record(st)
-        _lib.check(L.kmc_pass(X.data_ptr(), X.shape[0], d, Cin.data_ptr(), k, cm.data_ptr(), n_total,
-                              b["totals"].data_ptr(), None, None, flags, b["ws"].data_ptr(), b["wsb"], sp))
+        if bounded:
+            _lib.check(L.kmc_pass_bounded(X.data_ptr(), X.shape[0], d, Cin.data_ptr(), k, cm.data_ptr(), n_total,
+                                          b["totals"].data_ptr(), flags, bb.data_ptr(), bbytes, b["ws"].data_ptr(),
+                                          b["wsb"], sp))
+        else:
+            _lib.check(L.kmc_pass(X.data_ptr(), X.shape[0], d, Cin.data_ptr(), k, cm.data_ptr(), n_total,
+                                  b["totals"].data_ptr(), None, None, flags, b["ws"].data_ptr(), b["wsb"], sp))
         ev[i][1].record(st)
         if world > 1:
             dist.all_reduce(b["totals"], op=dist.ReduceOp.SUM, group=group)
@@ -264,6 +273,7 @@ def main():
     st_host = stats.cpu().numpy().view(np.int64).reshape(K, 8)
     reloc_steps = int((st_host[:, 3] != 0).sum())
     rescored = float(st_host[:, 5].mean())
+    screened = float(st_host[:, 6].mean()) / max(1, hi - lo)
     if world > 1:
         t = torch.tensor([total_ms, pass_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
@@ -322,6 +332,8 @@ def main():
                    "l2": "inputs larger than L2 (%.2f GB per GPU), no flush" % (bytes_per_launch / 1e9),
                    "relocation_steps_in_timed_region": reloc_steps,
                    "rows_rescored_in_float64_per_pass": rescored,
+                   "per_row_bounds": bounded,
+                   "fraction_of_rows_compared_with_every_center": screened if bounded else 1.0,
                    "kernel": "generic" if args.generic else "auto"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / pk["hbm_gbs"], "traffic": traffic,

@@ -51,7 +51,8 @@ typedef struct kmc_stats {
     int64_t needs_reloc;   /* 1: clusters emptied and no candidate rows were given; C_new not written */
     int64_t flags;         /* 1 = non-finite data, centers or distance */
     int64_t rescored;      /* rows whose label was decided in float64 (diagnostic) */
-    int64_t reserved[2];
+    int64_t screened;      /* rows compared with every center (bounded passes: those whose bound failed) */
+    int64_t reserved;
 } kmc_stats;
 
 /* ---------------------------------------------------------------- library */
@@ -93,6 +94,22 @@ int kmc_colmax(const float *X, int64_t n, int d, uint32_t *colmax, unsigned flag
 int kmc_pass(const float *X, int64_t n, int d, const float *C, int k, const uint32_t *colmax, int64_t n_total,
              int64_t *totals, int32_t *labels, float *best, unsigned flags, void *workspace, size_t ws_bytes,
              void *stream);
+
+/* Per-row bounds between Lloyd passes (the reference keeps per-centre bounds for high d, core.py:1690-2015;
+ * here: Hamerly-style, one 32-bit word per row for the fused low-d kernel).  A caller buffer of
+ * kmc_bounds_bytes(n, d, k) bytes per slice holds the drift of the centers, the centers of the last pass and
+ * one word per row: a lower bound on the row's distance to every center but its label, with the label in its
+ * low bits.  kmc_pass_bounded is kmc_pass (same totals, same labels) that reads and refreshes these words:
+ * a row whose distance to its stored label is below its bound less the centers' drift since keeps its label
+ * without being compared to the other centers.  The first pass after kmc_bounds_reset (or on a zeroed buffer)
+ * compares every row and writes all words.  Centers may change arbitrarily between passes: the drift is
+ * measured from the centers themselves.  Shapes outside the fused kernel (d > 8 or k above its limit) run
+ * the plain pass and leave the buffer untouched.  No labels/best outputs (use kmc_pass for those). */
+size_t kmc_bounds_bytes(int64_t n, int d, int k);
+int kmc_bounds_reset(void *bounds, void *stream);
+int kmc_pass_bounded(const float *X, int64_t n, int d, const float *C, int k, const uint32_t *colmax,
+                     int64_t n_total, int64_t *totals, unsigned flags, void *bounds, size_t bounds_size,
+                     void *workspace, size_t ws_bytes, void *stream);
 
 /* kmc_pass without a caller workspace.  No counterpart in the reference: it exists for callers that cannot
  * allocate device memory -- a host runtime that owns every device allocation through its own pool, or a

@@ -111,6 +111,7 @@ class Dataset:
             self.rank, self.world, self.row0, self.n_total = 0, 1, 0, self.n_local
         self._ws = {}
         self._colmax = None
+        self._bounds = {}
 
     # -- per-dataset state
     @property
@@ -157,19 +158,43 @@ class Dataset:
             b["best"] = [torch.empty(p.shape[0], dtype=torch.float32, device=self.device) for p in self.parts]
         return b["labels"], b["best"]
 
+    # -- per-row bounds kept between passes (kmc_pass_bounded), one buffer per slice and k
+    def bounds(self, k):
+        bb = self._bounds.get(k)
+        if bb is None:
+            L = _lib.load()
+            bb = []
+            for p in self.parts:
+                nb = int(L.kmc_bounds_bytes(p.shape[0], self.d, k))
+                bb.append((torch.zeros(nb, dtype=torch.uint8, device=self.device), nb))
+            self._bounds[k] = bb
+        return bb
+
+    def reset_bounds(self):
+        """Forget the per-row bounds: the next bounded pass compares every row with every center."""
+        for bb in self._bounds.values():
+            for t, _ in bb:
+                _lib.call("kmc_bounds_reset", _ptr(t), _stream())
+
     # -- one pass
-    def run_pass(self, C, labels=False, generic=False):
-        """kmc_pass over every local slice, then the all-reduce of the totals. C: (k, d) float32 CUDA."""
+    def run_pass(self, C, labels=False, generic=False, bounded=False):
+        """kmc_pass over every local slice, then the all-reduce of the totals. C: (k, d) float32 CUDA.
+        bounded: use and refresh the per-row bounds (kmc_pass_bounded; no labels)."""
         k = C.shape[0]
         b = self.buffers(k)
         lab, bst = self._label_buffers(b) if labels else (None, None)
         cm = self.colmax
         flags = _lib.KMC_PASS_GENERIC if generic else 0
         st = _stream()
+        bb = self.bounds(k) if bounded and not labels and not generic else None
         for i, p in enumerate(self.parts):
-            _lib.call("kmc_pass", _ptr(p), p.shape[0], self.d, _ptr(C), k, _ptr(cm), self.n_total,
-                      _ptr(b["totals"]), _ptr(lab[i]) if labels else None, _ptr(bst[i]) if labels else None,
-                      flags, _ptr(b["ws"]), b["wsb"], st)
+            if bb is not None:
+                _lib.call("kmc_pass_bounded", _ptr(p), p.shape[0], self.d, _ptr(C), k, _ptr(cm), self.n_total,
+                          _ptr(b["totals"]), flags, _ptr(bb[i][0]), bb[i][1], _ptr(b["ws"]), b["wsb"], st)
+            else:
+                _lib.call("kmc_pass", _ptr(p), p.shape[0], self.d, _ptr(C), k, _ptr(cm), self.n_total,
+                          _ptr(b["totals"]), _ptr(lab[i]) if labels else None, _ptr(bst[i]) if labels else None,
+                          flags, _ptr(b["ws"]), b["wsb"], st)
             flags |= _lib.KMC_PASS_ACCUMULATE
         if self.group is not None:
             import torch.distributed as dist
@@ -180,13 +205,15 @@ class Dataset:
         host = np.zeros(8, dtype=np.int64)
         _lib.call("kmc_stats_read", _ptr(b["stats"]), host.ctypes.data, _stream())
         return dict(inertia=float(host[:1].view(np.float64)[0]), n_empty=int(host[1]), n_relocated=int(host[2]),
-                    needs_reloc=int(host[3]), flags=int(host[4]), rescored=int(host[5]))
+                    needs_reloc=int(host[3]), flags=int(host[4]), rescored=int(host[5]), screened=int(host[6]))
 
-    def step(self, C, generic=False):
+    def step(self, C, generic=False, bounded=True):
         """One Lloyd iteration on the device: C (k, d) CUDA -> (C_new CUDA tensor (a buffer reused by the
-        next step with the same k; copy it to keep it), stats dict)."""
+        next step with the same k; copy it to keep it), stats dict).  bounded: keep per-row bounds between
+        steps so rows whose label cannot have changed skip the comparison with every center (the labels are
+        those of a full pass; the totals agree to the float32 rounding of the per-lane partial sums)."""
         k = C.shape[0]
-        b = self.run_pass(C, generic=generic)
+        b = self.run_pass(C, generic=generic, bounded=bounded)
         _lib.call("kmc_finish", _ptr(b["totals"]), k, self.d, None, 0, 1, _ptr(b["C_new"]), _ptr(b["stats"]),
                   _ptr(b["ws"]), b["wsb"], _stream())
         s = self.read_stats(b)

@@ -79,6 +79,20 @@ FarWorkspace carve_far(void* base, int64_t cand_rows) {
     return w;
 }
 
+BoundsState carve_bounds(void* base, int64_t n, int d, int k) {
+    BoundsState b;
+    char* p = static_cast<char*>(base);
+    b.meta = reinterpret_cast<double*>(p);
+    b.cprev = reinterpret_cast<float*>(p + 256);
+    b.rows = reinterpret_cast<uint32_t*>(p + 256 + a256(sizeof(float) * (size_t)k * d));
+    (void)n;
+    return b;
+}
+
+size_t bounds_bytes(int64_t n, int d, int k) {
+    return 256 + a256(sizeof(float) * (size_t)k * d) + a256(sizeof(uint32_t) * (size_t)(n > 0 ? n : 1));
+}
+
 }  // namespace kmc
 
 using namespace kmc;
@@ -111,25 +125,29 @@ int kmc_colmax(const float* X, int64_t n, int d, uint32_t* colmax, unsigned flag
     return KMC_OK;
 }
 
-int kmc_pass(const float* X, int64_t n, int d, const float* C, int k, const uint32_t* colmax, int64_t n_total,
-             int64_t* totals, int32_t* labels, float* best, unsigned flags, void* workspace, size_t ws_bytes,
-             void* stream) {
+}  // extern "C"
+
+namespace {
+// kmc_pass and kmc_pass_bounded: bounds == nullptr for a plain pass
+int pass_impl(const char* who, const float* X, int64_t n, int d, const float* C, int k, const uint32_t* colmax,
+              int64_t n_total, int64_t* totals, int32_t* labels, float* best, unsigned flags, void* workspace,
+              size_t ws_bytes, void* bounds, void* stream) {
     if (int s = check_shape(n, d, k)) return s;
     if (!C || !colmax || !totals || !workspace || (n > 0 && !X))
-        return fail(KMC_ERR_INVALID, "kmc_pass: null pointer");
-    if (n_total < n) return fail(KMC_ERR_INVALID, "kmc_pass: n_total %lld < n %lld", (long long)n_total, (long long)n);
+        return fail(KMC_ERR_INVALID, "%s: null pointer", who);
+    if (n_total < n) return fail(KMC_ERR_INVALID, "%s: n_total %lld < n %lld", who, (long long)n_total, (long long)n);
     Workspace ws = carve(workspace, d, k);
-    if (ws_bytes < ws.bytes) return fail(KMC_ERR_INVALID, "kmc_pass: workspace of %zu bytes, need %zu", ws_bytes, ws.bytes);
+    if (ws_bytes < ws.bytes) return fail(KMC_ERR_INVALID, "%s: workspace of %zu bytes, need %zu", who, ws_bytes, ws.bytes);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e;
     if (!(flags & KMC_PASS_ACCUMULATE)) {
         e = cudaMemsetAsync(totals, 0, sizeof(int64_t) * (size_t)k * (d + 2), st);
-        if (e != cudaSuccess) return cuda_fail(e, "kmc_pass: clear totals");
+        if (e != cudaSuccess) return cuda_fail(e, who);
         e = cudaMemsetAsync(ws.counters, 0, sizeof(long long) * 8, st);
-        if (e != cudaSuccess) return cuda_fail(e, "kmc_pass: clear counters");
+        if (e != cudaSuccess) return cuda_fail(e, who);
     }
     e = launch_prepare(C, k, d, colmax, n_total, ws.prep, ws.scale_x, ws.hc, st);
-    if (e != cudaSuccess) return cuda_fail(e, "kmc_pass: prepare");
+    if (e != cudaSuccess) return cuda_fail(e, who);
     if (n == 0) return KMC_OK;
     PassArgs a;
     a.X = X;
@@ -147,11 +165,52 @@ int kmc_pass(const float* X, int64_t n, int d, const float* C, int k, const uint
     a.smem_acc = 0;
     a.ctile = 0;
     a.key_keep = 0;
+    a.brows = nullptr;
+    const bool fused = !(flags & KMC_PASS_GENERIC) && lowd_supports(d, k);
+    if (bounds && fused) {
+        BoundsState b = carve_bounds(bounds, n, d, k);
+        e = launch_bounds_prepare(C, k, d, b.meta, b.cprev, ws.prep, st);
+        if (e != cudaSuccess) return cuda_fail(e, who);
+        a.brows = b.rows;
+        a.labels = nullptr;
+        a.best = nullptr;
+    }
     e = cudaErrorNotSupported;
-    if (!(flags & KMC_PASS_GENERIC)) e = launch_pass_lowd(a, st);
+    if (fused) e = launch_pass_lowd(a, st);
     if (e == cudaErrorNotSupported) e = launch_pass_generic(a, st);
-    if (e != cudaSuccess) return cuda_fail(e, "kmc_pass");
+    if (e != cudaSuccess) return cuda_fail(e, who);
     return KMC_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int kmc_pass(const float* X, int64_t n, int d, const float* C, int k, const uint32_t* colmax, int64_t n_total,
+             int64_t* totals, int32_t* labels, float* best, unsigned flags, void* workspace, size_t ws_bytes,
+             void* stream) {
+    return pass_impl("kmc_pass", X, n, d, C, k, colmax, n_total, totals, labels, best, flags, workspace, ws_bytes,
+                     nullptr, stream);
+}
+
+size_t kmc_bounds_bytes(int64_t n, int d, int k) { return bounds_bytes(n, d, k); }
+
+int kmc_bounds_reset(void* bounds, void* stream) {
+    if (!bounds) return fail(KMC_ERR_INVALID, "kmc_bounds_reset: null pointer");
+    cudaError_t e = cudaMemsetAsync(bounds, 0, 16, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_bounds_reset");
+    return KMC_OK;
+}
+
+int kmc_pass_bounded(const float* X, int64_t n, int d, const float* C, int k, const uint32_t* colmax,
+                     int64_t n_total, int64_t* totals, unsigned flags, void* bounds, size_t bounds_size,
+                     void* workspace, size_t ws_bytes, void* stream) {
+    if (int s = check_shape(n, d, k)) return s;
+    if (!bounds) return fail(KMC_ERR_INVALID, "kmc_pass_bounded: null bounds");
+    if (bounds_size < bounds_bytes(n, d, k))
+        return fail(KMC_ERR_INVALID, "kmc_pass_bounded: bounds of %zu bytes, need %zu", bounds_size,
+                    bounds_bytes(n, d, k));
+    return pass_impl("kmc_pass_bounded", X, n, d, C, k, colmax, n_total, totals, nullptr, nullptr, flags, workspace,
+                     ws_bytes, bounds, stream);
 }
 
 int kmc_far_rows(const float* X, int64_t n, int d, const int32_t* labels, const float* best, int64_t row0,

@@ -29,6 +29,8 @@ struct Prep {
     float win_abs;
     int si;
     int flags;              // kFlag* below
+    int bvalid;             // bounded passes: the per-row bounds were written by an earlier pass
+    float bcum_lo, bcum_up; // bounded passes: total center drift so far, rounded down / up
     int pad;
 };
 
@@ -44,7 +46,8 @@ struct Stats {
     int64_t needs_reloc;    // 1: empties exist and the finish had no candidate rows -> centers not written
     int64_t flags;          // kFlag*
     int64_t rescored;       // rows re-scored in float64 by the pass kernels (diagnostic)
-    int64_t pad[2];
+    int64_t screened;       // rows compared with every center (bounded passes: the rows whose bound failed)
+    int64_t pad;
 };
 
 // ---------------------------------------------------------------- fixed point

@@ -223,7 +223,8 @@ __global__ void __launch_bounds__(1024) k_finish(FinishArgs a) {
             s.needs_reloc = 1;
             s.flags = (long long)a.prep->flags | a.counters[1];
             s.rescored = a.counters[0];
-            s.pad[0] = s.pad[1] = 0;
+            s.screened = a.counters[2];
+            s.pad = 0;
             *a.stats = s;
         }
         return;
@@ -279,7 +280,8 @@ __global__ void __launch_bounds__(1024) k_finish(FinishArgs a) {
         s.needs_reloc = 0;
         s.flags = (long long)a.prep->flags | a.counters[1];
         s.rescored = a.counters[0];
-        s.pad[0] = s.pad[1] = 0;
+        s.screened = a.counters[2];
+        s.pad = 0;
         *a.stats = s;
     }
 }

@@ -26,7 +26,18 @@ struct PassArgs {
     int smem_acc;             // generic kernel: accumulate in shared memory
     int ctile;                // generic kernel: centers per shared tile
     unsigned key_keep;        // fused low-d kernel: ~(center index bits) of a key
+    uint32_t* brows;          // bounded pass: one bound word per row (nullptr: plain pass)
 };
+
+// Bounds state of one slice (caller memory): [meta: double drift, int64 valid][centers of the last pass].
+struct BoundsState {
+    double* meta;
+    float* cprev;             // k x d
+    uint32_t* rows;           // n
+};
+BoundsState carve_bounds(void* base, int64_t n, int d, int k);
+size_t bounds_bytes(int64_t n, int d, int k);
+bool lowd_supports(int d, int k);
 
 // Pass workspace carve-up (256-byte aligned pieces): kmc_pass writes prep/scale_x/hc/counters,
 // kmc_finish and kmc_totals_unpack read them.
@@ -54,6 +65,8 @@ cudaError_t launch_colmax(const float* X, int64_t n, int d, unsigned int* colmax
 cudaError_t launch_prepare(const float* C, int k, int d, const unsigned int* colmax, int64_t n_total, Prep* prep,
                            double* scale_x, float* hc, cudaStream_t st);
 cudaError_t launch_pass_generic(PassArgs a, cudaStream_t st);
+cudaError_t launch_bounds_prepare(const float* C, int k, int d, double* meta, float* cprev, Prep* prep,
+                                  cudaStream_t st);
 // Specialised low-dimensional fused pass; returns cudaErrorNotSupported when (d, k) has no instance.
 cudaError_t launch_pass_lowd(PassArgs a, cudaStream_t st);
 int64_t lowd_block_rows();

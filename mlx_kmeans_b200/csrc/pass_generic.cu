@@ -89,6 +89,9 @@ __global__ void k_prepare(const float* __restrict__ C, int k, int d, const unsig
         p.win_coef = (float)(4.0 * (d + 2) / 16777216.0 + (double)d / 281474976710656.0);
         p.win_abs = (float)((d + 2) * 7.174648137343064e-43);               // (d+2) 2^-140
         p.flags = (s_bad || bound > 3.0e38) ? kFlagNonFinite : 0;
+        p.bvalid = 0;
+        p.bcum_lo = 0.0f;
+        p.bcum_up = 0.0f;
         p.pad = 0;
         *prep = p;
     }
@@ -202,6 +205,48 @@ cudaError_t launch_colmax(const float* X, int64_t n, int d, unsigned int* colmax
 cudaError_t launch_prepare(const float* C, int k, int d, const unsigned int* colmax, int64_t n_total, Prep* prep,
                            double* scale_x, float* hc, cudaStream_t st) {
     k_prepare<<<1, 1024, 0, st>>>(C, k, d, colmax, n_total, prep, scale_x, hc);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- per-row bounds: drift of the centers
+// One CTA, after k_prepare.  The drift of center c is |c - c_prev| (float64, rounded up); the bounds lose
+// max_c drift per pass (Hamerly: the distance to any other center shrinks by at most its move).  The running
+// total goes to the pass as float32 bounds on both sides; the current centers become c_prev.  When the bounds
+// are not valid yet the pass writes them all, so they are valid afterwards with zero drift.
+__global__ void k_bounds_prepare(const float* __restrict__ C, int k, int d, double* __restrict__ meta,
+                                 float* __restrict__ cprev, Prep* __restrict__ prep) {
+    __shared__ double s_max[32];
+    const bool valid = meta[1] != 0.0;
+    double mx = 0.0;
+    if (valid) {
+        for (int c = threadIdx.x; c < k; c += blockDim.x) {
+            double s = 0.0;
+            for (int j = 0; j < d; j++) {
+                double q = (double)C[(int64_t)c * d + j] - (double)cprev[(int64_t)c * d + j];
+                s = __fma_ru(q, q, s);
+            }
+            mx = fmax(mx, __dsqrt_ru(s));
+        }
+    }
+    for (int o = 16; o; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) mx = fmax(mx, s_max[w]);
+        const double cum = valid ? __dadd_ru(meta[0], mx) : 0.0;
+        prep->bvalid = valid ? 1 : 0;
+        prep->bcum_lo = __double2float_rd(cum);
+        prep->bcum_up = __double2float_ru(cum);
+        meta[0] = cum;
+        meta[1] = 1.0;
+    }
+    __syncthreads();
+    for (int64_t e = threadIdx.x; e < (int64_t)k * d; e += blockDim.x) cprev[e] = C[e];
+}
+
+cudaError_t launch_bounds_prepare(const float* C, int k, int d, double* meta, float* cprev, Prep* prep,
+                                  cudaStream_t st) {
+    k_bounds_prepare<<<1, 1024, 0, st>>>(C, k, d, meta, cprev, prep);
     return cudaGetLastError();
 }
 

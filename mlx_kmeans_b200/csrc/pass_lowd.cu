@@ -210,25 +210,31 @@ __device__ __noinline__ int rescore_rows(unsigned fm, RowVec<D> x, const float* 
 
 }  // namespace
 
-template <int D, int K>
+template <int D, int K, bool BND>
 struct LowdSmem {
     static constexpr int kSums = K * D * 32;                       // floats per warp
     static constexpr int kCnts = ((K + 3) / 4) * 32;               // packed 8-bit counts per warp (words)
+    static constexpr int kQueue = 64;                              // queued rows per warp (power of two)
     static constexpr size_t ring = (size_t)kStages * kThreads * D * 4;
     static constexpr size_t sums = (size_t)kWarps * kSums * 4;
     static constexpr size_t cnts = (size_t)kWarps * kCnts * 4;
     static constexpr size_t fold = (size_t)kWarps * K * (D + 1) * 8;
     static constexpr size_t centers = (size_t)32 * D * 4;
     static constexpr size_t acc = (size_t)K * (D + 2) * 8;
-    static constexpr size_t total = ring + sums + cnts + fold + centers + acc;
+    static constexpr size_t wring = BND ? (size_t)kStages * kThreads * 4 : 0;
+    static constexpr size_t queue = BND ? (size_t)kWarps * kQueue * 4 : 0;
+    static constexpr size_t total = ring + sums + cnts + fold + centers + acc + wring + queue;
 };
 
 // Per-thread state of the row loop.
 template <int D, int K>
 struct LowdRow {
+    static constexpr unsigned IDXBITS = idx_bits(K);
+    static constexpr unsigned MASK = (1u << IDXBITS) - 1u;
     unsigned long long cp2[K / 2][D];   // -c, two centers per register pair
     unsigned long long hp2[K / 2];      // |c|^2 / 2
     float coef, slack, cmax2, wabs;
+    float cum_lo, cum_up;               // drift of the centers since the bounds were started (bounds mode)
     unsigned keep;                      // ~(index mask), a launch argument so it stays in a register
     const float* cs;                    // shared copy of the centers (zero padded to 32 rows)
     unsigned cs_s;                      // its shared-window address
@@ -237,8 +243,15 @@ struct LowdRow {
     unsigned sums_s, cnts_s;            // their shared-window addresses
     int lane, k;
     double inert;
-    long long rescored;
+    float ichunk;
+    long long rescored, screened;
     int bad;
+
+    struct Scr {
+        int l;          // label
+        float m2, x2;   // second smallest key, |x|^2
+        bool exact;     // decided in float64
+    };
 
     // keys of centers 2P and 2P+1: one packed distance chain, then one lop3 each inserting the index
     template <int P>
@@ -257,12 +270,8 @@ struct LowdRow {
         (pair<P>(xx, xh2, t1, t2), ...);
     }
 
-    template <bool CHECK, bool OUT>
-    __device__ __forceinline__ void row(const float (&x)[D], int64_t row, int64_t n, int32_t* labels, float* best) {
-        constexpr unsigned IDXBITS = K <= 2 ? 1 : K <= 4 ? 2 : K <= 8 ? 3 : K <= 16 ? 4 : 5;
-        constexpr unsigned MASK = (1u << IDXBITS) - 1u;
-        const bool valid = !CHECK || row < n;
-        // ---- screen
+    // Nearest center of x over all k centers.  Warp-collective (every lane calls it; `valid` marks real rows).
+    __device__ __forceinline__ Scr screen(const float (&x)[D], bool valid) {
         unsigned long long xx[D];
         float x2 = 0.0f;
 #pragma unroll
@@ -286,25 +295,30 @@ struct LowdRow {
             }
         }
         const float m1 = t1[0], m2 = t2[0];
-        int l = (int)(__float_as_uint(m1) & MASK);
+        Scr s;
+        s.l = (int)(__float_as_uint(m1) & MASK);
+        s.m2 = m2;
+        s.x2 = x2;
         const float win = __fmaf_rn(coef, x2 + cmax2, wabs) + slack * (fabsf(m1) + fabsf(m2));
         const bool flag = valid && !(m2 - m1 > win);
-
-        // ---- rows inside the window: float64, one center per lane, lowest index on ties
+        s.exact = flag;
+        // rows inside the window: float64, one center per lane, lowest index on ties
         unsigned fm = __ballot_sync(0xffffffffu, flag);
         if (fm) {
             rescored += flag ? 1 : 0;
             RowVec<D> xv;
 #pragma unroll
             for (int j = 0; j < D; j++) xv.v[j] = x[j];
-            l = rescore_rows<D>(fm, xv, cs, k, lane, l);
+            s.l = rescore_rows<D>(fm, xv, cs, k, lane, s.l);
         }
-        if (!valid) return;
+        return s;
+    }
 
-        // ---- residual t = x - c_l and best = sum t^2 (each op rounded on its own, in column order)
+    // residual t = x - c_l and best = sum t^2 (each op rounded on its own, in column order)
+    __device__ __forceinline__ float residual(const float (&x)[D], int l, float (&t)[D]) {
         float c[D];
         load_row<D>(c, cs_s + (unsigned)(l * D * 4));
-        float t[D], q[D];
+        float q[D];
         if constexpr (D % 2 == 0) {
 #pragma unroll
             for (int j = 0; j < D; j += 2) {
@@ -323,13 +337,40 @@ struct LowdRow {
         float b = q[0];                    // 0 + q0 == q0 exactly
 #pragma unroll
         for (int j = 1; j < D; j++) b = __fadd_rn(b, q[j]);
-        // this lane's slot of cluster l (plain read-modify-write: nobody else touches it)
+        return b;
+    }
+
+    // this lane's slot of cluster l (plain read-modify-write: nobody else touches it)
+    __device__ __forceinline__ void accumulate(int l, const float (&t)[D], float b) {
         add_row<D>(sums_s + (unsigned)((l * 32 + lane) * D * 4), t);
         add_u32(cnts_s + (unsigned)(((l >> 2) * 32 + lane) * 4), 1u << ((l & 3) * 8));
         ichunk = __fadd_rn(ichunk, b);     // float32 over at most kStages rows, then float64
+    }
+
+    // Bound word of a screened row: a lower bound on its distance to every center but its label, plus the
+    // drift so far, rounded down, with the label in the low mantissa bits.  Keys of the other centers are at
+    // least m2 less the index bits' share; the float32 error of a half distance is at most half of
+    // coef (|x|^2 + max|c|^2).  A row decided in float64 gets no bound (0).
+    __device__ __forceinline__ unsigned bound_word(const Scr& s) {
+        float h = s.m2 - slack * fabsf(s.m2) - coef * (s.x2 + cmax2);
+        float lb = (h > 0.0f && !s.exact) ? __fsqrt_rn(2.0f * h) : 0.0f;
+        float adj = __fmul_rn(__fadd_rn(lb, cum_lo), 1.0f - 1.0f / (float)(1u << (20 - IDXBITS)));
+        return (__float_as_uint(adj) & keep) | (unsigned)s.l;
+    }
+
+    // plain row: screen, residual, totals (and optionally the bound word, labels, best)
+    template <bool CHECK, bool OUT, bool BW>
+    __device__ __forceinline__ void row(const float (&x)[D], int64_t row, int64_t n, const PassArgs& a) {
+        const bool valid = !CHECK || row < n;
+        const Scr s = screen(x, valid);
+        if (!valid) return;
+        float t[D];
+        const float b = residual(x, s.l, t);
+        accumulate(s.l, t, b);
+        if (BW) a.brows[row] = bound_word(s);
         if (OUT) {
-            if (labels) labels[row] = l;
-            if (best) best[row] = b;
+            if (a.labels) a.labels[row] = s.l;
+            if (a.best) a.best[row] = b;
         }
     }
 
@@ -338,20 +379,24 @@ struct LowdRow {
         inert = __dadd_rn(inert, (double)ichunk);
         ichunk = 0.0f;
     }
-    float ichunk;
 };
 
 #ifndef KMC_LOWD_MIN_BLOCKS
 #define KMC_LOWD_MIN_BLOCKS 4
 #endif
 
-template <int D, int K, bool OUT>
+// BND: the pass keeps per-row bounds (a.brows, one word per row; a.bmeta holds validity and drift).  On the
+// first pass (bounds not valid yet) every row is screened and its word written; afterwards a row whose
+// distance to its stored label is below its stored bound less the drift keeps its label without a screen,
+// and the others queue per warp and are screened 32 at a time (one per lane) so the warp does not diverge.
+template <int D, int K, bool OUT, bool BND>
 __global__ void __launch_bounds__(kThreads, KMC_LOWD_MIN_BLOCKS) k_pass_lowd(PassArgs a) {
     static_assert(K % 2 == 0 && K <= 32, "K even, at most 32");
     constexpr int CPB = (D % 4 == 0) ? 16 : ((D % 2 == 0) ? 8 : 4);   // bytes per cp.async
     constexpr int NCP = D * 4 / CPB;
-    constexpr unsigned IDXBITS = K <= 2 ? 1 : K <= 4 ? 2 : K <= 8 ? 3 : K <= 16 ? 4 : 5;
-    using L = LowdSmem<D, K>;
+    constexpr unsigned IDXBITS = idx_bits(K);
+    constexpr unsigned MASK = (1u << IDXBITS) - 1u;
+    using L = LowdSmem<D, K, BND>;
     extern __shared__ __align__(16) unsigned char smem[];
     float* ring = reinterpret_cast<float*>(smem);
     float* sums_all = reinterpret_cast<float*>(smem + L::ring);
@@ -359,6 +404,8 @@ __global__ void __launch_bounds__(kThreads, KMC_LOWD_MIN_BLOCKS) k_pass_lowd(Pas
     double* fold_all = reinterpret_cast<double*>(smem + L::ring + L::sums + L::cnts);
     float* cs = reinterpret_cast<float*>(smem + L::ring + L::sums + L::cnts + L::fold);
     long long* acc = reinterpret_cast<long long*>(smem + L::ring + L::sums + L::cnts + L::fold + L::centers);
+    unsigned* wring = reinterpret_cast<unsigned*>(smem + L::ring + L::sums + L::cnts + L::fold + L::centers + L::acc);
+    int* queue_all = reinterpret_cast<int*>(smem + L::ring + L::sums + L::cnts + L::fold + L::centers + L::acc + L::wring);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int k = a.k;
@@ -381,7 +428,6 @@ __global__ void __launch_bounds__(kThreads, KMC_LOWD_MIN_BLOCKS) k_pass_lowd(Pas
         for (int j = 0; j < D; j++) st.cp2[p][j] = pack2(-cs[c0 * D + j], -cs[c1 * D + j]);
     }
     const Prep prep = *a.prep;
-    // both keys' index bits move them by < 2^(IDXBITS-23) |key| <= 2^(IDXBITS-23) (|x|^2 + max|c|^2)
     // Window of the screen.  With u = 2^-24 and g = D u / (1 - D u), the computed half distance of every
     // center is within (2 g + u / 2)(|x|^2 + |c|^2) of the exact one (|x|^2 and |c|^2 each carry g, the add
     // that joins them u, the fma chain g on |x|^2/2 + |c|^2/2 + |x||c|), so two centers within
@@ -394,6 +440,8 @@ __global__ void __launch_bounds__(kThreads, KMC_LOWD_MIN_BLOCKS) k_pass_lowd(Pas
     st.keep = a.key_keep;
     st.cmax2 = prep.cmax2;
     st.wabs = prep.win_abs;
+    st.cum_lo = prep.bcum_lo;
+    st.cum_up = prep.bcum_up;
     st.cs = cs;
     st.cs_s = (unsigned)__cvta_generic_to_shared(cs);
     st.sums = sums_all + (size_t)warp * L::kSums;
@@ -405,16 +453,20 @@ __global__ void __launch_bounds__(kThreads, KMC_LOWD_MIN_BLOCKS) k_pass_lowd(Pas
     st.inert = 0.0;
     st.ichunk = 0.0f;
     st.rescored = 0;
+    st.screened = 0;
     st.bad = 0;
+    // bounded steps only once the bounds exist (the first pass writes them)
+    const bool bounded = BND && prep.bvalid != 0;
 
     // Row of thread tid at step r of block b: b * kBlockRows + r * kThreads + tid.  Ring slot r % kStages
     // holds step r; the prefetch of step r + kStages - 1 is issued at step r into the slot read at step
     // r - 1, so this thread's reads of that slot have completed.  The prefetch walks a pointer (and, near
     // the end of the rows, a row index) kStages - 1 steps ahead of the reads, jumping to the CTA's next
-    // block when it leaves the current one.
+    // block when it leaves the current one.  Bounded passes stream the rows' bound words the same way.
     const int64_t nblk = (n + kBlockRows - 1) / kBlockRows;
     float* myring = ring + (size_t)tid * D;
     const unsigned myring_s = (unsigned)__cvta_generic_to_shared(myring);
+    unsigned* mywring = wring + tid;
     constexpr int SLOT = kThreads * D;
     constexpr int STEP = kThreads * D;                 // floats between a thread's consecutive rows
     const float* pf = a.X + ((int64_t)blockIdx.x * kBlockRows + tid) * D;
@@ -424,6 +476,7 @@ __global__ void __launch_bounds__(kThreads, KMC_LOWD_MIN_BLOCKS) k_pass_lowd(Pas
             float* dst = myring + slot * SLOT;
 #pragma unroll
             for (int q = 0; q < NCP; q++) cp_async<CPB>(dst + q * (CPB / 4), pf + q * (CPB / 4));
+            if (BND && bounded) cp_async<4>(mywring + slot * kThreads, a.brows + pf_row);
         }
         cp_commit();
         pf += STEP;
@@ -432,11 +485,37 @@ __global__ void __launch_bounds__(kThreads, KMC_LOWD_MIN_BLOCKS) k_pass_lowd(Pas
 #pragma unroll
     for (int s = 0; s < kStages - 1; s++) fetch(s, pf_row < n);
 
+    // per-warp queue of rows that failed their bound (offsets within the block), screened 32 at a time
+    int* queue = queue_all + warp * L::kQueue;
+    int qhead = 0, qcount = 0;
+
     for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
         const int64_t base = blk * kBlockRows + tid;
+        const int64_t blk0 = blk * kBlockRows;
         const int64_t next = (blk + gridDim.x) * kBlockRows + tid;
         // checks are needed only while this block or the prefetched part of the next one is ragged
         const bool clean = (blk + gridDim.x + 1) * kBlockRows <= n;
+
+        // screen `cnt` queued rows, one per lane
+        auto flush = [&](int cnt) {
+            const bool v = lane < cnt;
+            const int off = v ? queue[(qhead + lane) & (L::kQueue - 1)] : 0;
+            const int64_t row = blk0 + off;
+            float x[D];
+#pragma unroll
+            for (int j = 0; j < D; j++) x[j] = v ? __ldg(a.X + row * D + j) : 0.0f;
+            const auto s = st.screen(x, v);
+            if (v) {
+                float t[D];
+                const float b = st.residual(x, s.l, t);
+                st.accumulate(s.l, t, b);
+                a.brows[row] = st.bound_word(s);
+            }
+            st.screened += v ? 1 : 0;
+            qhead = (qhead + cnt) & (L::kQueue - 1);
+            qcount -= cnt;
+        };
+
         auto steps = [&](auto check) {
             constexpr bool CHECK = decltype(check)::value;
             for (int ch = 0; ch < kRowsPerLane / kStages; ch++) {
@@ -451,13 +530,44 @@ __global__ void __launch_bounds__(kThreads, KMC_LOWD_MIN_BLOCKS) k_pass_lowd(Pas
                     cp_wait<kStages - 1>();
                     float x[D];
                     load_row<D>(x, myring_s + (unsigned)(s * SLOT * 4));
-                    st.template row<CHECK, OUT>(x, base + (int64_t)r * kThreads, n, a.labels, a.best);
+                    const int64_t row = base + (int64_t)r * kThreads;
+                    if constexpr (BND) {
+                        if (bounded) {
+                            const bool valid = !CHECK || row < n;
+                            const unsigned w = mywring[s * kThreads];
+                            const int l = (int)(w & MASK);
+                            float t[D];
+                            const float b = st.residual(x, l, t);
+                            // stored bound less the drift since it was stored (both rounded against the row)
+                            const float lbn = __fmul_rn(__fsub_rn(__uint_as_float(w & st.keep), st.cum_up),
+                                                        1.0f - 1.0f / 4194304.0f);
+                            const bool keep_label = valid && lbn > 0.0f &&
+                                                    __fmul_rn(b, 1.0f + (float)(D + 4) / 8388608.0f) <
+                                                        __fmul_rn(__fmul_rn(lbn, lbn), 1.0f - 1.0f / 4194304.0f);
+                            if (keep_label) st.accumulate(l, t, b);
+                            const unsigned fm = __ballot_sync(0xffffffffu, valid && !keep_label);
+                            if (fm) {
+                                const int pos = __popc(fm & ((1u << lane) - 1u));
+                                if ((fm >> lane) & 1u)
+                                    queue[(qhead + qcount + pos) & (L::kQueue - 1)] = (int)(row - blk0);
+                                qcount += __popc(fm);
+                                if (qcount >= 32) flush(32);
+                            }
+                            continue;
+                        }
+                        st.template row<CHECK, OUT, true>(x, row, n, a);
+                        st.screened += (!CHECK || row < n) ? 1 : 0;
+                    } else {
+                        st.template row<CHECK, OUT, false>(x, row, n, a);
+                    }
                 }
                 st.chunk_done();
             }
         };
         if (clean) steps(std::integral_constant<bool, false>{});
         else steps(std::integral_constant<bool, true>{});
+        if (BND && qcount > 0) flush(qcount);
+        st.chunk_done();
 
         // ---- fold the lanes' slots into the CTA's int64 totals (fixed order => deterministic)
         __syncwarp();
@@ -515,29 +625,34 @@ __global__ void __launch_bounds__(kThreads, KMC_LOWD_MIN_BLOCKS) k_pass_lowd(Pas
         long long v = acc[e];
         if (v) atomicAdd(reinterpret_cast<unsigned long long*>(a.totals + e), (unsigned long long)v);
     }
-    long long rescored = st.rescored;
-    for (int o = 16; o; o >>= 1) rescored += __shfl_xor_sync(0xffffffffu, rescored, o);
+    long long rescored = st.rescored, screened = st.screened;
+    for (int o = 16; o; o >>= 1) {
+        rescored += __shfl_xor_sync(0xffffffffu, rescored, o);
+        screened += __shfl_xor_sync(0xffffffffu, screened, o);
+    }
     if (lane == 0 && rescored) atomicAdd(reinterpret_cast<unsigned long long*>(&a.counters[0]), (unsigned long long)rescored);
+    if (BND && lane == 0 && screened)
+        atomicAdd(reinterpret_cast<unsigned long long*>(&a.counters[2]), (unsigned long long)screened);
     if (st.bad) atomicOr(reinterpret_cast<unsigned long long*>(&a.counters[1]), (unsigned long long)kFlagNonFinite);
-    (void)IDXBITS;
 }
 
 namespace {
 
-template <int D, int K, bool OUT>
+template <int D, int K, bool OUT, bool BND>
 cudaError_t run(PassArgs a, cudaStream_t st) {
-    using L = LowdSmem<D, K>;
+    using L = LowdSmem<D, K, BND>;
     const size_t smem = L::total;
     static unsigned long long configured = 0;   // one bit per device: the attribute is per device
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(configured >> (dev & 63) & 1ull)) {
-        cudaError_t e = cudaFuncSetAttribute(k_pass_lowd<D, K, OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(k_pass_lowd<D, K, OUT, BND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
         if (e != cudaSuccess) return e;
         configured |= 1ull << (dev & 63);
     }
     int per_sm = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_pass_lowd<D, K, OUT>, kThreads, smem);
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_pass_lowd<D, K, OUT, BND>, kThreads, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorNotSupported;
     const int64_t nblk = (a.n + kBlockRows - 1) / kBlockRows;
@@ -545,13 +660,15 @@ cudaError_t run(PassArgs a, cudaStream_t st) {
     if (grid > nblk) grid = nblk;
     if (grid < 1) grid = 1;
     a.key_keep = ~((1u << idx_bits(K)) - 1u);
-    k_pass_lowd<D, K, OUT><<<(int)grid, kThreads, smem, st>>>(a);
+    k_pass_lowd<D, K, OUT, BND><<<(int)grid, kThreads, smem, st>>>(a);
     return cudaGetLastError();
 }
 
+// bounded passes write no labels; plain passes optionally do
 template <int D, int K>
 cudaError_t run_out(PassArgs a, cudaStream_t st) {
-    return (a.labels || a.best) ? run<D, K, true>(a, st) : run<D, K, false>(a, st);
+    if (a.brows) return run<D, K, false, true>(a, st);
+    return (a.labels || a.best) ? run<D, K, true, false>(a, st) : run<D, K, false, false>(a, st);
 }
 
 template <int D>
@@ -574,8 +691,10 @@ cudaError_t run_k(PassArgs a, cudaStream_t st) {
 
 int64_t lowd_block_rows() { return kBlockRows; }
 
+bool lowd_supports(int d, int k) { return d >= 1 && d <= 8 && k >= 1 && k <= (d <= 2 ? 32 : d <= 5 ? 16 : 8); }
+
 cudaError_t launch_pass_lowd(PassArgs a, cudaStream_t st) {
-    if (a.k > 32 || a.d > 8) return cudaErrorNotSupported;
+    if (!lowd_supports(a.d, a.k)) return cudaErrorNotSupported;
     switch (a.d) {
         case 1: return run_k<1>(a, st);
         case 2: return run_k<2>(a, st);

@@ -95,6 +95,7 @@ class KMeans:
         """estimator.py:132-150 with the centers kept on the device between steps."""
         rng = np.random.default_rng(seed)
         C = torch.from_numpy(core.kmeans_pp_init(ds, rows, self.n_clusters, rng)).to(ds.device)
+        ds.reset_bounds()                  # a restart: the previous run's per-row bounds say nothing useful
         if self.spherical:
             C = self._normalise(C)
         prev = None

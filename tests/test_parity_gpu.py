@@ -226,3 +226,73 @@ def test_window_rows_are_rescored(cuda_device):
     assert s["rescored"] > 50
     labels = ds.assign(C, return_labels=True)[3]
     assert np.array_equal(labels, g["labels"])
+
+
+# ---------------------------------------------------------------- per-row bounds (kmc_pass_bounded)
+
+def _word_labels(ds, k):
+    """Labels stored in the low bits of the bound words of a one-slice Dataset."""
+    from mlx_kmeans_b200 import _lib
+    buf, nbytes = ds.bounds(k)[0]
+    n, d = ds.parts[0].shape
+    off = nbytes - (((n * 4) + 255) // 256) * 256
+    words = buf[off:off + n * 4].view(torch_int32()).cpu().numpy().view(np.uint32)
+    kp = next(v for v in (2, 4, 8, 16, 32) if v >= k)
+    return (words & (kp - 1)).astype(np.int64)
+
+
+def torch_int32():
+    import torch
+    return torch.int32
+
+
+@pytest.mark.parametrize("cfg,n", [(3, 1_000_000), (1, 100_000)])
+def test_bounded_steps_match_full_steps(cfg, n, cuda_device):
+    """Lloyd steps with per-row bounds against full steps from the same start: identical counts, empties,
+    labels (read back from the bound words), inertia within 1e-7 relative and centers within 1e-7 of the data
+    RMS at every step."""
+    import mlx_kmeans_b200 as km
+    from mlx_kmeans_b200.data import CONFIGS, generate
+    torch = _torch()
+    X = generate(cfg, 0, n, cuda_device, rows_total=n)
+    k = CONFIGS[cfg]["k"]
+    rng = np.random.default_rng(1)
+    C0 = X[torch.from_numpy(rng.choice(n, k, replace=False)).to(cuda_device)].contiguous()
+    rms = float(torch.sqrt((X.double() ** 2).mean()))
+    a, b = km.Dataset([X]), km.Dataset([X])
+    Ca, Cb = C0.clone(), C0.clone()
+    screened = []
+    for step in range(8):
+        Na, sa = a.step(Ca, bounded=True)
+        Nb, sb = b.step(Cb, bounded=False)
+        assert sa["n_empty"] == sb["n_empty"]
+        # per-lane float32 partials of `best` are summed in another order once rows are queued
+        assert abs(sa["inertia"] - sb["inertia"]) <= 1e-7 * sb["inertia"]
+        lab_full = b.assign(Cb, return_labels=True)[3]
+        assert np.array_equal(_word_labels(a, k), lab_full), f"step {step}: labels differ"
+        assert np.array_equal(a.assign(Ca)[1], b.assign(Cb)[1])
+        # the same holds for the per-lane partial sums of x: the last float32 bit of a center may move
+        assert float((Na - Nb).abs().max()) <= 1e-7 * rms
+        screened.append(sa["screened"])
+        Ca, Cb = Na.clone(), Nb.clone()
+    assert screened[0] == n                       # the first pass compares every row
+    assert min(screened[3:]) < n // 2             # later passes keep most labels from their bounds
+
+
+def test_bounds_survive_a_jump_of_the_centers(cuda_device):
+    """Centers replaced by unrelated ones (a restart without reset): the drift makes every bound fail and
+    the pass is still exact."""
+    import mlx_kmeans_b200 as km
+    from mlx_kmeans_b200.data import generate
+    torch = _torch()
+    n, k = 300_000, 16
+    X = generate(3, 0, n, cuda_device, rows_total=n)
+    ds = km.Dataset([X])
+    C = X[:k].contiguous()
+    for _ in range(3):
+        C, _ = ds.step(C, bounded=True)
+        C = C.clone()
+    C2 = X[1000:1000 + k].contiguous() * 0.5
+    _, s = ds.step(C2, bounded=True)
+    ref = km.Dataset([X]).assign(C2, return_labels=True)[3]
+    assert np.array_equal(_word_labels(ds, k), ref)
