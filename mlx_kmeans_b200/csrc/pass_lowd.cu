@@ -4,7 +4,7 @@
 // Reference: the one-hot fused kernel of core.py:1537-1675 (configs with d <= 16: rows assigned and summed
 // per cluster in one read of X) and the rows kernel's label rule (core.py:263-274); built here for B200.
 //
-// Per thread, one row at a time (rows streamed into shared memory by cp.async, kStages - 1 rows ahead):
+// Per thread, one row at a time (rows streamed into shared memory by cp.async, several rows ahead):
 //   screen   score_c = |c|^2/2 - x.c for all k centers with packed fma.rn.f32x2 (two centers per
 //            instruction, centers held in registers); each score carries its center index in the low
 //            mantissa bits, and a tournament over the keys yields the smallest key (value and index) and the
@@ -19,6 +19,15 @@
 //            integers into the CTA's int64 totals.  Inertia: float64 per lane, folded per block likewise.
 // A block is a fixed range of kBlockRows local rows, so results are bit-reproducible; with shard starts that
 // are multiples of kBlockRows they are also identical for any split of the rows over GPUs.
+//
+// Two kernels:
+//   k_pass_lowd     every row is screened (optionally writing labels and `best`).
+//   k_pass_bounded  per-row bounds: each row carries one 32-bit word, a lower bound on its distance to every
+//                   center but its label (plus the drift at the time it was stored) with the label in the low
+//                   bits.  A row whose distance to its stored label's center is below the stored bound less
+//                   the drift since keeps that label without a screen -- the same label the screen would give,
+//                   so totals, labels and inertia are those of a full pass.  Failing rows queue per warp and
+//                   are screened 32 at a time, one per lane.  The first pass after a reset screens every row.
 #include <type_traits>
 
 #include "common.cuh"
@@ -30,10 +39,19 @@ namespace {
 
 constexpr int kThreads = 128;          // 4 warps per CTA
 constexpr int kWarps = kThreads / 32;
-constexpr int kStages = 8;             // ring slots per thread (power of two)
-constexpr int kRowsPerLane = 128;      // rows per lane between folds (a multiple of kStages, < 256)
+constexpr int kStages = 8;             // ring slots per thread of the screening kernel (power of two)
+#ifndef KMC_BOUNDED_AHEAD
+#define KMC_BOUNDED_AHEAD 0
+#endif
+#ifndef KMC_BOUNDED_MAX_CTAS
+#define KMC_BOUNDED_MAX_CTAS 0
+#endif
+// rows per thread in flight in the bounded kernel, held in registers: about 128 bytes of rows
+constexpr int bounded_ahead(int d) { return KMC_BOUNDED_AHEAD ? KMC_BOUNDED_AHEAD : d <= 4 ? 8 : 4; }
+constexpr int kRowsPerLane = 128;      // rows per lane between folds (a multiple of 8, < 256)
 constexpr int kBlockRows = kThreads * kRowsPerLane;   // 16384 rows per block
-static_assert(kRowsPerLane % kStages == 0 && kRowsPerLane < 256, "block layout");
+constexpr int kQueue = 64;             // queued rows per warp in the bounded kernel (power of two, >= 64)
+static_assert(kRowsPerLane % kStages == 0 && kRowsPerLane % 8 == 0 && kRowsPerLane < 256, "block layout");
 
 __device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
     return ((unsigned long long)__float_as_uint(hi) << 32) | __float_as_uint(lo);
@@ -78,47 +96,105 @@ __device__ __forceinline__ float keyed_imm(float s, unsigned keep) {
 
 __host__ __device__ constexpr unsigned idx_bits(int k) { return k <= 2 ? 1 : k <= 4 ? 2 : k <= 8 ? 3 : k <= 16 ? 4 : 5; }
 
-// s[0..D) += t in shared memory (a slot only this thread touches, so a plain read-modify-write), in
-// 16- / 8-byte pieces where D allows
+// D floats from shared memory (32-bit shared-window address), in 16- or 8-byte pieces where D allows;
+// the caller guarantees the alignment (rows and centers start at multiples of D floats, the buffers at 16 B)
 template <int D>
-__device__ __forceinline__ void add_row(unsigned saddr, const float (&t)[D]) {
+__device__ __forceinline__ void load_row(float (&x)[D], unsigned saddr) {
     if constexpr (D % 4 == 0) {
 #pragma unroll
-        for (int q = 0; q < D / 4; q++) {
-            float a0, a1, a2, a3;
-            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(a0), "=f"(a1), "=f"(a2), "=f"(a3) : "r"(saddr + 16 * q));
-            unsigned long long lo = add2(pack2(a0, a1), pack2(t[4 * q], t[4 * q + 1]));
-            unsigned long long hi = add2(pack2(a2, a3), pack2(t[4 * q + 2], t[4 * q + 3]));
-            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(saddr + 16 * q), "f"(lo_of(lo)), "f"(hi_of(lo)),
-                         "f"(lo_of(hi)), "f"(hi_of(hi)) : "memory");
-        }
+        for (int q = 0; q < D / 4; q++)
+            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(x[4 * q]), "=f"(x[4 * q + 1]), "=f"(x[4 * q + 2]), "=f"(x[4 * q + 3])
+                         : "r"(saddr + 16 * q));
     } else if constexpr (D % 2 == 0) {
 #pragma unroll
-        for (int q = 0; q < D / 2; q++) {
-            float a0, a1;
-            asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(a0), "=f"(a1) : "r"(saddr + 8 * q));
-            unsigned long long s = add2(pack2(a0, a1), pack2(t[2 * q], t[2 * q + 1]));
-            asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(saddr + 8 * q), "f"(lo_of(s)), "f"(hi_of(s)) : "memory");
-        }
+        for (int q = 0; q < D / 2; q++)
+            asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(x[2 * q]), "=f"(x[2 * q + 1]) : "r"(saddr + 8 * q));
     } else {
 #pragma unroll
-        for (int j = 0; j < D; j++) {
-            float a;
-            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(a) : "r"(saddr + 4 * j));
-            asm volatile("st.shared.f32 [%0], %1;" ::"r"(saddr + 4 * j), "f"(__fadd_rn(a, t[j])) : "memory");
-        }
+        for (int j = 0; j < D; j++) asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x[j]) : "r"(saddr + 4 * j));
     }
 }
 
-__device__ __forceinline__ void add_u32(unsigned saddr, unsigned v) {
-    unsigned a;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(a) : "r"(saddr));
-    asm volatile("st.shared.u32 [%0], %1;" ::"r"(saddr), "r"(a + v) : "memory");
+// store D floats (same pieces as load_row)
+template <int D>
+__device__ __forceinline__ void store_row(unsigned saddr, const float (&v)[D]) {
+    if constexpr (D % 4 == 0) {
+#pragma unroll
+        for (int q = 0; q < D / 4; q++)
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(saddr + 16 * q), "f"(v[4 * q]),
+                         "f"(v[4 * q + 1]), "f"(v[4 * q + 2]), "f"(v[4 * q + 3]) : "memory");
+    } else if constexpr (D % 2 == 0) {
+#pragma unroll
+        for (int q = 0; q < D / 2; q++)
+            asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(saddr + 8 * q), "f"(v[2 * q]), "f"(v[2 * q + 1])
+                         : "memory");
+    } else {
+#pragma unroll
+        for (int j = 0; j < D; j++) asm volatile("st.shared.f32 [%0], %1;" ::"r"(saddr + 4 * j), "f"(v[j]) : "memory");
+    }
 }
 
+// s += t elementwise, in packed pairs where D allows
+template <int D>
+__device__ __forceinline__ void add_into(float (&s)[D], const float (&t)[D]) {
+#pragma unroll
+    for (int j = 0; j + 1 < D; j += 2) {
+        const unsigned long long r = add2(pack2(s[j], s[j + 1]), pack2(t[j], t[j + 1]));
+        s[j] = lo_of(r);
+        s[j + 1] = hi_of(r);
+    }
+    if constexpr (D % 2 == 1) s[D - 1] = __fadd_rn(s[D - 1], t[D - 1]);
+}
+
+// s[0..D) += t in shared memory (a slot only this thread touches, so a plain read-modify-write)
+template <int D>
+__device__ __forceinline__ void add_row(unsigned saddr, const float (&t)[D]) {
+    float s[D];
+    load_row<D>(s, saddr);
+    add_into<D>(s, t);
+    store_row<D>(saddr, s);
+}
+
+__device__ __forceinline__ unsigned long long ld_u64(unsigned saddr) {
+    unsigned long long a;
+    asm volatile("ld.shared.u64 %0, [%1];" : "=l"(a) : "r"(saddr));
+    return a;
+}
+
+__device__ __forceinline__ void red_u32(unsigned saddr, unsigned v) {
+    asm volatile("red.shared.add.u32 [%0], %1;" ::"r"(saddr), "r"(v) : "memory");
+}
+
+// global loads for data read once in a pass (read-only path, no L1 allocation), kept in program order
+template <int D>
+__device__ __forceinline__ void ldg_row(float (&x)[D], const float* p) {
+    if constexpr (D % 4 == 0) {
+#pragma unroll
+        for (int q = 0; q < D / 4; q++)
+            asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(x[4 * q]), "=f"(x[4 * q + 1]), "=f"(x[4 * q + 2]), "=f"(x[4 * q + 3])
+                         : "l"(p + 4 * q));
+    } else if constexpr (D % 2 == 0) {
+#pragma unroll
+        for (int q = 0; q < D / 2; q++)
+            asm volatile("ld.global.nc.L1::no_allocate.v2.f32 {%0, %1}, [%2];" : "=f"(x[2 * q]), "=f"(x[2 * q + 1])
+                         : "l"(p + 2 * q));
+    } else {
+#pragma unroll
+        for (int j = 0; j < D; j++)
+            asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(x[j]) : "l"(p + j));
+    }
+}
+__device__ __forceinline__ unsigned ldg_u32(const uint32_t* p) {
+    unsigned v;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+
+// cp.async of BYTES (4, 8 or 16) from global memory to a shared-window address
 template <int BYTES>
-__device__ __forceinline__ void cp_async(void* smem, const void* gmem) {
-    unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+__device__ __forceinline__ void cp_async(unsigned s, const void* gmem) {
     if constexpr (BYTES == 16)
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
     else
@@ -159,26 +235,6 @@ __device__ __forceinline__ double d64_regs(const float* x, const float* c) {
     }
 }
 
-// D floats from shared memory (32-bit shared-window address), in 16- or 8-byte pieces where D allows;
-// the caller guarantees the alignment (rows and centers start at multiples of D floats, the buffers at 16 B)
-template <int D>
-__device__ __forceinline__ void load_row(float (&x)[D], unsigned saddr) {
-    if constexpr (D % 4 == 0) {
-#pragma unroll
-        for (int q = 0; q < D / 4; q++)
-            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                         : "=f"(x[4 * q]), "=f"(x[4 * q + 1]), "=f"(x[4 * q + 2]), "=f"(x[4 * q + 3])
-                         : "r"(saddr + 16 * q));
-    } else if constexpr (D % 2 == 0) {
-#pragma unroll
-        for (int q = 0; q < D / 2; q++)
-            asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(x[2 * q]), "=f"(x[2 * q + 1]) : "r"(saddr + 8 * q));
-    } else {
-#pragma unroll
-        for (int j = 0; j < D; j++) asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x[j]) : "r"(saddr + 4 * j));
-    }
-}
-
 template <int D>
 struct RowVec {
     float v[D];
@@ -210,41 +266,99 @@ __device__ __noinline__ int rescore_rows(unsigned fm, RowVec<D> x, const float* 
 
 }  // namespace
 
-template <int D, int K, bool BND>
-struct LowdSmem {
+// Centers packed two per 64-bit register pair for the screen: hp2[P] = (|c_2P|^2/2, |c_2P+1|^2/2) and
+// cp2[P][j] = (-c_2P[j], -c_2P+1[j]).  Padding centers (index >= k) score 2^126: finite, never below a real
+// score of representable data.
+template <int D, int K>
+struct Packed {
+    unsigned long long cp2[K / 2][D];
+    unsigned long long hp2[K / 2];
+
+    static constexpr int kWords = K / 2 * (D + 1);   // shared layout: per pair, hp2 then cp2[0..D)
+
+    __device__ __forceinline__ static unsigned long long word(const float* C, const float* hc, int k, int e) {
+        const int P = e / (D + 1), j = e % (D + 1), c0 = 2 * P, c1 = 2 * P + 1;
+        if (j == 0) return pack2(c0 < k ? hc[c0] : 8.5070591730234616e37f, c1 < k ? hc[c1] : 8.5070591730234616e37f);
+        return pack2(c0 < k ? -C[c0 * D + j - 1] : -0.0f, c1 < k ? -C[c1 * D + j - 1] : -0.0f);
+    }
+    // from the shared layout (volatile loads: the compiler keeps them where they are written)
+    __device__ __forceinline__ void load(unsigned saddr) {
+#pragma unroll
+        for (int P = 0; P < K / 2; P++) {
+            hp2[P] = ld_u64(saddr + (unsigned)(P * (D + 1)) * 8u);
+#pragma unroll
+            for (int j = 0; j < D; j++) cp2[P][j] = ld_u64(saddr + (unsigned)(P * (D + 1) + 1 + j) * 8u);
+        }
+    }
+    __device__ __forceinline__ unsigned long long hp(int P) const { return hp2[P]; }
+    __device__ __forceinline__ unsigned long long cp(int P, int j) const { return cp2[P][j]; }
+    __device__ __forceinline__ void load(const float* C, const float* hc, int k) {
+#pragma unroll
+        for (int P = 0; P < K / 2; P++) {
+            hp2[P] = word(C, hc, k, P * (D + 1));
+#pragma unroll
+            for (int j = 0; j < D; j++) cp2[P][j] = word(C, hc, k, P * (D + 1) + 1 + j);
+        }
+    }
+};
+
+
+// The same packed centers read from their shared layout at the point of use (volatile loads, so they are not
+// hoisted into registers held across a loop): for screens that are rare enough not to need registers.
+template <int D, int K>
+struct PackedShared {
+    unsigned s;
+    __device__ __forceinline__ unsigned long long hp(int P) const { return ld_u64(s + (unsigned)(P * (D + 1)) * 8u); }
+    __device__ __forceinline__ unsigned long long cp(int P, int j) const {
+        return ld_u64(s + (unsigned)(P * (D + 1) + 1 + j) * 8u);
+    }
+};
+
+template <int D, int K>
+struct PlainSmem {
     static constexpr int kSums = K * D * 32;                       // floats per warp
     static constexpr int kCnts = ((K + 3) / 4) * 32;               // packed 8-bit counts per warp (words)
-    static constexpr int kQueue = 64;                              // queued rows per warp (power of two)
     static constexpr size_t ring = (size_t)kStages * kThreads * D * 4;
     static constexpr size_t sums = (size_t)kWarps * kSums * 4;
     static constexpr size_t cnts = (size_t)kWarps * kCnts * 4;
-    static constexpr size_t fold = (size_t)kWarps * K * (D + 1) * 8;
     static constexpr size_t centers = (size_t)32 * D * 4;
     static constexpr size_t acc = (size_t)K * (D + 2) * 8;
-    static constexpr size_t wring = BND ? (size_t)kStages * kThreads * 4 : 0;
-    static constexpr size_t queue = BND ? (size_t)kWarps * kQueue * 4 : 0;
-    static constexpr size_t total = ring + sums + cnts + fold + centers + acc + wring + queue;
+    static constexpr size_t total = ring + sums + cnts + centers + acc;
 };
 
-// Per-thread state of the row loop.
+template <int D, int K>
+struct BoundSmem {
+    static constexpr int kSums = K * D * 32;
+    static constexpr int kCnts = ((K + 3) / 4) * 32;
+    static constexpr size_t sums = (size_t)kWarps * kSums * 4;
+    static constexpr size_t cnts = (size_t)kWarps * kCnts * 4;
+    static constexpr size_t centers = (size_t)32 * D * 4;
+    static constexpr size_t packed = (size_t)Packed<D, K>::kWords * 8;
+    static constexpr size_t acc = (size_t)K * (D + 2) * 8;
+    static constexpr size_t queue = (size_t)kWarps * kQueue * 4;
+    static constexpr size_t total = sums + cnts + centers + packed + acc + queue;
+    static_assert(sums % 16 == 0 && cnts % 16 == 0 && centers % 16 == 0 && packed % 8 == 0 && acc % 8 == 0,
+                  "shared carve alignment");
+};
+
+// Per-thread state of the row loop.  Counts are packed four 8-bit fields to a word: a lane adds at most
+// kRowsPerLane < 256 rows to one cluster between folds.
 template <int D, int K>
 struct LowdRow {
     static constexpr unsigned IDXBITS = idx_bits(K);
     static constexpr unsigned MASK = (1u << IDXBITS) - 1u;
-    unsigned long long cp2[K / 2][D];   // -c, two centers per register pair
-    unsigned long long hp2[K / 2];      // |c|^2 / 2
     float coef, slack, cmax2, wabs;
     float cum_lo, cum_up;               // drift of the centers since the bounds were started (bounds mode)
     unsigned keep;                      // ~(index mask), a launch argument so it stays in a register
     const float* cs;                    // shared copy of the centers (zero padded to 32 rows)
     unsigned cs_s;                      // its shared-window address
     float* sums;                        // this warp's sums slots: [cluster][lane][D]
-    unsigned* cnts;                     // this warp's packed 8-bit counts: [cluster / 4][lane]
-    unsigned sums_s, cnts_s;            // their shared-window addresses
+    unsigned* cnts;                     // this warp's packed counts: [cluster / 4][lane]
+    unsigned slot0_s, cnt0_s;           // shared-window addresses of this lane's slot / count word of cluster 0
     int lane, k;
     double inert;
     float ichunk;
-    long long rescored, screened;
+    int rescored, screened;
     int bad;
 
     struct Scr {
@@ -254,24 +368,26 @@ struct LowdRow {
     };
 
     // keys of centers 2P and 2P+1: one packed distance chain, then one lop3 each inserting the index
-    template <int P>
-    __device__ __forceinline__ void pair(const unsigned long long (&xx)[D], unsigned long long xh2, float (&t1)[K / 2],
-                                         float (&t2)[K / 2]) {
-        unsigned long long s = add2(xh2, hp2[P]);
+    template <int P, class PK>
+    __device__ __forceinline__ void pair(const PK& pk, const unsigned long long (&xx)[D], unsigned long long xh2,
+                                         float (&t1)[K / 2], float (&t2)[K / 2]) {
+        unsigned long long s = add2(xh2, pk.hp(P));
 #pragma unroll
-        for (int j = 0; j < D; j++) s = fma2(xx[j], cp2[P][j], s);
+        for (int j = 0; j < D; j++) s = fma2(xx[j], pk.cp(P, j), s);
         const float ka = keyed_imm<2 * P>(lo_of(s), keep), kb = keyed_imm<2 * P + 1>(hi_of(s), keep);
         t1[P] = fminf(ka, kb);
         t2[P] = fmaxf(ka, kb);
     }
-    template <int... P>
-    __device__ __forceinline__ void pairs(std::integer_sequence<int, P...>, const unsigned long long (&xx)[D],
-                                          unsigned long long xh2, float (&t1)[K / 2], float (&t2)[K / 2]) {
-        (pair<P>(xx, xh2, t1, t2), ...);
+    template <class PK, int... P>
+    __device__ __forceinline__ void pairs(std::integer_sequence<int, P...>, const PK& pk,
+                                          const unsigned long long (&xx)[D], unsigned long long xh2,
+                                          float (&t1)[K / 2], float (&t2)[K / 2]) {
+        (pair<P>(pk, xx, xh2, t1, t2), ...);
     }
 
     // Nearest center of x over all k centers.  Warp-collective (every lane calls it; `valid` marks real rows).
-    __device__ __forceinline__ Scr screen(const float (&x)[D], bool valid) {
+    template <class PK>
+    __device__ __forceinline__ Scr screen(const float (&x)[D], bool valid, const PK& pk) {
         unsigned long long xx[D];
         float x2 = 0.0f;
 #pragma unroll
@@ -284,7 +400,7 @@ struct LowdRow {
         const float xh = 0.5f * x2;
         const unsigned long long xh2 = pack2(xh, xh);
         float t1[K / 2], t2[K / 2];
-        pairs(std::make_integer_sequence<int, K / 2>{}, xx, xh2, t1, t2);
+        pairs(std::make_integer_sequence<int, K / 2>{}, pk, xx, xh2, t1, t2);
 #pragma unroll
         for (int w = K / 4; w >= 1; w >>= 1) {
 #pragma unroll
@@ -314,10 +430,8 @@ struct LowdRow {
         return s;
     }
 
-    // residual t = x - c_l and best = sum t^2 (each op rounded on its own, in column order)
-    __device__ __forceinline__ float residual(const float (&x)[D], int l, float (&t)[D]) {
-        float c[D];
-        load_row<D>(c, cs_s + (unsigned)(l * D * 4));
+    // residual t = x - c and best = sum t^2 (each op rounded on its own, in column order)
+    __device__ __forceinline__ float residual(const float (&x)[D], const float (&c)[D], float (&t)[D]) {
         float q[D];
         if constexpr (D % 2 == 0) {
 #pragma unroll
@@ -339,12 +453,21 @@ struct LowdRow {
         for (int j = 1; j < D; j++) b = __fadd_rn(b, q[j]);
         return b;
     }
+    __device__ __forceinline__ float residual(const float (&x)[D], int l, float (&t)[D]) {
+        float c[D];
+        load_row<D>(c, cs_s + (unsigned)(l * D * 4));
+        return residual(x, c, t);
+    }
+
+    __device__ __forceinline__ unsigned slot_addr(int l) const { return slot0_s + (unsigned)l * (32u * D * 4u); }
+    __device__ __forceinline__ unsigned cnt_addr(int l) const { return cnt0_s + (unsigned)(l >> 2) * 128u; }
+    __device__ __forceinline__ static unsigned cnt_one(int l) { return 1u << ((l & 3) * 8); }
 
     // this lane's slot of cluster l (plain read-modify-write: nobody else touches it)
     __device__ __forceinline__ void accumulate(int l, const float (&t)[D], float b) {
-        add_row<D>(sums_s + (unsigned)((l * 32 + lane) * D * 4), t);
-        add_u32(cnts_s + (unsigned)(((l >> 2) * 32 + lane) * 4), 1u << ((l & 3) * 8));
-        ichunk = __fadd_rn(ichunk, b);     // float32 over at most kStages rows, then float64
+        add_row<D>(slot_addr(l), t);
+        red_u32(cnt_addr(l), cnt_one(l));
+        ichunk = __fadd_rn(ichunk, b);     // float32 over at most 8 rows, then float64
     }
 
     // Bound word of a screened row: a lower bound on its distance to every center but its label, plus the
@@ -358,59 +481,158 @@ struct LowdRow {
         return (__float_as_uint(adj) & keep) | (unsigned)s.l;
     }
 
-    // plain row: screen, residual, totals (and optionally the bound word, labels, best)
-    template <bool CHECK, bool OUT, bool BW>
-    __device__ __forceinline__ void row(const float (&x)[D], int64_t row, int64_t n, const PassArgs& a) {
+    // Does the stored label still hold?  w: the row's bound word, b: its float32 distance to the stored label's
+    // center.  With Y = stored bound - drift since (cum_up rounds the drift up), the row keeps its label when
+    // the exact distance is below Y^2: b carries at most (D + 4) 2^-23 of relative error, and the computed
+    // y = fl(Y) and fl(y y) exceed Y and Y^2 by at most 2^-24 and 3 2^-24 relative, fl(b F) falls short of
+    // b F by at most 2^-24 -- all inside F's extra factor 1 + 2^-20.
+    static constexpr float kHoldF = (float)((1.0 + (D + 4) / 8388608.0) * (1.0 + 1.0 / 1048576.0) * (1.0 + 1.0 / 8388608.0));
+    __device__ __forceinline__ bool holds(unsigned w, float b) const {
+        const float y = __fsub_rn(__uint_as_float(w & keep), cum_up);
+        return y > 0.0f && __fmul_rn(b, kHoldF) < __fmul_rn(y, y);
+    }
+
+    // screened row: screen, residual, totals (and optionally labels and best)
+    template <bool CHECK, bool OUT>
+    __device__ __forceinline__ void row(const float (&x)[D], int64_t row, int64_t n, const PassArgs& a,
+                                        const Packed<D, K>& pk) {
         const bool valid = !CHECK || row < n;
-        const Scr s = screen(x, valid);
+        const Scr s = screen(x, valid, pk);
         if (!valid) return;
         float t[D];
         const float b = residual(x, s.l, t);
         accumulate(s.l, t, b);
-        if (BW) a.brows[row] = bound_word(s);
         if (OUT) {
             if (a.labels) a.labels[row] = s.l;
             if (a.best) a.best[row] = b;
         }
     }
 
-    // end of a chunk of kStages rows: the float32 partial of the inertia joins the float64 one
+    // end of a chunk of 8 rows: the float32 partial of the inertia joins the float64 one
     __device__ __forceinline__ void chunk_done() {
         inert = __dadd_rn(inert, (double)ichunk);
         ichunk = 0.0f;
     }
+
+    __device__ __forceinline__ void init(const PassArgs& a, const Prep& prep, const float* cs_, float* sums_all,
+                                         unsigned* cnts_all, int kSums, int kCnts, int warp, int lane_) {
+        // Window of the screen.  With u = 2^-24 and g = D u / (1 - D u), the computed half distance of every
+        // center is within (2 g + u / 2)(|x|^2 + |c|^2) of the exact one (|x|^2 and |c|^2 each carry g, the
+        // add that joins them u, the fma chain g on |x|^2/2 + |c|^2/2 + |x||c|), so two centers within
+        // (4 g + u)(|x|^2 + max|c|^2) -- taken with a 2^-10 margin plus D 2^-48 for the float64 rounding of
+        // D64 -- may be misordered.  The index bits move a key by less than 2^(IDXBITS-23) of itself; every
+        // key above the second smallest is at least that key less that share, hence slack = 2^(IDXBITS-22)
+        // on |m1| + |m2| (a factor two to spare).
+        coef = (float)(((4.0 * D + 2.0) / 16777216.0) * (1.0 + 1.0 / 1024.0) + (double)D / 281474976710656.0);
+        slack = 1.0f / (float)(1u << (22 - IDXBITS));
+        keep = a.key_keep;
+        cmax2 = prep.cmax2;
+        wabs = prep.win_abs;
+        cum_lo = prep.bcum_lo;
+        cum_up = prep.bcum_up;
+        cs = cs_;
+        cs_s = (unsigned)__cvta_generic_to_shared(cs_);
+        sums = sums_all + (size_t)warp * kSums;
+        cnts = cnts_all + (size_t)warp * kCnts;
+        slot0_s = (unsigned)__cvta_generic_to_shared(sums) + (unsigned)(lane_ * D * 4);
+        cnt0_s = (unsigned)__cvta_generic_to_shared(cnts) + (unsigned)(lane_ * 4);
+        lane = lane_;
+        k = a.k;
+        inert = 0.0;
+        ichunk = 0.0f;
+        rescored = 0;
+        screened = 0;
+        bad = 0;
+    }
+
+    // End of a block: fold the lanes' slots into the CTA's int64 totals (fixed order => deterministic) and
+    // the block's inertia into acc[1].  Lane L folds columns s = c * D + j (s = L, L + 32, ...): the 32 lanes'
+    // partial sums in float64 in a fixed rotation, the cluster's count, then sum x = sum t + count * c rounded
+    // once to the fixed-point grid.
+    __device__ __forceinline__ void fold_block(long long* acc, const double* scale_x, double scale_i, int kSums,
+                                               int kCnts) {
+        __syncwarp();
+        for (int s = lane; s < K * D; s += 32) {
+            const int c = s / D, j = s % D;
+            const float* col = sums + (size_t)c * 32 * D + j;
+            const unsigned* ccol = cnts + (c >> 2) * 32;
+            const int sh = (c & 3) * 8;
+            double sum = 0.0;
+            unsigned cnt = 0;
+#pragma unroll 8
+            for (int i = 0; i < 32; i++) {
+                const int li = (i + lane) & 31;
+                sum = __dadd_rn(sum, (double)col[li * D]);
+                cnt += (ccol[li] >> sh) & 255u;
+            }
+            if (c < k && cnt) {
+                const double sxv = __fma_rn((double)cnt, (double)cs[c * D + j], sum);
+                atomicAdd(reinterpret_cast<unsigned long long*>(&acc[c * (D + 2) + 2 + j]),
+                          (unsigned long long)__double2ll_rn(__dmul_rn(sxv, scale_x[j])));
+                if (j == 0) atomicAdd(reinterpret_cast<unsigned long long*>(&acc[c * (D + 2)]), (unsigned long long)cnt);
+            }
+        }
+        __syncwarp();
+        for (int e = lane; e < kCnts; e += 32) cnts[e] = 0u;
+        for (int e = lane; e < kSums; e += 32) sums[e] = 0.0f;
+        // inertia of the block: fixed xor-tree over the warp, one quantised add
+        double in = inert;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) in = __dadd_rn(in, __shfl_xor_sync(0xffffffffu, in, o));
+        if (!(in <= 1.0e300)) bad = 1;            // a non-finite distance anywhere in the block
+        else if (lane == 0 && in != 0.0)
+            atomicAdd(reinterpret_cast<unsigned long long*>(&acc[1]),
+                      (unsigned long long)__double2ll_rn(__dmul_rn(in, scale_i)));
+        inert = 0.0;
+        __syncwarp();
+    }
+
+    // End of the kernel (after a __syncthreads): the CTA's totals and counters into global memory.
+    __device__ __forceinline__ void finish(const long long* acc, const PassArgs& a, int tid) {
+        for (int e = tid; e < k * (D + 2); e += kThreads) {
+            long long v = acc[e];
+            if (v) atomicAdd(reinterpret_cast<unsigned long long*>(a.totals + e), (unsigned long long)v);
+        }
+        int r = rescored, s = screened;
+        for (int o = 16; o; o >>= 1) {
+            r += __shfl_xor_sync(0xffffffffu, r, o);
+            s += __shfl_xor_sync(0xffffffffu, s, o);
+        }
+        if (lane == 0 && r) atomicAdd(reinterpret_cast<unsigned long long*>(&a.counters[0]), (unsigned long long)r);
+        if (lane == 0 && s) atomicAdd(reinterpret_cast<unsigned long long*>(&a.counters[2]), (unsigned long long)s);
+        if (bad) atomicOr(reinterpret_cast<unsigned long long*>(&a.counters[1]), (unsigned long long)kFlagNonFinite);
+    }
 };
 
-#ifndef KMC_LOWD_MIN_BLOCKS
-#define KMC_LOWD_MIN_BLOCKS 4
-#endif
+// CTAs per SM that the shared memory of one CTA allows (228 KB per SM, 1 KB of it reserved per CTA), at most
+// eight.  The register cap of __launch_bounds__ follows from it (128 registers at four CTAs of 128 threads,
+// 168 at three), so an instance is not squeezed below what its shared memory lets run anyway; the screening
+// kernel, which holds the packed centers in registers, asks for at most four.
+constexpr int ctas_per_sm(size_t smem) {
+    int c = 8;
+    while (c > 1 && (smem + 1024) * c > 233472) c--;
+    return c;
+}
 
-// BND: the pass keeps per-row bounds (a.brows, one word per row; a.bmeta holds validity and drift).  On the
-// first pass (bounds not valid yet) every row is screened and its word written; afterwards a row whose
-// distance to its stored label is below its stored bound less the drift keeps its label without a screen,
-// and the others queue per warp and are screened 32 at a time (one per lane) so the warp does not diverge.
-template <int D, int K, bool OUT, bool BND>
-__global__ void __launch_bounds__(kThreads, KMC_LOWD_MIN_BLOCKS) k_pass_lowd(PassArgs a) {
+// Every row screened; OUT: labels and best written too.
+template <int D, int K, bool OUT>
+__global__ void __launch_bounds__(kThreads, ctas_per_sm(PlainSmem<D, K>::total) < 4 ? ctas_per_sm(PlainSmem<D, K>::total)
+                                                                                 : 4) k_pass_lowd(PassArgs a) {
     static_assert(K % 2 == 0 && K <= 32, "K even, at most 32");
     constexpr int CPB = (D % 4 == 0) ? 16 : ((D % 2 == 0) ? 8 : 4);   // bytes per cp.async
     constexpr int NCP = D * 4 / CPB;
-    constexpr unsigned IDXBITS = idx_bits(K);
-    constexpr unsigned MASK = (1u << IDXBITS) - 1u;
-    using L = LowdSmem<D, K, BND>;
+    using L = PlainSmem<D, K>;
     extern __shared__ __align__(16) unsigned char smem[];
     float* ring = reinterpret_cast<float*>(smem);
     float* sums_all = reinterpret_cast<float*>(smem + L::ring);
     unsigned* cnts_all = reinterpret_cast<unsigned*>(smem + L::ring + L::sums);
-    double* fold_all = reinterpret_cast<double*>(smem + L::ring + L::sums + L::cnts);
-    float* cs = reinterpret_cast<float*>(smem + L::ring + L::sums + L::cnts + L::fold);
-    long long* acc = reinterpret_cast<long long*>(smem + L::ring + L::sums + L::cnts + L::fold + L::centers);
-    unsigned* wring = reinterpret_cast<unsigned*>(smem + L::ring + L::sums + L::cnts + L::fold + L::centers + L::acc);
-    int* queue_all = reinterpret_cast<int*>(smem + L::ring + L::sums + L::cnts + L::fold + L::centers + L::acc + L::wring);
+    float* cs = reinterpret_cast<float*>(smem + L::ring + L::sums + L::cnts);
+    long long* acc = reinterpret_cast<long long*>(smem + L::ring + L::sums + L::cnts + L::centers);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int k = a.k;
     const int64_t n = a.n;
-    double* fold = fold_all + (size_t)warp * K * (D + 1);
+    const Prep prep = *a.prep;
 
     for (int e = tid; e < 32 * D; e += kThreads) cs[e] = (e / D) < k ? a.C[e] : 0.0f;
     for (int e = tid; e < K * (D + 2); e += kThreads) acc[e] = 0;
@@ -418,65 +640,27 @@ __global__ void __launch_bounds__(kThreads, KMC_LOWD_MIN_BLOCKS) k_pass_lowd(Pas
     for (int e = tid; e < kWarps * L::kCnts; e += kThreads) cnts_all[e] = 0u;
     __syncthreads();
 
+    Packed<D, K> pk;
+    pk.load(cs, a.hc, k);
     LowdRow<D, K> st;
-#pragma unroll
-    for (int p = 0; p < K / 2; p++) {
-        const int c0 = 2 * p, c1 = 2 * p + 1;
-        // padding centers score 2^126: finite, never below a real score of representable data
-        st.hp2[p] = pack2(c0 < k ? a.hc[c0] : 8.5070591730234616e37f, c1 < k ? a.hc[c1] : 8.5070591730234616e37f);
-#pragma unroll
-        for (int j = 0; j < D; j++) st.cp2[p][j] = pack2(-cs[c0 * D + j], -cs[c1 * D + j]);
-    }
-    const Prep prep = *a.prep;
-    // Window of the screen.  With u = 2^-24 and g = D u / (1 - D u), the computed half distance of every
-    // center is within (2 g + u / 2)(|x|^2 + |c|^2) of the exact one (|x|^2 and |c|^2 each carry g, the add
-    // that joins them u, the fma chain g on |x|^2/2 + |c|^2/2 + |x||c|), so two centers within
-    // (4 g + u)(|x|^2 + max|c|^2) -- taken with a 2^-10 margin plus D 2^-48 for the float64 rounding of
-    // D64 -- may be misordered.  The index bits move a key by less than 2^(IDXBITS-23) of itself; every key
-    // above the second smallest is at least that key less that share, hence slack = 2^(IDXBITS-22) on
-    // |m1| + |m2| (a factor two to spare).
-    st.coef = (float)(((4.0 * D + 2.0) / 16777216.0) * (1.0 + 1.0 / 1024.0) + (double)D / 281474976710656.0);
-    st.slack = 1.0f / (float)(1u << (22 - IDXBITS));
-    st.keep = a.key_keep;
-    st.cmax2 = prep.cmax2;
-    st.wabs = prep.win_abs;
-    st.cum_lo = prep.bcum_lo;
-    st.cum_up = prep.bcum_up;
-    st.cs = cs;
-    st.cs_s = (unsigned)__cvta_generic_to_shared(cs);
-    st.sums = sums_all + (size_t)warp * L::kSums;
-    st.cnts = cnts_all + (size_t)warp * L::kCnts;
-    st.sums_s = (unsigned)__cvta_generic_to_shared(st.sums);
-    st.cnts_s = (unsigned)__cvta_generic_to_shared(st.cnts);
-    st.lane = lane;
-    st.k = k;
-    st.inert = 0.0;
-    st.ichunk = 0.0f;
-    st.rescored = 0;
-    st.screened = 0;
-    st.bad = 0;
-    // bounded steps only once the bounds exist (the first pass writes them)
-    const bool bounded = BND && prep.bvalid != 0;
+    st.init(a, prep, cs, sums_all, cnts_all, L::kSums, L::kCnts, warp, lane);
 
     // Row of thread tid at step r of block b: b * kBlockRows + r * kThreads + tid.  Ring slot r % kStages
     // holds step r; the prefetch of step r + kStages - 1 is issued at step r into the slot read at step
     // r - 1, so this thread's reads of that slot have completed.  The prefetch walks a pointer (and, near
     // the end of the rows, a row index) kStages - 1 steps ahead of the reads, jumping to the CTA's next
-    // block when it leaves the current one.  Bounded passes stream the rows' bound words the same way.
+    // block when it leaves the current one.
     const int64_t nblk = (n + kBlockRows - 1) / kBlockRows;
-    float* myring = ring + (size_t)tid * D;
-    const unsigned myring_s = (unsigned)__cvta_generic_to_shared(myring);
-    unsigned* mywring = wring + tid;
+    const unsigned myring_s = (unsigned)__cvta_generic_to_shared(ring + (size_t)tid * D);
     constexpr int SLOT = kThreads * D;
     constexpr int STEP = kThreads * D;                 // floats between a thread's consecutive rows
     const float* pf = a.X + ((int64_t)blockIdx.x * kBlockRows + tid) * D;
     int64_t pf_row = (int64_t)blockIdx.x * kBlockRows + tid;
     auto fetch = [&](int slot, bool ok) {
         if (ok) {
-            float* dst = myring + slot * SLOT;
+            const unsigned dst = myring_s + (unsigned)(slot * SLOT * 4);
 #pragma unroll
-            for (int q = 0; q < NCP; q++) cp_async<CPB>(dst + q * (CPB / 4), pf + q * (CPB / 4));
-            if (BND && bounded) cp_async<4>(mywring + slot * kThreads, a.brows + pf_row);
+            for (int q = 0; q < NCP; q++) cp_async<CPB>(dst + q * CPB, pf + q * (CPB / 4));
         }
         cp_commit();
         pf += STEP;
@@ -485,36 +669,11 @@ __global__ void __launch_bounds__(kThreads, KMC_LOWD_MIN_BLOCKS) k_pass_lowd(Pas
 #pragma unroll
     for (int s = 0; s < kStages - 1; s++) fetch(s, pf_row < n);
 
-    // per-warp queue of rows that failed their bound (offsets within the block), screened 32 at a time
-    int* queue = queue_all + warp * L::kQueue;
-    int qhead = 0, qcount = 0;
-
     for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
         const int64_t base = blk * kBlockRows + tid;
-        const int64_t blk0 = blk * kBlockRows;
         const int64_t next = (blk + gridDim.x) * kBlockRows + tid;
         // checks are needed only while this block or the prefetched part of the next one is ragged
         const bool clean = (blk + gridDim.x + 1) * kBlockRows <= n;
-
-        // screen `cnt` queued rows, one per lane
-        auto flush = [&](int cnt) {
-            const bool v = lane < cnt;
-            const int off = v ? queue[(qhead + lane) & (L::kQueue - 1)] : 0;
-            const int64_t row = blk0 + off;
-            float x[D];
-#pragma unroll
-            for (int j = 0; j < D; j++) x[j] = v ? __ldg(a.X + row * D + j) : 0.0f;
-            const auto s = st.screen(x, v);
-            if (v) {
-                float t[D];
-                const float b = st.residual(x, s.l, t);
-                st.accumulate(s.l, t, b);
-                a.brows[row] = st.bound_word(s);
-            }
-            st.screened += v ? 1 : 0;
-            qhead = (qhead + cnt) & (L::kQueue - 1);
-            qcount -= cnt;
-        };
 
         auto steps = [&](auto check) {
             constexpr bool CHECK = decltype(check)::value;
@@ -530,145 +689,222 @@ __global__ void __launch_bounds__(kThreads, KMC_LOWD_MIN_BLOCKS) k_pass_lowd(Pas
                     cp_wait<kStages - 1>();
                     float x[D];
                     load_row<D>(x, myring_s + (unsigned)(s * SLOT * 4));
-                    const int64_t row = base + (int64_t)r * kThreads;
-                    if constexpr (BND) {
-                        if (bounded) {
-                            const bool valid = !CHECK || row < n;
-                            const unsigned w = mywring[s * kThreads];
-                            const int l = (int)(w & MASK);
-                            float t[D];
-                            const float b = st.residual(x, l, t);
-                            // stored bound less the drift since it was stored (both rounded against the row)
-                            const float lbn = __fmul_rn(__fsub_rn(__uint_as_float(w & st.keep), st.cum_up),
-                                                        1.0f - 1.0f / 4194304.0f);
-                            const bool keep_label = valid && lbn > 0.0f &&
-                                                    __fmul_rn(b, 1.0f + (float)(D + 4) / 8388608.0f) <
-                                                        __fmul_rn(__fmul_rn(lbn, lbn), 1.0f - 1.0f / 4194304.0f);
-                            if (keep_label) st.accumulate(l, t, b);
-                            const unsigned fm = __ballot_sync(0xffffffffu, valid && !keep_label);
-                            if (fm) {
-                                const int pos = __popc(fm & ((1u << lane) - 1u));
-                                if ((fm >> lane) & 1u)
-                                    queue[(qhead + qcount + pos) & (L::kQueue - 1)] = (int)(row - blk0);
-                                qcount += __popc(fm);
-                                if (qcount >= 32) flush(32);
-                            }
-                            continue;
-                        }
-                        st.template row<CHECK, OUT, true>(x, row, n, a);
-                        st.screened += (!CHECK || row < n) ? 1 : 0;
-                    } else {
-                        st.template row<CHECK, OUT, false>(x, row, n, a);
-                    }
+                    st.template row<CHECK, OUT>(x, base + (int64_t)r * kThreads, n, a, pk);
+                    if (s % 8 == 7) st.chunk_done();
                 }
-                st.chunk_done();
             }
         };
         if (clean) steps(std::integral_constant<bool, false>{});
         else steps(std::integral_constant<bool, true>{});
-        if (BND && qcount > 0) flush(qcount);
         st.chunk_done();
-
-        // ---- fold the lanes' slots into the CTA's int64 totals (fixed order => deterministic)
-        __syncwarp();
-        float* sums = st.sums;
-        unsigned* cnts = st.cnts;
-        // slot (c, lane) holds D floats at sums[(c * 32 + lane) * D]; lane L folds columns s = c * D + j
-        for (int s = lane; s < K * D; s += 32) {
-            float* col = sums + (size_t)(s / D) * 32 * D + (s % D);
-            double sum = 0.0;
-#pragma unroll 8
-            for (int i = 0; i < 32; i++) {
-                const int li = (i + lane) & 31;
-                sum = __dadd_rn(sum, (double)col[li * D]);
-            }
-            fold[(s / D) * (D + 1) + (s % D)] = sum;
-        }
-        if (lane < K) {
-            const unsigned* col = cnts + (lane >> 2) * 32;
-            const int sh = (lane & 3) * 8;
-            unsigned c = 0;
-#pragma unroll 8
-            for (int i = 0; i < 32; i++) c += (col[(i + lane) & 31] >> sh) & 255u;
-            fold[lane * (D + 1) + D] = (double)c;
-        }
-        __syncwarp();
-        for (int e = lane; e < L::kCnts; e += 32) cnts[e] = 0u;
-        for (int e = lane; e < L::kSums; e += 32) sums[e] = 0.0f;
-        for (int s = lane; s < K * (D + 1); s += 32) {
-            const int c = s / (D + 1), j = s % (D + 1);
-            if (c >= k) continue;
-            const double cnt = fold[c * (D + 1) + D];
-            if (cnt == 0.0) continue;
-            if (j == D) {
-                atomicAdd(reinterpret_cast<unsigned long long*>(&acc[c * (D + 2)]), (unsigned long long)(long long)cnt);
-            } else {
-                const double sxv = __fma_rn(cnt, (double)cs[c * D + j], fold[s]);
-                atomicAdd(reinterpret_cast<unsigned long long*>(&acc[c * (D + 2) + 2 + j]),
-                          (unsigned long long)__double2ll_rn(__dmul_rn(sxv, a.scale_x[j])));
-            }
-        }
-        // inertia of the block: fixed xor-tree over the warp, one quantised add
-        double inert = st.inert;
-#pragma unroll
-        for (int o = 16; o; o >>= 1) inert = __dadd_rn(inert, __shfl_xor_sync(0xffffffffu, inert, o));
-        if (!(inert <= 1.0e300)) st.bad = 1;            // a non-finite distance anywhere in the block
-        else if (lane == 0 && inert != 0.0)
-            atomicAdd(reinterpret_cast<unsigned long long*>(&acc[1]),
-                      (unsigned long long)__double2ll_rn(__dmul_rn(inert, prep.scale_i)));
-        st.inert = 0.0;
-        __syncwarp();
+        st.fold_block(acc, a.scale_x, prep.scale_i, L::kSums, L::kCnts);
     }
     cp_wait<0>();
     __syncthreads();
-    for (int e = tid; e < k * (D + 2); e += kThreads) {
-        long long v = acc[e];
-        if (v) atomicAdd(reinterpret_cast<unsigned long long*>(a.totals + e), (unsigned long long)v);
+    st.finish(acc, a, tid);
+}
+
+// The bounded pass.  Each thread streams its rows and their bound words straight into registers, P rows ahead
+// (global loads that skip L1: every byte is read once), so neither passes through shared memory; the center
+// of the next row's stored label is read one row ahead.  A row whose bound holds adds its residual to its
+// lane's slot of the stored label.  Rows whose bound fails queue per warp (offsets within the block) and are
+// screened 32 at a time, one per lane, reading the row again (from L2) and the packed centers from shared
+// memory at the point of use, so the screen holds no registers across the row loop.  Before the bounds exist
+// (the first pass after a reset) every row takes that route and gets its word.
+// CTAs per SM of the bounded kernel: four (128 registers) up to five columns, three (168) above, where the
+// rows in flight and the screen's operands need more registers
+constexpr int bounded_ctas(int d, size_t smem) {
+    const int cap = KMC_BOUNDED_MAX_CTAS ? KMC_BOUNDED_MAX_CTAS : d <= 5 ? 4 : 3;
+    return ctas_per_sm(smem) < cap ? ctas_per_sm(smem) : cap;
+}
+
+template <int D, int K, int P>
+__global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::total)) k_pass_bounded(PassArgs a) {
+    static_assert(K % 2 == 0 && K <= 32, "K even, at most 32");
+    static_assert(P == 4 || P == 8 || P == 16, "prefetch depth");
+    constexpr int U = P > 8 ? P : 8;                    // steps per unrolled chunk
+    constexpr unsigned MASK = LowdRow<D, K>::MASK;
+    using L = BoundSmem<D, K>;
+    extern __shared__ __align__(16) unsigned char smem[];
+    size_t off = 0;
+    float* sums_all = reinterpret_cast<float*>(smem + off);        off += L::sums;
+    unsigned* cnts_all = reinterpret_cast<unsigned*>(smem + off);  off += L::cnts;
+    float* cs = reinterpret_cast<float*>(smem + off);              off += L::centers;
+    unsigned long long* pks = reinterpret_cast<unsigned long long*>(smem + off);   off += L::packed;
+    long long* acc = reinterpret_cast<long long*>(smem + off);     off += L::acc;
+    int* queue_all = reinterpret_cast<int*>(smem + off);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int k = a.k;
+    const int64_t n = a.n;
+
+    for (int e = tid; e < 32 * D; e += kThreads) cs[e] = (e / D) < k ? a.C[e] : 0.0f;
+    for (int e = tid; e < Packed<D, K>::kWords; e += kThreads) pks[e] = Packed<D, K>::word(a.C, a.hc, k, e);
+    for (int e = tid; e < K * (D + 2); e += kThreads) acc[e] = 0;
+    for (int e = tid; e < kWarps * L::kSums; e += kThreads) sums_all[e] = 0.0f;
+    for (int e = tid; e < kWarps * L::kCnts; e += kThreads) cnts_all[e] = 0u;
+    __syncthreads();
+
+    const Prep prep = *a.prep;
+    LowdRow<D, K> st;
+    st.init(a, prep, cs, sums_all, cnts_all, L::kSums, L::kCnts, warp, lane);
+    const PackedShared<D, K> pk_s{(unsigned)__cvta_generic_to_shared(pks)};
+    const bool bounded = prep.bvalid != 0;
+
+    // Row of thread tid at step r of block b: b * kBlockRows + r * kThreads + tid, as in the screening kernel.
+    // Register slot r % P holds row r; it is refilled with row r + P once row r is done.
+    const int64_t nblk = (n + kBlockRows - 1) / kBlockRows;
+    const float* pf = a.X + ((int64_t)blockIdx.x * kBlockRows + tid) * D;
+    const uint32_t* pw = a.brows + (int64_t)blockIdx.x * kBlockRows + tid;
+    float xq[P][D];
+    unsigned wq[P];
+    auto fetch = [&](float (&x)[D], unsigned& w, bool ok) {
+        if (ok) {
+            ldg_row<D>(x, pf);
+            w = ldg_u32(pw);
+        } else {
+#pragma unroll
+            for (int j = 0; j < D; j++) x[j] = 0.0f;
+            w = 0u;
+        }
+        pf += kThreads * D;
+        pw += kThreads;
+    };
+#pragma unroll
+    for (int q = 0; q < P; q++) fetch(xq[q], wq[q], (int64_t)blockIdx.x * kBlockRows + q * kThreads + tid < n);
+    // the center of the row in flight's stored label (a label past the end is masked: inside the 32-row table)
+    float cr[D];
+    load_row<D>(cr, st.cs_s + (wq[0] & MASK) * (unsigned)(D * 4));
+    constexpr int kJump = kRowsPerLane - P;             // step whose refill is the next block's first row
+
+    int* queue = queue_all + warp * kQueue;
+    int qhead = 0, qcount = 0;
+
+    for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+        const int64_t base = blk * kBlockRows + tid;
+        const int64_t blk0 = blk * kBlockRows;
+        const int64_t next = (blk + gridDim.x) * kBlockRows + tid;
+        const bool clean = (blk + gridDim.x + 1) * kBlockRows <= n;
+
+        // screen `cnt` queued rows, one per lane
+        auto flush = [&](int cnt) {
+            const bool v = lane < cnt;
+            const int qoff = v ? queue[(qhead + lane) & (kQueue - 1)] : 0;
+            const int64_t row = blk0 + qoff;
+            float x[D];
+            if (v) ldg_row<D>(x, a.X + row * D);
+            else {
+#pragma unroll
+                for (int j = 0; j < D; j++) x[j] = 0.0f;
+            }
+            const auto s = st.screen(x, v, pk_s);
+            if (v) {
+                float t[D];
+                const float b = st.residual(x, s.l, t);
+                st.accumulate(s.l, t, b);
+                a.brows[row] = st.bound_word(s);
+            }
+            st.screened += v ? 1 : 0;
+            qhead = (qhead + cnt) & (kQueue - 1);
+            qcount -= cnt;
+        };
+
+        auto steps = [&](auto check) {
+            constexpr bool CHECK = decltype(check)::value;
+            for (int ch = 0; ch < kRowsPerLane / U; ch++) {
+#pragma unroll
+                for (int s = 0; s < U; s++) {
+                    const int r = ch * U + s;
+                    const int q = s % P;
+                    const int rofs = r * kThreads + tid;             // row within the block
+                    const bool valid = !CHECK || blk0 + rofs < n;
+                    const unsigned w = wq[q];
+                    const int l = (int)(w & MASK);
+                    // this lane's slot of the stored label first: its latency overlaps the arithmetic
+                    const unsigned sa = st.slot_addr(l);
+                    float sl[D];
+                    load_row<D>(sl, sa);
+                    float t[D];
+                    const float b = st.residual(xq[q], cr, t);
+                    const bool keep = bounded && valid && st.holds(w, b);
+                    load_row<D>(cr, st.cs_s + (wq[(s + 1) % P] & MASK) * (unsigned)(D * 4));   // row r + 1's
+                    if (keep) {
+                        add_into<D>(sl, t);
+                        store_row<D>(sa, sl);
+                        red_u32(st.cnt_addr(l), LowdRow<D, K>::cnt_one(l));
+                        st.ichunk = __fadd_rn(st.ichunk, b);
+                    }
+                    const unsigned fm = __ballot_sync(0xffffffffu, valid && !keep);
+                    if (fm) {
+                        const int pos = __popc(fm & ((1u << lane) - 1u));
+                        if ((fm >> lane) & 1u) queue[(qhead + qcount + pos) & (kQueue - 1)] = rofs;
+                        qcount += __popc(fm);
+                        if (qcount >= 32) flush(32);
+                    }
+                    if (s == kJump % U && ch == kJump / U) {
+                        pf = a.X + next * D;
+                        pw = a.brows + next;
+                    }
+                    // the refill is row r + P of this block or, past its end, of the next one
+                    const int64_t frow = r + P < kRowsPerLane ? blk0 + rofs + P * kThreads
+                                                              : next + (r + P - kRowsPerLane) * kThreads;
+                    fetch(xq[q], wq[q], !CHECK || frow < n);
+                    if (s % 8 == 7) st.chunk_done();
+                }
+            }
+        };
+        if (clean) steps(std::integral_constant<bool, false>{});
+        else steps(std::integral_constant<bool, true>{});
+        if (qcount > 0) flush(qcount);
+        st.chunk_done();
+        st.fold_block(acc, a.scale_x, prep.scale_i, L::kSums, L::kCnts);
     }
-    long long rescored = st.rescored, screened = st.screened;
-    for (int o = 16; o; o >>= 1) {
-        rescored += __shfl_xor_sync(0xffffffffu, rescored, o);
-        screened += __shfl_xor_sync(0xffffffffu, screened, o);
-    }
-    if (lane == 0 && rescored) atomicAdd(reinterpret_cast<unsigned long long*>(&a.counters[0]), (unsigned long long)rescored);
-    if (BND && lane == 0 && screened)
-        atomicAdd(reinterpret_cast<unsigned long long*>(&a.counters[2]), (unsigned long long)screened);
-    if (st.bad) atomicOr(reinterpret_cast<unsigned long long*>(&a.counters[1]), (unsigned long long)kFlagNonFinite);
+    __syncthreads();
+    st.finish(acc, a, tid);
 }
 
 namespace {
 
-template <int D, int K, bool OUT, bool BND>
-cudaError_t run(PassArgs a, cudaStream_t st) {
-    using L = LowdSmem<D, K, BND>;
-    const size_t smem = L::total;
-    static unsigned long long configured = 0;   // one bit per device: the attribute is per device
+template <typename Kern>
+cudaError_t launch_grid(Kern kern, size_t smem, unsigned long long& configured, PassArgs a, cudaStream_t st) {
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!(configured >> (dev & 63) & 1ull)) {
-        cudaError_t e = cudaFuncSetAttribute(k_pass_lowd<D, K, OUT, BND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
+    if (!(configured >> (dev & 63) & 1ull)) {   // one bit per device: the attribute is per device
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         configured |= 1ull << (dev & 63);
     }
     int per_sm = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_pass_lowd<D, K, OUT, BND>, kThreads, smem);
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorNotSupported;
     const int64_t nblk = (a.n + kBlockRows - 1) / kBlockRows;
     int64_t grid = (int64_t)num_sms() * per_sm;
     if (grid > nblk) grid = nblk;
     if (grid < 1) grid = 1;
-    a.key_keep = ~((1u << idx_bits(K)) - 1u);
-    k_pass_lowd<D, K, OUT, BND><<<(int)grid, kThreads, smem, st>>>(a);
+    kern<<<(int)grid, kThreads, smem, st>>>(a);
     return cudaGetLastError();
 }
 
-// bounded passes write no labels; plain passes optionally do
+template <int D, int K, bool OUT>
+cudaError_t run(PassArgs a, cudaStream_t st) {
+    static unsigned long long configured = 0;
+    a.key_keep = ~((1u << idx_bits(K)) - 1u);
+    return launch_grid(k_pass_lowd<D, K, OUT>, PlainSmem<D, K>::total, configured, a, st);
+}
+
+template <int D, int K>
+cudaError_t run_bounded(PassArgs a, cudaStream_t st) {
+    static unsigned long long configured = 0;
+    a.key_keep = ~((1u << idx_bits(K)) - 1u);
+    return launch_grid(k_pass_bounded<D, K, bounded_ahead(D)>, BoundSmem<D, K>::total, configured, a, st);
+}
+
+// bounded passes write no labels; plain passes optionally write labels and best
 template <int D, int K>
 cudaError_t run_out(PassArgs a, cudaStream_t st) {
-    if (a.brows) return run<D, K, false, true>(a, st);
-    return (a.labels || a.best) ? run<D, K, true, false>(a, st) : run<D, K, false, false>(a, st);
+    if (a.brows) return run_bounded<D, K>(a, st);
+    return (a.labels || a.best) ? run<D, K, true>(a, st) : run<D, K, false>(a, st);
 }
 
 template <int D>

@@ -235,7 +235,8 @@ def _word_labels(ds, k):
     from mlx_kmeans_b200 import _lib
     buf, nbytes = ds.bounds(k)[0]
     n, d = ds.parts[0].shape
-    off = nbytes - (((n * 4) + 255) // 256) * 256
+    a256 = lambda v: (v + 255) // 256 * 256
+    off = 256 + a256(k * d * 4)            # after the drift record and the centers of the last pass
     words = buf[off:off + n * 4].view(torch_int32()).cpu().numpy().view(np.uint32)
     kp = next(v for v in (2, 4, 8, 16, 32) if v >= k)
     return (words & (kp - 1)).astype(np.int64)
