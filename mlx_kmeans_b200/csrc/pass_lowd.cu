@@ -752,30 +752,33 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
     const bool bounded = prep.bvalid != 0;
 
     // Row of thread tid at step r of block b: b * kBlockRows + r * kThreads + tid, as in the screening kernel.
-    // Register slot r % P holds row r; it is refilled with row r + P once row r is done.
+    // Register slot r % P holds row r; it is refilled with row r + P once row r is done.  Steps run in chunks
+    // of U; a refill reads from this chunk's or the next chunk's base (the next block's first chunk after the
+    // last one) at a constant offset, so the loads carry immediate offsets and no per-row pointer arithmetic.
     const int64_t nblk = (n + kBlockRows - 1) / kBlockRows;
-    const float* pf = a.X + ((int64_t)blockIdx.x * kBlockRows + tid) * D;
-    const uint32_t* pw = a.brows + (int64_t)blockIdx.x * kBlockRows + tid;
+    constexpr int XSTEP = kThreads * D;                 // floats between a thread's consecutive rows
+    constexpr int NCH = kRowsPerLane / U;
     float xq[P][D];
     unsigned wq[P];
-    auto fetch = [&](float (&x)[D], unsigned& w, bool ok) {
+    auto fetch = [&](float (&x)[D], unsigned& w, const float* px, const uint32_t* pw, bool ok) {
         if (ok) {
-            ldg_row<D>(x, pf);
+            ldg_row<D>(x, px);
             w = ldg_u32(pw);
         } else {
 #pragma unroll
             for (int j = 0; j < D; j++) x[j] = 0.0f;
             w = 0u;
         }
-        pf += kThreads * D;
-        pw += kThreads;
     };
+    {
+        const int64_t r0 = (int64_t)blockIdx.x * kBlockRows + tid;
 #pragma unroll
-    for (int q = 0; q < P; q++) fetch(xq[q], wq[q], (int64_t)blockIdx.x * kBlockRows + q * kThreads + tid < n);
+        for (int q = 0; q < P; q++)
+            fetch(xq[q], wq[q], a.X + (r0 + q * kThreads) * D, a.brows + r0 + q * kThreads, r0 + q * kThreads < n);
+    }
     // the center of the row in flight's stored label (a label past the end is masked: inside the 32-row table)
     float cr[D];
     load_row<D>(cr, st.cs_s + (wq[0] & MASK) * (unsigned)(D * 4));
-    constexpr int kJump = kRowsPerLane - P;             // step whose refill is the next block's first row
 
     int* queue = queue_all + warp * kQueue;
     int qhead = 0, qcount = 0;
@@ -809,9 +812,18 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
             qcount -= cnt;
         };
 
+        const float* xblk = a.X + base * D;
+        const uint32_t* wblk = a.brows + base;
         auto steps = [&](auto check) {
             constexpr bool CHECK = decltype(check)::value;
-            for (int ch = 0; ch < kRowsPerLane / U; ch++) {
+            for (int ch = 0; ch < NCH; ch++) {
+                // this chunk's rows and the next chunk's (the next block's first chunk after the last)
+                const bool last = ch == NCH - 1;
+                const float* xc = xblk + (int64_t)ch * U * XSTEP;
+                const uint32_t* wc = wblk + ch * U * kThreads;
+                const float* xn = last ? a.X + next * D : xc + U * XSTEP;
+                const uint32_t* wn = last ? a.brows + next : wc + U * kThreads;
+                const int64_t nrow = last ? next : base + (int64_t)(ch + 1) * U * kThreads;
 #pragma unroll
                 for (int s = 0; s < U; s++) {
                     const int r = ch * U + s;
@@ -841,14 +853,13 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
                         qcount += __popc(fm);
                         if (qcount >= 32) flush(32);
                     }
-                    if (s == kJump % U && ch == kJump / U) {
-                        pf = a.X + next * D;
-                        pw = a.brows + next;
-                    }
-                    // the refill is row r + P of this block or, past its end, of the next one
-                    const int64_t frow = r + P < kRowsPerLane ? blk0 + rofs + P * kThreads
-                                                              : next + (r + P - kRowsPerLane) * kThreads;
-                    fetch(xq[q], wq[q], !CHECK || frow < n);
+                    // the refill: row r + P, in this chunk or the next
+                    if (s + P < U)                       // resolved at compile time: the loop is unrolled
+                        fetch(xq[q], wq[q], xc + (s + P) * XSTEP, wc + (s + P) * kThreads,
+                              !CHECK || base + (int64_t)(r + P) * kThreads < n);
+                    else
+                        fetch(xq[q], wq[q], xn + (s + P - U) * XSTEP, wn + (s + P - U) * kThreads,
+                              !CHECK || nrow + (int64_t)(s + P - U) * kThreads < n);
                     if (s % 8 == 7) st.chunk_done();
                 }
             }
@@ -869,9 +880,27 @@ template <typename Kern>
 cudaError_t launch_grid(Kern kern, size_t smem, unsigned long long& configured, PassArgs a, cudaStream_t st) {
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!(configured >> (dev & 63) & 1ull)) {   // one bit per device: the attribute is per device
+    if (!(configured >> (dev & 63) & 1ull)) {   // one bit per device: the attributes are per device
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
+        // Shared memory and L1 split one 256 KB array per SM.  Left to itself the driver may give shared memory
+        // all of it (room for more CTAs than the registers allow), which leaves L1 too small to hold the global
+        // loads in flight and caps a streaming kernel well below HBM bandwidth.  Ask for the smallest carveout
+        // that still fits the CTAs the kernel can run, and give the rest to L1.
+        int want = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&want, kern, kThreads, smem);
+        if (e != cudaSuccess) return e;
+        if (want >= 1) {
+            int pct = (int)((100 * (size_t)want * (smem + 1024) + 233471) / 233472);
+            for (; pct <= 100; pct++) {
+                e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, pct);
+                if (e != cudaSuccess) return e;
+                int got = 0;
+                e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&got, kern, kThreads, smem);
+                if (e != cudaSuccess) return e;
+                if (got >= want) break;
+            }
+        }
         configured |= 1ull << (dev & 63);
     }
     int per_sm = 0;
