@@ -234,8 +234,11 @@ def main():
     stats = torch.zeros((K, _lib.STATS_BYTES), dtype=torch.uint8, device=dev)
     Cs = [C.clone(), torch.empty_like(C)]
     # per-row bounds carried over from the warm-up steps (the fit's own state)
-    bounded = not args.no_bounds and not args.generic
+    tc = ds.tensor_cores and not args.generic       # d >= 32: the tensor-core pass (kmc_pass_split)
+    bounded = not args.no_bounds and not args.generic and not tc
     bb, bbytes = ds.bounds(k)[0] if bounded else (None, 0)
+    if tc:
+        (spl, splb), (csp, cspb) = ds.split()[0], ds.csplit(k)
     flags = _lib.KMC_PASS_GENERIC if args.generic else 0
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -251,7 +254,11 @@ def main():
     for i in range(K):
         Cin, Cout = Cs[i % 2], Cs[(i + 1) % 2]
         ev[i][0].record(st)
-        if bounded:
+        if tc:
+            _lib.check(L.kmc_pass_split(X.data_ptr(), X.shape[0], d, Cin.data_ptr(), k, cm.data_ptr(), n_total,
+                                        b["totals"].data_ptr(), None, None, flags, spl.data_ptr(), splb,
+                                        csp.data_ptr(), cspb, b["ws"].data_ptr(), b["wsb"], sp))
+        elif bounded:
             _lib.check(L.kmc_pass_bounded(X.data_ptr(), X.shape[0], d, Cin.data_ptr(), k, cm.data_ptr(), n_total,
                                           b["totals"].data_ptr(), flags, bb.data_ptr(), bbytes, b["ws"].data_ptr(),
                                           b["wsb"], sp))
@@ -313,7 +320,13 @@ def main():
 
     pk, src = peaks()
     bytes_per_launch = (hi - lo) * d * 4
+    flops_per_launch = 2.0 * (hi - lo) * k * d
     achieved = bytes_per_launch / (pass_ms * 1e-3) / 1e9
+    # the roofline is the slower of one read of X at HBM bandwidth and the distance GEMM at tensor peak (the
+    # sustained bf16 figure: the pass runs in a long loop); the split pass issues three bf16 MMAs per product,
+    # so its own ceiling is a third of that peak
+    tpeak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+    tensor_bound = tc and flops_per_launch / (tpeak * 1e12) > bytes_per_launch / (pk["hbm_gbs"] * 1e9)
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
@@ -334,13 +347,20 @@ def main():
                    "rows_rescored_in_float64_per_pass": rescored,
                    "per_row_bounds": bounded,
                    "fraction_of_rows_compared_with_every_center": screened if bounded else 1.0,
-                   "kernel": "generic" if args.generic else "auto"},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
-                     "kernel_ms": pass_ms, "algorithmic_bytes_per_launch": bytes_per_launch,
-                     "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)" if src == "measured" else "fallback"},
+                   "kernel": "generic" if args.generic else ("tensor cores (kmc_pass_split)" if tc else "auto")},
+        "roofline": ({"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                      "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
+                      "kernel_ms": pass_ms, "algorithmic_bytes_per_launch": bytes_per_launch,
+                      "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)" if src == "measured" else "fallback"}
+                     if not tensor_bound else
+                     {"bound": "tensor", "achieved": flops_per_launch / (pass_ms * 1e-3) / 1e12, "peak": tpeak,
+                      "unit": "TFLOP/s", "frac": flops_per_launch / (pass_ms * 1e-3) / 1e12 / tpeak,
+                      "frac_of_split_ceiling": 3 * flops_per_launch / (pass_ms * 1e-3) / 1e12 / tpeak,
+                      "traffic": traffic, "kernel_ms": pass_ms, "algorithmic_flops_per_launch": flops_per_launch,
+                      "peak_source": (f"{src} bf16_tflops_sustained (MEASURED_PEAKS.json)" if src == "measured"
+                                      else "fallback")}),
         "clocks": clk,
-        "gpu_launches": 3 * K,
+        "gpu_launches": (5 if tc else 4 if bounded else 3) * K,   # prepare (+ split or bounds), pass, finish
         "e2e": e2e,
     }
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -111,6 +111,21 @@ int kmc_pass_bounded(const float *X, int64_t n, int d, const float *C, int k, co
                      int64_t n_total, int64_t *totals, unsigned flags, void *bounds, size_t bounds_size,
                      void *workspace, size_t ws_bytes, void *stream);
 
+/* Tensor-core pass for high d (the reference's tiles / tiles1 paths, core.py:289-377 and 675-844).  x.c is
+ * computed on the tcgen05 tensor cores from bf16 hi/lo splits of x and c (three MMAs per product); a row whose
+ * two best centers are closer than the proven error window is decided in float64, so labels, best and totals
+ * are those of kmc_pass.  The row split is per dataset slice: kmc_split_bytes(n, d) bytes filled once by
+ * kmc_split_rows (bf16 copies of X, row norms, and the per-row label scratch of the pass); the center split,
+ * kmc_csplit_bytes(d, k) bytes, is refilled by every pass.  Any d is accepted; it pays off from d = 32 up.
+ * Arguments, outputs and errors otherwise as kmc_pass. */
+size_t kmc_split_bytes(int64_t n, int d);
+int kmc_split_rows(const float *X, int64_t n, int d, void *split, size_t split_bytes, void *stream);
+size_t kmc_csplit_bytes(int d, int k);
+int kmc_pass_split(const float *X, int64_t n, int d, const float *C, int k, const uint32_t *colmax,
+                   int64_t n_total, int64_t *totals, int32_t *labels, float *best, unsigned flags, void *split,
+                   size_t split_bytes, void *csplit, size_t csplit_bytes, void *workspace, size_t ws_bytes,
+                   void *stream);
+
 /* kmc_pass without a caller workspace.  No counterpart in the reference: it exists for callers that cannot
  * allocate device memory -- a host runtime that owns every device allocation through its own pool, or a
  * phase of a program in which calling an allocator is not allowed -- and so cannot provide the workspace

@@ -37,6 +37,11 @@ SIGNATURES = {
     "kmc_bounds_bytes": (_sz, [_i64, _int, _int]),
     "kmc_bounds_reset": (_int, [_vp, _vp]),
     "kmc_pass_bounded": (_int, [_vp, _i64, _int, _vp, _int, _vp, _i64, _vp, _u, _vp, _sz, _vp, _sz, _vp]),
+    "kmc_split_bytes": (_sz, [_i64, _int]),
+    "kmc_split_rows": (_int, [_vp, _i64, _int, _vp, _sz, _vp]),
+    "kmc_csplit_bytes": (_sz, [_int, _int]),
+    "kmc_pass_split": (_int, [_vp, _i64, _int, _vp, _int, _vp, _i64, _vp, _vp, _vp, _u, _vp, _sz, _vp, _sz, _vp, _sz,
+                              _vp]),
     "kmc_far_rows": (_int, [_vp, _i64, _int, _vp, _vp, _i64, _i64, _vp, _vp, _sz, _vp]),
     "kmc_finish": (_int, [_vp, _int, _int, _vp, _i64, _int, _vp, _vp, _vp, _sz, _vp]),
     "kmc_stats_read": (_int, [_vp, _vp, _vp]),

@@ -80,7 +80,9 @@ class Dataset:
     contiguous block of rows starting at global row `row0`); None on one GPU.
     """
 
-    def __init__(self, parts, group=None, device=None):
+    TC_MIN_DIMS = 32                # from here up the assign runs on the tensor cores (kmc_pass_split)
+
+    def __init__(self, parts, group=None, device=None, tensor_cores=None):
         if isinstance(parts, (torch.Tensor, np.ndarray)) or not isinstance(parts, (list, tuple)):
             parts = [parts]
         if not parts:
@@ -112,6 +114,10 @@ class Dataset:
         self._ws = {}
         self._colmax = None
         self._bounds = {}
+        # tensor_cores: None = by dims (d >= TC_MIN_DIMS), True / False to force
+        self.tensor_cores = (d >= self.TC_MIN_DIMS) if tensor_cores is None else bool(tensor_cores)
+        self._split = None
+        self._csplit = {}
 
     # -- per-dataset state
     @property
@@ -170,6 +176,27 @@ class Dataset:
             self._bounds[k] = bb
         return bb
 
+    # -- tensor-core operands: bf16 hi / lo copies of the rows (once per dataset), the centers' (per k)
+    def split(self):
+        if self._split is None:
+            L = _lib.load()
+            sp = []
+            for p in self.parts:
+                nb = int(L.kmc_split_bytes(p.shape[0], self.d))
+                t = torch.empty(nb, dtype=torch.uint8, device=self.device)
+                _lib.call("kmc_split_rows", _ptr(p), p.shape[0], self.d, _ptr(t), nb, _stream())
+                sp.append((t, nb))
+            self._split = sp
+        return self._split
+
+    def csplit(self, k):
+        cs = self._csplit.get(k)
+        if cs is None:
+            nb = int(_lib.load().kmc_csplit_bytes(self.d, k))
+            cs = (torch.empty(nb, dtype=torch.uint8, device=self.device), nb)
+            self._csplit[k] = cs
+        return cs
+
     def reset_bounds(self):
         """Forget the per-row bounds: the next bounded pass compares every row with every center."""
         for bb in self._bounds.values():
@@ -187,8 +214,16 @@ class Dataset:
         flags = _lib.KMC_PASS_GENERIC if generic else 0
         st = _stream()
         bb = self.bounds(k) if bounded and not labels and not generic else None
+        tc = self.tensor_cores and not generic
+        if tc:
+            bb = None
+            sp, cs = self.split(), self.csplit(k)
         for i, p in enumerate(self.parts):
-            if bb is not None:
+            if tc:
+                _lib.call("kmc_pass_split", _ptr(p), p.shape[0], self.d, _ptr(C), k, _ptr(cm), self.n_total,
+                          _ptr(b["totals"]), _ptr(lab[i]) if labels else None, _ptr(bst[i]) if labels else None,
+                          flags, _ptr(sp[i][0]), sp[i][1], _ptr(cs[0]), cs[1], _ptr(b["ws"]), b["wsb"], st)
+            elif bb is not None:
                 _lib.call("kmc_pass_bounded", _ptr(p), p.shape[0], self.d, _ptr(C), k, _ptr(cm), self.n_total,
                           _ptr(b["totals"]), flags, _ptr(bb[i][0]), bb[i][1], _ptr(b["ws"]), b["wsb"], st)
             else:

@@ -213,6 +213,90 @@ int kmc_pass_bounded(const float* X, int64_t n, int d, const float* C, int k, co
                      ws_bytes, bounds, stream);
 }
 
+size_t kmc_split_bytes(int64_t n, int d) { return split_rows_bytes(n, d); }
+
+size_t kmc_csplit_bytes(int d, int k) { return split_centers_bytes(d, k); }
+
+int kmc_split_rows(const float* X, int64_t n, int d, void* split, size_t split_bytes, void* stream) {
+    if (int s = check_shape(n, d, 1)) return s;
+    if (!split || (n > 0 && !X)) return fail(KMC_ERR_INVALID, "kmc_split_rows: null pointer");
+    if (split_bytes < split_rows_bytes(n, d))
+        return fail(KMC_ERR_INVALID, "kmc_split_rows: split of %zu bytes, need %zu", split_bytes,
+                    split_rows_bytes(n, d));
+    cudaError_t e = launch_split_rows(X, n, d, carve_rows(split, n, d), static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_split_rows");
+    return KMC_OK;
+}
+
+int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, const uint32_t* colmax,
+                   int64_t n_total, int64_t* totals, int32_t* labels, float* best, unsigned flags, void* split,
+                   size_t split_bytes, void* csplit, size_t csplit_bytes, void* workspace, size_t ws_bytes,
+                   void* stream) {
+    const char* who = "kmc_pass_split";
+    if (int s = check_shape(n, d, k)) return s;
+    if (!C || !colmax || !totals || !workspace || !split || !csplit || (n > 0 && !X))
+        return fail(KMC_ERR_INVALID, "%s: null pointer", who);
+    if (n_total < n) return fail(KMC_ERR_INVALID, "%s: n_total %lld < n %lld", who, (long long)n_total, (long long)n);
+    Workspace ws = carve(workspace, d, k);
+    if (ws_bytes < ws.bytes) return fail(KMC_ERR_INVALID, "%s: workspace of %zu bytes, need %zu", who, ws_bytes, ws.bytes);
+    if (split_bytes < split_rows_bytes(n, d))
+        return fail(KMC_ERR_INVALID, "%s: split of %zu bytes, need %zu", who, split_bytes, split_rows_bytes(n, d));
+    if (csplit_bytes < split_centers_bytes(d, k))
+        return fail(KMC_ERR_INVALID, "%s: center split of %zu bytes, need %zu", who, csplit_bytes,
+                    split_centers_bytes(d, k));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    if (!(flags & KMC_PASS_ACCUMULATE)) {
+        e = cudaMemsetAsync(totals, 0, sizeof(int64_t) * (size_t)k * (d + 2), st);
+        if (e != cudaSuccess) return cuda_fail(e, who);
+        e = cudaMemsetAsync(ws.counters, 0, sizeof(long long) * 8, st);
+        if (e != cudaSuccess) return cuda_fail(e, who);
+    }
+    e = launch_prepare(C, k, d, colmax, n_total, ws.prep, ws.scale_x, ws.hc, st);
+    if (e != cudaSuccess) return cuda_fail(e, who);
+    if (n == 0) return KMC_OK;
+    const RowSplit rs = carve_rows(split, n, d);
+    const CenterSplit cs = carve_centers(csplit, d, k);
+    e = launch_split_centers(C, k, d, cs, st);
+    if (e != cudaSuccess) return cuda_fail(e, who);
+    TcSplit ts;
+    ts.n = n;
+    ts.dp = split_dp(d);
+    ts.kp = split_kp(k);
+    ts.k = k;
+    ts.xh = rs.xh;
+    ts.xl = rs.xl;
+    ts.ch = cs.ch;
+    ts.cl = cs.cl;
+    ts.hs = cs.hs;
+    ts.xn = rs.xn;
+    ts.cmax = reinterpret_cast<const float*>(cs.cmax_bits);
+    ts.lab = rs.lab;
+    ts.error = cs.error;
+    e = launch_assign_tc(ts, st);
+    if (e != cudaSuccess) return cuda_fail(e, who);
+    PassArgs a;
+    a.X = X;
+    a.n = n;
+    a.d = d;
+    a.k = k;
+    a.C = C;
+    a.hc = ws.hc;
+    a.scale_x = ws.scale_x;
+    a.prep = ws.prep;
+    a.totals = reinterpret_cast<long long*>(totals);
+    a.labels = labels;
+    a.best = best;
+    a.counters = ws.counters;
+    a.smem_acc = 0;
+    a.ctile = 0;
+    a.key_keep = 0;
+    a.brows = nullptr;
+    e = launch_accum_split(a, rs.lab, cs.error, st);
+    if (e != cudaSuccess) return cuda_fail(e, who);
+    return KMC_OK;
+}
+
 int kmc_far_rows(const float* X, int64_t n, int d, const int32_t* labels, const float* best, int64_t row0,
                  int64_t cand_rows, uint32_t* cands, void* workspace, size_t ws_bytes, void* stream) {
     if (int s = check_shape(n, d, 1)) return s;

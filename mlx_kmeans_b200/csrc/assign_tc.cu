@@ -1,0 +1,385 @@
+// assign_tc.cu -- nearest center for d >= 32 on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Reference: the high-d exact assign of core.py:289-377 / 675-844 (a distance GEMM tile by tile with an online
+// per-row argmin, x.c computed in float32) and the rows kernel's label rule (core.py:263-274); built here for
+// B200 with split-precision operands and a proven error window, so the label is the float64-optimal one.
+//
+// Operands: x = xh + xl + ex and c = ch + cl + ec with xh = bf16(x), xl = bf16(x - xh), |ex| <= 2^-16 |x|
+// (elementwise; the same for c).  One pass of three bf16 MMAs, xh.ch + xh.cl + xl.ch, accumulated in float32
+// in TMEM, gives x.c to within E |x| |c| with E = 3.1 2^-16 (the dropped terms, Cauchy-Schwarz) plus the
+// float32 accumulation, bounded by 3 dp 2^-24 (a sequential float32 sum of 3 dp terms each at most |x| |c|
+// in total).  The score of center c is s_c = |c|^2/2 - x.c (half the distance less |x|^2/2).  A row whose two
+// best scores are closer than the window (both scores' errors plus the float64 rounding of D64) is flagged
+// (exact ties included); the accumulation kernel decides it in float64 (NumPy-pairwise D64, lowest index on
+// ties).
+//
+// Kernel layout (one CTA per SM, persistent over 128-row tiles):
+//   warp 0   TMA producer: per (row tile, center tile, 64-column chunk) one stage = xh, xl (128 x 64 bf16)
+//            and ch, cl (BN x 64 bf16), 128-byte swizzled, two stages in flight.
+//   warp 1   MMA issuer: 3 x 4 tcgen05.mma (M=128, N=BN, K=16) per stage into one of two TMEM accumulators;
+//            tcgen05.commit frees the stage and, after the last chunk, hands the accumulator to the epilogue.
+//   warps 2-5  epilogue: each thread owns one row (TMEM lane), reads its BN scores 32 columns at a time
+//            (tcgen05.ld), keeps the best and second-best score with the lowest index, and at the end of the
+//            row tile writes label | flag << 31.
+// Every wait on an mbarrier is bounded; on a timeout the CTA records an error, stops its loops and frees TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kmc_internal.h"
+
+namespace kmc {
+
+namespace {
+
+constexpr int BM = 128;                  // rows per tile (UMMA M)
+constexpr int BK = 64;                   // bf16 columns per chunk: one 128-byte swizzle row
+constexpr int kTcStages = 2;
+constexpr int kTcThreads = 192;          // producer warp, MMA warp, four epilogue warps
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+template <int BN>
+struct TcSmem {
+    static constexpr int A = BM * BK * 2;             // one 128 x 64 bf16 operand chunk (16 KB)
+    static constexpr int B = BN * BK * 2;             // one BN x 64 bf16 chunk
+    static constexpr int STAGE = 2 * A + 2 * B;       // hi and lo of each
+    static constexpr int BAR = 256;                   // barriers, TMEM address, abort flag
+    static constexpr int total = kTcStages * STAGE + BAR + 1024;   // + slack to align the stages to 1024 B
+    static_assert(A % 1024 == 0 && B % 1024 == 0, "swizzle atoms are 1024-byte aligned");
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Wait for the phase of parity `parity` to complete, at most kSpinLimit polls; false (and the abort flag set)
+// on a timeout or when another role already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+    for (uint32_t i = 0; i < kSpinLimit; i++) {
+        if (mbar_try(bar, parity)) return true;
+        if (*abort_flag) return false;
+    }
+    *abort_flag = 1;
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major operand in the 128-byte swizzle layout TMA writes: rows of 128 B, 8-row atoms of 1024 B.  Fields:
+// start address >> 4 [0,14), leading byte offset >> 4 [16,30) (1, unused by swizzled K-major), stride byte
+// offset >> 4 [32,46) (1024 B between 8-row groups), descriptor version 1 [46,48), swizzle mode 2 [61,64).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// kind::f16 instruction descriptor: f32 accumulator [4,6), bf16 A [7,10) and B [10,13), both K-major,
+// N >> 3 at [17,23), M >> 4 at [24,29)
+template <int BN>
+constexpr uint32_t idesc_bf16() {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// 32 consecutive float32 columns of this thread's TMEM lane (the load and its wait in one statement, so no
+// use of the registers can be scheduled between them)
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+}
+
+struct TcArgs {
+    int64_t n;
+    int dp;                  // padded dims (multiple of 64)
+    int kp;                  // padded centers (multiple of BN)
+    int k;
+    const float* hs;         // kp: |c|^2 / 2 (padding centers: 2^126)
+    const float* xn;         // n: |x| rounded up
+    const float* cmax;       // max |c| rounded up (one value)
+    int32_t* lab;            // n: label | flag << 31
+    int* error;              // set on a barrier timeout
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    k_assign_tc(const __grid_constant__ CUtensorMap mxh, const __grid_constant__ CUtensorMap mxl,
+                const __grid_constant__ CUtensorMap mch, const __grid_constant__ CUtensorMap mcl, TcArgs a) {
+    using S = TcSmem<BN>;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // stages at the first 1024-byte boundary, then the barrier block
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char* gbase = smem_raw + (base - raw);
+    const uint32_t bars = base + kTcStages * S::STAGE;
+    unsigned char* gbars = gbase + kTcStages * S::STAGE;
+    // barrier block: full[2] empty[2] accf[2] acce[2] (8 B each), TMEM base (4 B), abort flag (4 B)
+    auto full = [&](int s) { return bars + 8u * s; };
+    auto empty = [&](int s) { return bars + 16u + 8u * s; };
+    auto accf = [&](int b) { return bars + 32u + 8u * b; };
+    auto acce = [&](int b) { return bars + 48u + 8u * b; };
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbars + 64);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(gbars + 68);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t tiles = (a.n + BM - 1) / BM;
+    const int ntiles = a.kp / BN, kchunks = a.dp / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kTcStages; s++) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(accf(b), 1);
+            mbar_init(acce(b), 4 * 32);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {   // two accumulators of BN float32 columns each
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(2 * BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---- TMA producer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x)
+                for (int nt = 0; nt < ntiles && ok; nt++)
+                    for (int kc = 0; kc < kchunks && ok; kc++) {
+                        ok = mbar_wait(empty(stage), phase ^ 1u, abort_flag);
+                        if (!ok) break;
+                        const uint32_t st = base + stage * S::STAGE;
+                        mbar_expect_tx(full(stage), S::STAGE);
+                        tma_load_2d(st, &mxh, kc * BK, (int)(t * BM), full(stage));
+                        tma_load_2d(st + S::A, &mxl, kc * BK, (int)(t * BM), full(stage));
+                        tma_load_2d(st + 2 * S::A, &mch, kc * BK, nt * BN, full(stage));
+                        tma_load_2d(st + 2 * S::A + S::B, &mcl, kc * BK, nt * BN, full(stage));
+                        if (++stage == kTcStages) { stage = 0; phase ^= 1u; }
+                    }
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16<BN>();
+            int stage = 0;
+            uint32_t phase = 0, abuf = 0, aphase = 0;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x)
+                for (int nt = 0; nt < ntiles && ok; nt++) {
+                    ok = mbar_wait(acce(abuf), aphase ^ 1u, abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem + abuf * BN;
+                    for (int kc = 0; kc < kchunks && ok; kc++) {
+                        ok = mbar_wait(full(stage), phase, abort_flag);
+                        if (!ok) break;
+                        tc_fence_after();
+                        const uint32_t st = base + stage * S::STAGE;
+                        const uint64_t ah = sw128_desc(st), al = sw128_desc(st + S::A);
+                        const uint64_t bh = sw128_desc(st + 2 * S::A), bl = sw128_desc(st + 2 * S::A + S::B);
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; kk++) {
+                            const uint64_t off = (uint64_t)((kk * 32) >> 4);   // 16 bf16 = 32 B along K
+                            mma_bf16(d_tmem, ah + off, bh + off, idesc, (kc | kk) != 0);
+                            mma_bf16(d_tmem, ah + off, bl + off, idesc, 1u);
+                            mma_bf16(d_tmem, al + off, bh + off, idesc, 1u);
+                        }
+                        mma_commit(empty(stage));          // the stage is free once these MMAs are done
+                        if (++stage == kTcStages) { stage = 0; phase ^= 1u; }
+                    }
+                    if (!ok) break;
+                    mma_commit(accf(abuf));                // the accumulator is ready for the epilogue
+                    abuf ^= 1u;
+                    if (abuf == 0) aphase ^= 1u;
+                }
+        }
+    } else {
+        // ---- epilogue: thread = one row of the tile (TMEM lane 32 * (warp % 4) + lane)
+        const int q = warp & 3;
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+        const float cmax = *a.cmax;
+        // Window on the gap between the two best scores: each score is off by at most E |x| |c| (the dropped
+        // split terms and the float32 accumulation) plus 2^-24 (|c|^2 + |x| |c|) (rounding of |c|^2/2 and of
+        // the subtraction); two of them, with |c| <= cmax, and a 2^-10 margin for the float32 evaluation of the
+        // window itself.  The float64 rounding of D64, which defines the label, adds 2^-40 (|x| + cmax)^2.
+        const float E2 = (float)(2.0 * (3.1 / 65536.0 + 3.0 * a.dp / 16777216.0));
+        uint32_t abuf = 0, aphase = 0;
+        bool ok = true;
+        for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            float m1 = INFINITY, m2 = INFINITY;
+            int l1 = 0;
+            for (int nt = 0; nt < ntiles && ok; nt++) {
+                ok = mbar_wait(accf(abuf), aphase, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll 1
+                for (int cc = 0; cc < BN; cc += 32) {
+                    float v[32];
+                    tmem_ld32(lane_base + abuf * BN + cc, v);
+                    const int c0 = nt * BN + cc;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const float s = __ldg(a.hs + c0 + j) - v[j];
+                        if (s < m1) { m2 = m1; m1 = s; l1 = c0 + j; }
+                        else if (s < m2) m2 = s;
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(acce(abuf));
+                abuf ^= 1u;
+                if (abuf == 0) aphase ^= 1u;
+            }
+            if (!ok) break;
+            const int64_t row = t * BM + 32 * q + lane;
+            if (row < a.n) {
+                const float xr = __ldg(a.xn + row), r = xr + cmax;
+                const float win = (E2 * xr * cmax + cmax * (cmax + xr) * (1.0f / 8388608.0f)) * (1.0f + 1.0f / 1024.0f) +
+                                  r * r * (1.0f / 1099511627776.0f);
+                const bool flag = !(m2 - m1 > win) || l1 >= a.k;
+                a.lab[row] = (int32_t)((uint32_t)l1 | (flag ? 0x80000000u : 0u));
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
+    }
+    if (threadIdx.x == 0 && *abort_flag) atomicExch(a.error, 1);
+}
+
+// ---------------------------------------------------------------- host side: tensor maps and launch
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// rows x dp bf16, row-major; box of `box_rows` rows x 64 columns, 128-byte swizzle, zero fill past the end
+bool make_map(CUtensorMap* m, const void* base, int64_t rows, int dp, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)dp, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)dp * 2};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int BN>
+cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
+    CUtensorMap mxh, mxl, mch, mcl;
+    if (!make_map(&mxh, s.xh, s.n, s.dp, BM) || !make_map(&mxl, s.xl, s.n, s.dp, BM) ||
+        !make_map(&mch, s.ch, s.kp, s.dp, BN) || !make_map(&mcl, s.cl, s.kp, s.dp, BN))
+        return cudaErrorInvalidValue;
+    static unsigned long long configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const size_t smem = TcSmem<BN>::total;
+    if (!(configured >> (dev & 63) & 1ull)) {
+        cudaError_t e = cudaFuncSetAttribute(k_assign_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        configured |= 1ull << (dev & 63);
+    }
+    TcArgs a;
+    a.n = s.n;
+    a.dp = s.dp;
+    a.kp = s.kp;
+    a.k = s.k;
+    a.hs = s.hs;
+    a.xn = s.xn;
+    a.cmax = s.cmax;
+    a.lab = s.lab;
+    a.error = s.error;
+    const int64_t tiles = (s.n + BM - 1) / BM;
+    int64_t grid = num_sms();
+    if (grid > tiles) grid = tiles;
+    if (grid < 1) grid = 1;
+    k_assign_tc<BN><<<(int)grid, kTcThreads, smem, st>>>(mxh, mxl, mch, mcl, a);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+int tc_block_n(int k) { return k <= 64 ? 64 : k <= 128 ? 128 : 256; }
+
+cudaError_t launch_assign_tc(const TcSplit& s, cudaStream_t st) {
+    switch (tc_block_n(s.k)) {
+        case 64: return run_tc<64>(s, st);
+        case 128: return run_tc<128>(s, st);
+        default: return run_tc<256>(s, st);
+    }
+}
+
+}  // namespace kmc

@@ -71,6 +71,43 @@ cudaError_t launch_bounds_prepare(const float* C, int k, int d, double* meta, fl
 cudaError_t launch_pass_lowd(PassArgs a, cudaStream_t st);
 int64_t lowd_block_rows();
 
+// Tensor-core pass (d >= 32): per-slice operands, computed once per dataset ...
+struct RowSplit {
+    void* xh;                 // n x dp bf16, x rounded to bf16
+    void* xl;                 // n x dp bf16, the rest rounded to bf16
+    float* xn;                // n: |x| rounded up
+    int32_t* lab;             // n: label | flag << 31 from the tensor-core kernel
+};
+// ... and per-pass center operands
+struct CenterSplit {
+    unsigned int* cmax_bits;  // max |c| rounded up (float bits)
+    int* error;               // set when the tensor-core kernel timed out on a barrier
+    void* ch;                 // kp x dp bf16
+    void* cl;                 // kp x dp bf16
+    float* hs;                // kp: |c|^2 / 2 (padding centers 2^126)
+};
+struct TcSplit {
+    int64_t n;
+    int dp, kp, k;
+    const void *xh, *xl, *ch, *cl;
+    const float* hs;
+    const float* xn;
+    const float* cmax;
+    int32_t* lab;
+    int* error;
+};
+int split_dp(int d);
+int split_kp(int k);
+int tc_block_n(int k);
+size_t split_rows_bytes(int64_t n, int d);
+size_t split_centers_bytes(int d, int k);
+RowSplit carve_rows(void* base, int64_t n, int d);
+CenterSplit carve_centers(void* base, int d, int k);
+cudaError_t launch_split_rows(const float* X, int64_t n, int d, const RowSplit& s, cudaStream_t st);
+cudaError_t launch_split_centers(const float* C, int k, int d, const CenterSplit& s, cudaStream_t st);
+cudaError_t launch_assign_tc(const TcSplit& s, cudaStream_t st);
+cudaError_t launch_accum_split(PassArgs a, const int32_t* lab, const int* tc_error, cudaStream_t st);
+
 cudaError_t launch_far_rows(const float* X, int64_t n, int d, const int32_t* labels, const float* best, int64_t row0,
                             int64_t cand_rows, uint32_t* cands, const FarWorkspace& ws, cudaStream_t st);
 cudaError_t launch_finish(long long* totals, int k, int d, const uint32_t* cands, int64_t cand_rows, int ranks,
