@@ -113,10 +113,12 @@ int kmc_pass_bounded(const float *X, int64_t n, int d, const float *C, int k, co
 
 /* Tensor-core pass for high d (the reference's tiles / tiles1 paths, core.py:289-377 and 675-844).  x.c is
  * computed on the tcgen05 tensor cores from bf16 hi/lo splits of x and c (three MMAs per product); a row whose
- * two best centers are closer than the proven error window is decided in float64, so labels, best and totals
- * are those of kmc_pass.  The row split is per dataset slice: kmc_split_bytes(n, d) bytes filled once by
- * kmc_split_rows (bf16 copies of X, row norms, and the per-row label scratch of the pass); the center split,
- * kmc_csplit_bytes(d, k) bytes, is refilled by every pass.  Any d is accepted; it pays off from d = 32 up.
+ * two best centers are closer than the proven error window is decided in float64, so labels, best, counts and
+ * sums are those of kmc_pass; the inertia column sums each row's float64 distance (kmc_pass: the float32
+ * `best`), the same to about 1e-7.  The rows are then grouped by label and summed per cluster.  The row split
+ * is per dataset slice: kmc_split_bytes(n, d) bytes filled once by kmc_split_rows (bf16 copies of X, row
+ * norms, and per-row scratch of the pass); the center split, kmc_csplit_bytes(d, k) bytes, is refilled by
+ * every pass.  One call takes at most 2^32 - 1 rows.  Any d is accepted; it pays off from d = 32 up.
  * Arguments, outputs and errors otherwise as kmc_pass. */
 size_t kmc_split_bytes(int64_t n, int d);
 int kmc_split_rows(const float *X, int64_t n, int d, void *split, size_t split_bytes, void *stream);

@@ -237,6 +237,8 @@ int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, cons
     if (!C || !colmax || !totals || !workspace || !split || !csplit || (n > 0 && !X))
         return fail(KMC_ERR_INVALID, "%s: null pointer", who);
     if (n_total < n) return fail(KMC_ERR_INVALID, "%s: n_total %lld < n %lld", who, (long long)n_total, (long long)n);
+    if (n > (int64_t)UINT32_MAX)
+        return fail(KMC_ERR_INVALID, "%s: %lld rows in one call, at most 2^32 - 1", who, (long long)n);
     Workspace ws = carve(workspace, d, k);
     if (ws_bytes < ws.bytes) return fail(KMC_ERR_INVALID, "%s: workspace of %zu bytes, need %zu", who, ws_bytes, ws.bytes);
     if (split_bytes < split_rows_bytes(n, d))
@@ -272,6 +274,8 @@ int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, cons
     ts.xn = rs.xn;
     ts.cmax = reinterpret_cast<const float*>(cs.cmax_bits);
     ts.lab = rs.lab;
+    ts.flagged = rs.perm;                  // the list of flagged rows, until the rows are grouped by label
+    ts.nflag = cs.nflag;
     ts.error = cs.error;
     e = launch_assign_tc(ts, st);
     if (e != cudaSuccess) return cuda_fail(e, who);
@@ -292,7 +296,7 @@ int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, cons
     a.ctile = 0;
     a.key_keep = 0;
     a.brows = nullptr;
-    e = launch_accum_split(a, rs.lab, cs.error, st);
+    e = launch_accum_split(a, rs, cs, st);
     if (e != cudaSuccess) return cuda_fail(e, who);
     return KMC_OK;
 }

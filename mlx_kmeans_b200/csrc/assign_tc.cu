@@ -145,6 +145,8 @@ struct TcArgs {
     const float* xn;         // n: |x| rounded up
     const float* cmax;       // max |c| rounded up (one value)
     int32_t* lab;            // n: label | flag << 31
+    uint32_t* flagged;       // rows to decide in float64
+    unsigned int* nflag;     // their number (zeroed by the caller)
     int* error;              // set on a barrier timeout
 };
 
@@ -288,12 +290,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             if (!ok) break;
             const int64_t row = t * BM + 32 * q + lane;
+            bool flag = false;
             if (row < a.n) {
                 const float xr = __ldg(a.xn + row), r = xr + cmax;
                 const float win = (E2 * xr * cmax + cmax * (cmax + xr) * (1.0f / 8388608.0f)) * (1.0f + 1.0f / 1024.0f) +
                                   r * r * (1.0f / 1099511627776.0f);
-                const bool flag = !(m2 - m1 > win) || l1 >= a.k;
+                flag = !(m2 - m1 > win) || l1 >= a.k;
                 a.lab[row] = (int32_t)((uint32_t)l1 | (flag ? 0x80000000u : 0u));
+            }
+            // flagged rows join the list the float64 decision works through (one atomic per warp)
+            const unsigned fm = __ballot_sync(0xffffffffu, flag);
+            if (fm) {
+                const int leader = __ffs(fm) - 1;
+                unsigned at = 0;
+                if (lane == leader) at = atomicAdd(a.nflag, (unsigned)__popc(fm));
+                at = __shfl_sync(0xffffffffu, at, leader);
+                if (flag) a.flagged[at + __popc(fm & ((1u << lane) - 1u))] = (uint32_t)row;
             }
         }
     }
@@ -361,6 +373,8 @@ cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
     a.xn = s.xn;
     a.cmax = s.cmax;
     a.lab = s.lab;
+    a.flagged = s.flagged;
+    a.nflag = s.nflag;
     a.error = s.error;
     const int64_t tiles = (s.n + BM - 1) / BM;
     int64_t grid = num_sms();

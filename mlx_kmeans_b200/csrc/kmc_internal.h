@@ -76,15 +76,20 @@ struct RowSplit {
     void* xh;                 // n x dp bf16, x rounded to bf16
     void* xl;                 // n x dp bf16, the rest rounded to bf16
     float* xn;                // n: |x| rounded up
-    int32_t* lab;             // n: label | flag << 31 from the tensor-core kernel
+    int32_t* lab;             // n: label | flag << 31 from the tensor-core kernel, then the final label
+    uint32_t* perm;           // n: rows grouped by label
 };
 // ... and per-pass center operands
 struct CenterSplit {
     unsigned int* cmax_bits;  // max |c| rounded up (float bits)
     int* error;               // set when the tensor-core kernel timed out on a barrier
+    unsigned int* nflag;      // rows the tensor-core kernel left to float64 (listed in RowSplit::perm)
+    float* ct;                // d x k: the centers transposed, for the float64 decision's float32 screen
     void* ch;                 // kp x dp bf16
     void* cl;                 // kp x dp bf16
     float* hs;                // kp: |c|^2 / 2 (padding centers 2^126)
+    unsigned int* hist;       // k: rows per label
+    unsigned int* cursor;     // k: next slot of each label in the grouped rows
 };
 struct TcSplit {
     int64_t n;
@@ -94,6 +99,8 @@ struct TcSplit {
     const float* xn;
     const float* cmax;
     int32_t* lab;
+    uint32_t* flagged;
+    unsigned int* nflag;
     int* error;
 };
 int split_dp(int d);
@@ -106,7 +113,7 @@ CenterSplit carve_centers(void* base, int d, int k);
 cudaError_t launch_split_rows(const float* X, int64_t n, int d, const RowSplit& s, cudaStream_t st);
 cudaError_t launch_split_centers(const float* C, int k, int d, const CenterSplit& s, cudaStream_t st);
 cudaError_t launch_assign_tc(const TcSplit& s, cudaStream_t st);
-cudaError_t launch_accum_split(PassArgs a, const int32_t* lab, const int* tc_error, cudaStream_t st);
+cudaError_t launch_accum_split(PassArgs a, const RowSplit& rs, const CenterSplit& cs, cudaStream_t st);
 
 cudaError_t launch_far_rows(const float* X, int64_t n, int d, const int32_t* labels, const float* best, int64_t row0,
                             int64_t cand_rows, uint32_t* cands, const FarWorkspace& ws, cudaStream_t st);

@@ -4,13 +4,18 @@
 //                    multiple of 64 with zeros) and |x| rounded up, for assign_tc.cu
 //   k_split_centers  once per pass: the same split of the centers (rows padded to the MMA tile), |c|^2/2 and
 //                    max |c| (rounded up)
-//   k_accum_split    per row: the label from assign_tc.cu (rows it flagged are decided here in float64,
-//                    NumPy-pairwise D64 over all centers, lowest index on ties, one warp per flagged row),
-//                    `best` (the reference's float32 distance), and the row's totals quantised on its own
-//                    into int64 (shared-memory slots when k (d + 2) fits, else the global totals)
+//   k_fix_labels     per row: the label from assign_tc.cu; rows it flagged are decided here in float64
+//                    (NumPy-pairwise D64 over all centers, lowest index on ties, one warp per flagged row); the
+//                    histogram of the labels; the optional labels / best outputs (best: the reference's
+//                    float32 distance, each operation rounded on its own, in column order)
+//   k_scan_labels, k_scatter_rows   the rows grouped by label (a counting sort)
+//   k_reduce_rows    one warp per run of 256 grouped rows: every value quantised on its own into int64
+//                    lane-private shared-memory sums, flushed to the global totals when the label changes, so the
+//                    totals are exact integers whatever the order (and equal to the CUDA-core pass's); inertia
+//                    from the float64 distance of each row (float64 per lane, fixed reduction tree)
 //
-// Reference: the high-d exact path of core.py:289-377 / 675-844 and its accumulation (core.py:1292-1441); the
-// label rule of core.py:263-274.
+// Reference: the high-d exact path of core.py:289-377 / 675-844, its sorted accumulation for large k
+// (core.py:1292-1441, mx.argsort grouping at 976-987), and the label rule of core.py:263-274.
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -56,7 +61,8 @@ __global__ void __launch_bounds__(kSplitThreads) k_split_centers(const float* __
                                                                 int dp, __nv_bfloat16* __restrict__ ch,
                                                                 __nv_bfloat16* __restrict__ cl,
                                                                 float* __restrict__ hs,
-                                                                unsigned int* __restrict__ cmax_bits) {
+                                                                unsigned int* __restrict__ cmax_bits,
+                                                                float* __restrict__ ct) {
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (kSplitThreads / 32);
     for (int c = blockIdx.x * (kSplitThreads / 32) + (threadIdx.x >> 5); c < kp; c += warps) {
@@ -68,6 +74,7 @@ __global__ void __launch_bounds__(kSplitThreads) k_split_centers(const float* __
             split_bf16(v, h, l);
             ch[(int64_t)c * dp + j] = h;
             cl[(int64_t)c * dp + j] = l;
+            if (real && j < d) ct[(int64_t)j * k + c] = v;
             s = __fma_rn((double)v, (double)v, s);
             su = __fma_ru((double)v, (double)v, su);
         }
@@ -83,20 +90,63 @@ __global__ void __launch_bounds__(kSplitThreads) k_split_centers(const float* __
     }
 }
 
-// Decide the warp's rows flagged in `fm` in float64 over all k centers (lanes split the centers, ascending per
-// lane, then a lowest-index reduction); returns the calling lane's label (`l` when its row is not flagged).
-__device__ __noinline__ int rescore_all(unsigned fm, const float* __restrict__ X, int64_t row, int d,
-                                        const float* __restrict__ C, int k, int lane, int l) {
-    while (fm) {
-        const int src = __ffs(fm) - 1;
-        fm &= fm - 1;
-        const int64_t r = __shfl_sync(0xffffffffu, row, src);
-        const float* x = X + r * d;
+// The rows the tensor-core kernel could not decide, one CTA per row: a float32 screen of all scores
+// hc_c - x.c (an FMA chain from hc over the columns in order: the CUDA-core pass's form and error window;
+// the transposed centers make the loads coalesced), then the float64 distance (NumPy-pairwise D64) of every
+// center within the window of the smallest score; the smallest D64, lowest index on ties, is the label.
+// If the tensor-core kernel gave up, every row is decided here.
+constexpr int kRescoreThreads = 256;
+__global__ void __launch_bounds__(kRescoreThreads) k_rescore_tc(const float* __restrict__ X, int64_t n, int d,
+                                                               const float* __restrict__ C,
+                                                               const float* __restrict__ ct,
+                                                               const float* __restrict__ hc, int k,
+                                                               const Prep* __restrict__ prep_p,
+                                                               const uint32_t* __restrict__ list,
+                                                               const unsigned int* __restrict__ nflag,
+                                                               const int* __restrict__ tc_error,
+                                                               int32_t* __restrict__ lab,
+                                                               long long* __restrict__ counters) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float* xs = reinterpret_cast<float*>(smem_raw);                 // d
+    float* sc = xs + d;                                              // k scores
+    __shared__ float rmin[kRescoreThreads / 32];
+    __shared__ double rbv[kRescoreThreads / 32];
+    __shared__ int rbi[kRescoreThreads / 32];
+    __shared__ float sx2;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const Prep prep = *prep_p;
+    const bool all = *tc_error != 0;
+    const int64_t cnt = all ? n : (int64_t)*nflag;
+    for (int64_t f = blockIdx.x; f < cnt; f += gridDim.x) {
+        const int64_t row = all ? f : (int64_t)list[f];
+        const float* x = X + row * d;
+        for (int j = tid; j < d; j += kRescoreThreads) xs[j] = x[j];
+        __syncthreads();
+        if (tid == 0) {
+            float x2 = 0.0f;
+            for (int j = 0; j < d; j++) x2 = __fmaf_rn(xs[j], xs[j], x2);
+            sx2 = x2;
+        }
+        float m = INFINITY;
+        for (int c = tid; c < k; c += kRescoreThreads) {
+            float v = hc[c];
+            for (int j = 0; j < d; j++) v = __fmaf_rn(-xs[j], ct[(int64_t)j * k + c], v);
+            sc[c] = v;
+            m = fminf(m, v);
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) m = fminf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) rmin[warp] = m;
+        __syncthreads();
+        m = rmin[0];
+        for (int w = 1; w < kRescoreThreads / 32; w++) m = fminf(m, rmin[w]);
+        const float lim = m + __fmaf_rn(prep.win_coef, sx2 + prep.cmax2, prep.win_abs);
         double bv = INFINITY;
         int bi = 0x7fffffff;
-        for (int c = lane; c < k; c += 32) {
-            const double v = d64_pairwise(x, C + (int64_t)c * d, d);
-            if (v < bv) { bv = v; bi = c; }
+        for (int c = tid; c < k; c += kRescoreThreads) {
+            if (!(sc[c] <= lim)) continue;     // (a NaN score is a candidate too)
+            const double v = d64_pairwise(xs, C + (int64_t)c * d, d);
+            if (v < bv || (v == bv && c < bi)) { bv = v; bi = c; }
         }
 #pragma unroll
         for (int o = 16; o; o >>= 1) {
@@ -104,61 +154,207 @@ __device__ __noinline__ int rescore_all(unsigned fm, const float* __restrict__ X
             const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
             if (ov < bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
         }
-        if (lane == src) l = bi;
+        if (lane == 0) { rbv[warp] = bv; rbi[warp] = bi; }
+        __syncthreads();
+        if (tid == 0) {
+            for (int w = 1; w < kRescoreThreads / 32; w++)
+                if (rbv[w] < bv || (rbv[w] == bv && rbi[w] < bi)) { bv = rbv[w]; bi = rbi[w]; }
+            lab[row] = bi == 0x7fffffff ? 0 : bi;
+        }
+        __syncthreads();
     }
-    return l;
+    if (blockIdx.x == 0 && tid == 0 && cnt)
+        atomicAdd(reinterpret_cast<unsigned long long*>(&counters[0]), (unsigned long long)cnt);
 }
 
-// one thread per row
-__global__ void __launch_bounds__(kSplitThreads) k_accum_split(PassArgs a, const int32_t* __restrict__ lab,
-                                                              const int* __restrict__ tc_error) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    const int d = a.d, k = a.k;
-    const int W = d + 2;
-    long long* sacc = reinterpret_cast<long long*>(smem_raw);
-    const int nslots = a.smem_acc ? k * W : 0;
-    for (int s = threadIdx.x; s < nslots; s += blockDim.x) sacc[s] = 0;
+constexpr int kHistMax = 8192;           // labels counted in shared memory up to this k
+constexpr int kRun = 256;                // grouped rows per warp in k_reduce_rows
+constexpr int kReduceWarps = 8;
+
+// one thread per row: the histogram of the final labels and the optional labels / best outputs
+__global__ void __launch_bounds__(kSplitThreads) k_fix_labels(const float* __restrict__ X, int64_t n, int d,
+                                                             const float* __restrict__ C, int k,
+                                                             const int32_t* __restrict__ lab,
+                                                             unsigned int* __restrict__ hist,
+                                                             int32_t* __restrict__ labels_out,
+                                                             float* __restrict__ best_out) {
+    __shared__ unsigned int sh[kHistMax];
+    const bool local = k <= kHistMax;
+    if (local)
+        for (int c = threadIdx.x; c < k; c += blockDim.x) sh[c] = 0u;
     __syncthreads();
-    const Prep prep = *a.prep;
-    const bool all_flagged = *tc_error != 0;   // the tensor-core kernel gave up: decide every row here
-    const int lane = threadIdx.x & 31;
-    int rescored = 0, bad = 0;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    // the loop bound is uniform over the warp (rows of a warp are consecutive), so the warp re-scores together
-    for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < a.n; base += stride) {
-        const int64_t i = base + threadIdx.x;
-        const bool live = i < a.n;
-        const uint32_t w = live ? (uint32_t)lab[i] : 0u;
-        const bool flag = live && (all_flagged || (w >> 31) != 0);
-        int l = (int)(w & 0x7fffffffu);
-        const unsigned fm = __ballot_sync(0xffffffffu, flag);
-        if (fm) {
-            l = rescore_all(fm, a.X, i, d, a.C, k, lane, l);
-            rescored += flag ? 1 : 0;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const int l = lab[i];
+        if (local) atomicAdd(&sh[l], 1u);
+        else atomicAdd(&hist[l], 1u);
+        if (labels_out) labels_out[i] = l;
+        if (best_out) {
+            const float* xr = X + i * d;
+            const float* cr = C + (int64_t)l * d;
+            float b = 0.0f;
+            for (int j = 0; j < d; j++) b = best32_term(b, xr[j], cr[j]);
+            best_out[i] = b;
         }
-        if (!live) continue;
-        if (l >= k) l = 0;                     // a label past k only comes with a flag, which fixed it
-        const float* xr = a.X + i * d;
-        const float* cr = a.C + (int64_t)l * d;
-        float b = 0.0f;
-        for (int j = 0; j < d; j++) b = best32_term(b, xr[j], cr[j]);
-        if (!isfinite(b)) bad = 1;
-        if (a.labels) a.labels[i] = l;
-        if (a.best) a.best[i] = b;
-        long long* acc = a.smem_acc ? sacc + (size_t)l * W : a.totals + (size_t)l * W;
-        atomicAdd(reinterpret_cast<unsigned long long*>(acc), 1ull);
-        atomicAdd(reinterpret_cast<unsigned long long*>(acc + 1), (unsigned long long)quantize(b, prep.scale_i));
-        for (int j = 0; j < d; j++)
-            atomicAdd(reinterpret_cast<unsigned long long*>(acc + 2 + j),
-                      (unsigned long long)quantize(xr[j], a.scale_x[j]));
     }
     __syncthreads();
-    for (int s = threadIdx.x; s < nslots; s += blockDim.x)
-        if (sacc[s]) atomicAdd(reinterpret_cast<unsigned long long*>(a.totals + s), (unsigned long long)sacc[s]);
-    for (int o = 16; o; o >>= 1) rescored += __shfl_xor_sync(0xffffffffu, rescored, o);
-    if (lane == 0 && rescored)
-        atomicAdd(reinterpret_cast<unsigned long long*>(&a.counters[0]), (unsigned long long)rescored);
-    if (bad) atomicOr(reinterpret_cast<unsigned long long*>(&a.counters[1]), (unsigned long long)kFlagNonFinite);
+    if (local)
+        for (int c = threadIdx.x; c < k; c += blockDim.x)
+            if (sh[c]) atomicAdd(&hist[c], sh[c]);
+}
+
+// one CTA: exclusive prefix sum of the label counts -> each label's first slot (the scatter's cursors)
+__global__ void __launch_bounds__(1024) k_scan_labels(const unsigned int* __restrict__ hist, int k,
+                                                      unsigned int* __restrict__ cursor) {
+    __shared__ unsigned int part[1024];
+    const int t = threadIdx.x;
+    const int per = (k + 1023) / 1024;
+    const int lo = min(k, t * per), hi = min(k, lo + per);
+    unsigned int s = 0;
+    for (int c = lo; c < hi; c++) s += hist[c];
+    part[t] = s;
+    __syncthreads();
+    for (int o = 1; o < 1024; o <<= 1) {     // inclusive Hillis-Steele scan of the per-thread sums
+        const unsigned int v = t >= o ? part[t - o] : 0u;
+        __syncthreads();
+        part[t] += v;
+        __syncthreads();
+    }
+    unsigned int run = t ? part[t - 1] : 0u;
+    for (int c = lo; c < hi; c++) {
+        cursor[c] = run;
+        run += hist[c];
+    }
+}
+
+// Rows grouped by label.  Per CTA and chunk of kScatterRows rows: a shared histogram, one global atomic per
+// label present to reserve its slots, then each row's place in them (k above kScatterMax: one global atomic
+// per row).  The order inside a label is not fixed; the totals do not depend on it.
+constexpr int kScatterRows = 8192;
+constexpr int kScatterMax = 4096;
+__global__ void __launch_bounds__(kSplitThreads) k_scatter_rows(const int32_t* __restrict__ lab, int64_t n, int k,
+                                                               unsigned int* __restrict__ cursor,
+                                                               uint32_t* __restrict__ perm) {
+    __shared__ unsigned int cnt[kScatterMax];
+    __shared__ unsigned int at[kScatterMax];
+    const bool local = k <= kScatterMax;
+    for (int64_t c0 = (int64_t)blockIdx.x * kScatterRows; c0 < n; c0 += (int64_t)gridDim.x * kScatterRows) {
+        const int64_t c1 = min(n, c0 + kScatterRows);
+        if (!local) {
+            for (int64_t i = c0 + threadIdx.x; i < c1; i += blockDim.x) perm[atomicAdd(&cursor[lab[i]], 1u)] = (uint32_t)i;
+            continue;
+        }
+        for (int c = threadIdx.x; c < k; c += blockDim.x) cnt[c] = 0u;
+        __syncthreads();
+        for (int64_t i = c0 + threadIdx.x; i < c1; i += blockDim.x) atomicAdd(&cnt[lab[i]], 1u);
+        __syncthreads();
+        for (int c = threadIdx.x; c < k; c += blockDim.x) {
+            at[c] = cnt[c] ? atomicAdd(&cursor[c], cnt[c]) : 0u;
+            cnt[c] = 0u;
+        }
+        __syncthreads();
+        for (int64_t i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
+            const int l = lab[i];
+            perm[at[l] + atomicAdd(&cnt[l], 1u)] = (uint32_t)i;
+        }
+        __syncthreads();
+    }
+}
+
+// One warp per run of kRun grouped rows.  Lane-private int64 sums of column j = lane + 32 m live in shared
+// memory (d per warp); they go to the global totals (one atomic per column) whenever the label changes.  The
+// inertia is each row's float64 squared distance, quantised per (row, lane) partial: integer sums, so no order
+// matters.  Rows are taken 8 at a time (their indices and labels in one load each), and for d <= 32 * XR the
+// 8 rows' values are loaded before any is used.
+template <int XR>
+__global__ void __launch_bounds__(32 * kReduceWarps) k_reduce_rows(const float* __restrict__ X, int64_t n, int d,
+                                                                  const float* __restrict__ C,
+                                                                  const int32_t* __restrict__ lab,
+                                                                  const uint32_t* __restrict__ perm,
+                                                                  const double* __restrict__ scale_x,
+                                                                  const Prep* __restrict__ prep,
+                                                                  long long* __restrict__ totals,
+                                                                  long long* __restrict__ counters) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    long long* acc = reinterpret_cast<long long*>(smem_raw) + (size_t)warp * d;
+    for (int j = lane; j < d; j += 32) acc[j] = 0;
+    const double scale_i = prep->scale_i;
+    const int W = d + 2;
+    bool bad = false;
+    const int64_t runs = (n + kRun - 1) / kRun;
+    for (int64_t run = (int64_t)blockIdx.x * kReduceWarps + warp; run < runs;
+         run += (int64_t)gridDim.x * kReduceWarps) {
+        const int64_t r0 = run * kRun, r1 = min(n, r0 + kRun);
+        int cur = -1;
+        long long cnt = 0, iq = 0;
+        auto flush = [&]() {
+            if (cur < 0) return;
+            long long* t = totals + (size_t)cur * W;
+            for (int j = lane; j < d; j += 32) {
+                if (acc[j]) atomicAdd(reinterpret_cast<unsigned long long*>(t + 2 + j), (unsigned long long)acc[j]);
+                acc[j] = 0;
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) iq += __shfl_xor_sync(0xffffffffu, iq, o);
+            if (lane == 0) {
+                atomicAdd(reinterpret_cast<unsigned long long*>(t), (unsigned long long)cnt);
+                if (iq) atomicAdd(reinterpret_cast<unsigned long long*>(t + 1), (unsigned long long)iq);
+            }
+            cnt = 0;
+            iq = 0;
+        };
+        auto add = [&](const float* x, const float* c, int j, float v) {
+            acc[j] += quantize(v, scale_x[j]);
+            const double q = (double)v - (double)c[j];
+            return q * q;
+        };
+        for (int64_t r = r0; r < r1; r += 8) {
+            const int m = (int)min((int64_t)8, r1 - r);
+            const uint32_t pr = lane < m ? perm[r + lane] : 0u;
+            const int pl = lane < m ? lab[pr] : 0;
+            float xv[8][XR > 0 ? XR : 1];
+            if constexpr (XR > 0) {
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const int64_t row = __shfl_sync(0xffffffffu, pr, u);
+#pragma unroll
+                    for (int t = 0; t < XR; t++) {
+                        const int j = lane + 32 * t;
+                        xv[u][t] = (u < m && j < d) ? X[row * d + j] : 0.0f;
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) {          // unrolled, so xv stays in registers
+                if (u >= m) break;
+                const int64_t row = __shfl_sync(0xffffffffu, pr, u);
+                const int l = __shfl_sync(0xffffffffu, pl, u);
+                if (l != cur) {
+                    flush();
+                    cur = l;
+                }
+                const float* x = X + row * d;
+                const float* c = C + (int64_t)l * d;
+                double b = 0.0;
+                if constexpr (XR > 0) {
+#pragma unroll
+                    for (int t = 0; t < XR; t++) {
+                        const int j = lane + 32 * t;
+                        if (j < d) b += add(x, c, j, xv[u][t]);
+                    }
+                } else {
+                    for (int j = lane; j < d; j += 32) b += add(x, c, j, x[j]);
+                }
+                if (!(b <= 1.0e300)) bad = true;
+                else iq += __double2ll_rn(__dmul_rn(b, scale_i));
+                cnt++;
+            }
+        }
+        flush();
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0)
+        atomicOr(reinterpret_cast<unsigned long long*>(&counters[1]), (unsigned long long)kFlagNonFinite);
 }
 
 int64_t a256(int64_t v) { return (v + 255) / 256 * 256; }
@@ -170,12 +366,12 @@ int split_kp(int k) { return (k + tc_block_n(k) - 1) / tc_block_n(k) * tc_block_
 
 size_t split_rows_bytes(int64_t n, int d) {
     const int64_t nn = n > 0 ? n : 1, dp = split_dp(d);
-    return (size_t)(2 * a256(nn * dp * 2) + 2 * a256(nn * 4));
+    return (size_t)(2 * a256(nn * dp * 2) + 3 * a256(nn * 4));
 }
 
 size_t split_centers_bytes(int d, int k) {
     const int64_t dp = split_dp(d), kp = split_kp(k);
-    return (size_t)(256 + 2 * a256(kp * dp * 2) + a256(kp * 4));
+    return (size_t)(256 + 2 * a256(kp * dp * 2) + 3 * a256(kp * 4) + a256((int64_t)k * d * 4));
 }
 
 RowSplit carve_rows(void* base, int64_t n, int d) {
@@ -186,6 +382,7 @@ RowSplit carve_rows(void* base, int64_t n, int d) {
     s.xl = p + a256(nn * dp * 2);
     s.xn = reinterpret_cast<float*>(p + 2 * a256(nn * dp * 2));
     s.lab = reinterpret_cast<int32_t*>(p + 2 * a256(nn * dp * 2) + a256(nn * 4));
+    s.perm = reinterpret_cast<uint32_t*>(p + 2 * a256(nn * dp * 2) + 2 * a256(nn * 4));
     return s;
 }
 
@@ -195,9 +392,13 @@ CenterSplit carve_centers(void* base, int d, int k) {
     char* p = static_cast<char*>(base);
     s.cmax_bits = reinterpret_cast<unsigned int*>(p);
     s.error = reinterpret_cast<int*>(p + 4);
+    s.nflag = reinterpret_cast<unsigned int*>(p + 8);
     s.ch = p + 256;
     s.cl = p + 256 + a256(kp * dp * 2);
     s.hs = reinterpret_cast<float*>(p + 256 + 2 * a256(kp * dp * 2));
+    s.hist = reinterpret_cast<unsigned int*>(p + 256 + 2 * a256(kp * dp * 2) + a256(kp * 4));
+    s.cursor = reinterpret_cast<unsigned int*>(p + 256 + 2 * a256(kp * dp * 2) + 2 * a256(kp * 4));
+    s.ct = reinterpret_cast<float*>(p + 256 + 2 * a256(kp * dp * 2) + 3 * a256(kp * 4));
     return s;
 }
 
@@ -212,28 +413,51 @@ cudaError_t launch_split_rows(const float* X, int64_t n, int d, const RowSplit& 
 }
 
 cudaError_t launch_split_centers(const float* C, int k, int d, const CenterSplit& s, cudaStream_t st) {
-    cudaError_t e = cudaMemsetAsync(s.cmax_bits, 0, 8, st);   // max |c| and the tensor-core error flag
+    cudaError_t e = cudaMemsetAsync(s.cmax_bits, 0, 12, st);   // max |c|, the error flag, the flagged rows
     if (e != cudaSuccess) return e;
     const int kp = split_kp(k);
     const int blocks = (kp + kSplitThreads / 32 - 1) / (kSplitThreads / 32);
     k_split_centers<<<blocks, kSplitThreads, 0, st>>>(C, k, d, kp, split_dp(d), static_cast<__nv_bfloat16*>(s.ch),
-                                                       static_cast<__nv_bfloat16*>(s.cl), s.hs, s.cmax_bits);
+                                                       static_cast<__nv_bfloat16*>(s.cl), s.hs, s.cmax_bits, s.ct);
     return cudaGetLastError();
 }
 
-cudaError_t launch_accum_split(PassArgs a, const int32_t* lab, const int* tc_error, cudaStream_t st) {
-    const int W = a.d + 2;
-    a.smem_acc = (size_t)a.k * W * 8 <= 96 * 1024 ? 1 : 0;
-    const size_t smem = a.smem_acc ? (size_t)a.k * W * 8 : 0;
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(k_accum_split, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-    }
+cudaError_t launch_accum_split(PassArgs a, const RowSplit& rs, const CenterSplit& cs, cudaStream_t st) {
+    if (a.n == 0) return cudaSuccess;
+    cudaError_t e = cudaMemsetAsync(cs.hist, 0, sizeof(unsigned int) * (size_t)a.k, st);
+    if (e != cudaSuccess) return e;
     int64_t blocks = (a.n + kSplitThreads - 1) / kSplitThreads;
     const int64_t cap = (int64_t)num_sms() * 8;
     if (blocks > cap) blocks = cap;
-    if (blocks < 1) blocks = 1;
-    k_accum_split<<<(int)blocks, kSplitThreads, smem, st>>>(a, lab, tc_error);
+    const size_t rsm = sizeof(float) * ((size_t)a.d + a.k);
+    if (rsm > 48 * 1024) {
+        e = cudaFuncSetAttribute(k_rescore_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
+        if (e != cudaSuccess) return e;
+    }
+    k_rescore_tc<<<num_sms() * 8, kRescoreThreads, rsm, st>>>(a.X, a.n, a.d, a.C, cs.ct, a.hc, a.k, a.prep, rs.perm,
+                                                              cs.nflag, cs.error, rs.lab, a.counters);
+    k_fix_labels<<<(int)blocks, kSplitThreads, 0, st>>>(a.X, a.n, a.d, a.C, a.k, rs.lab, cs.hist, a.labels, a.best);
+    k_scan_labels<<<1, 1024, 0, st>>>(cs.hist, a.k, cs.cursor);
+    int64_t sb = (a.n + kScatterRows - 1) / kScatterRows;
+    if (sb > cap) sb = cap;
+    k_scatter_rows<<<(int)sb, kSplitThreads, 0, st>>>(rs.lab, a.n, a.k, cs.cursor, rs.perm);
+    const size_t smem = (size_t)kReduceWarps * a.d * 8;
+    const int64_t runs = (a.n + kRun - 1) / kRun;
+    int64_t rb = (runs + kReduceWarps - 1) / kReduceWarps;
+    const int64_t rcap = (int64_t)num_sms() * 8;
+    if (rb > rcap) rb = rcap;
+    auto go = [&](auto kern) -> cudaError_t {
+        if (smem > 48 * 1024) {
+            cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e2 != cudaSuccess) return e2;
+        }
+        kern<<<(int)rb, 32 * kReduceWarps, smem, st>>>(a.X, a.n, a.d, a.C, rs.lab, rs.perm, a.scale_x, a.prep,
+                                                       a.totals, a.counters);
+        return cudaSuccess;
+    };
+    e = a.d <= 32 ? go(k_reduce_rows<1>) : a.d <= 64 ? go(k_reduce_rows<2>) : a.d <= 128 ? go(k_reduce_rows<4>)
+                                                                            : go(k_reduce_rows<0>);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
