@@ -146,6 +146,7 @@ struct TcArgs {
     const float* cmax;       // max |c| rounded up (one value)
     int32_t* lab;            // n: label | flag << 31
     uint32_t* flagged;       // rows to decide in float64
+    int4* cands;             // their candidate centers (-1: none, w = -2: more than four)
     unsigned int* nflag;     // their number (zeroed by the caller)
     int* error;              // set on a barrier timeout
 };
@@ -265,8 +266,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         uint32_t abuf = 0, aphase = 0;
         bool ok = true;
         for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-            float m1 = INFINITY, m2 = INFINITY;
-            int l1 = 0;
+            // the two smallest scores with their centers (equal scores keep the lower index first) and the third
+            // smallest score
+            float m0 = INFINITY, m1 = INFINITY, m2 = INFINITY;
+            int l0 = 0, l1 = 0;
             for (int nt = 0; nt < ntiles && ok; nt++) {
                 ok = mbar_wait(accf(abuf), aphase, abort_flag);
                 if (!ok) break;
@@ -279,8 +282,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 32; j++) {
                         const float s = __ldg(a.hs + c0 + j) - v[j];
-                        if (s < m1) { m2 = m1; m1 = s; l1 = c0 + j; }
-                        else if (s < m2) m2 = s;
+                        if (s < m1) {
+                            m2 = m1;
+                            if (s < m0) { m1 = m0; l1 = l0; m0 = s; l0 = c0 + j; }
+                            else { m1 = s; l1 = c0 + j; }
+                        } else if (s < m2) m2 = s;
                     }
                 }
                 tc_fence_before();
@@ -291,12 +297,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (!ok) break;
             const int64_t row = t * BM + 32 * q + lane;
             bool flag = false;
+            int4 cand = make_int4(l0, -1, -1, -1);
             if (row < a.n) {
                 const float xr = __ldg(a.xn + row), r = xr + cmax;
                 const float win = (E2 * xr * cmax + cmax * (cmax + xr) * (1.0f / 8388608.0f)) * (1.0f + 1.0f / 1024.0f) +
                                   r * r * (1.0f / 1099511627776.0f);
-                flag = !(m2 - m1 > win) || l1 >= a.k;
-                a.lab[row] = (int32_t)((uint32_t)l1 | (flag ? 0x80000000u : 0u));
+                flag = !(m1 - m0 > win) || l0 >= a.k;
+                a.lab[row] = (int32_t)((uint32_t)l0 | (flag ? 0x80000000u : 0u));
+                // candidates: the centers whose score is within the window of the smallest; when the third is
+                // too (or a score is not finite), there may be more than two: -2 sends the row to the full decision
+                if (!(m1 - m0 > win)) cand.y = l1;
+                if (!(m2 - m0 > win) || !(m0 <= 3.0e38f) || l0 >= a.k) cand.w = -2;
             }
             // flagged rows join the list the float64 decision works through (one atomic per warp)
             const unsigned fm = __ballot_sync(0xffffffffu, flag);
@@ -305,7 +316,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 unsigned at = 0;
                 if (lane == leader) at = atomicAdd(a.nflag, (unsigned)__popc(fm));
                 at = __shfl_sync(0xffffffffu, at, leader);
-                if (flag) a.flagged[at + __popc(fm & ((1u << lane) - 1u))] = (uint32_t)row;
+                if (flag) {
+                    const unsigned f = at + __popc(fm & ((1u << lane) - 1u));
+                    a.flagged[f] = (uint32_t)row;
+                    a.cands[f] = cand;
+                }
             }
         }
     }
@@ -374,6 +389,7 @@ cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
     a.cmax = s.cmax;
     a.lab = s.lab;
     a.flagged = s.flagged;
+    a.cands = s.cands;
     a.nflag = s.nflag;
     a.error = s.error;
     const int64_t tiles = (s.n + BM - 1) / BM;

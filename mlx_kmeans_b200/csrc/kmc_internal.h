@@ -77,13 +77,16 @@ struct RowSplit {
     void* xl;                 // n x dp bf16, the rest rounded to bf16
     float* xn;                // n: |x| rounded up
     int32_t* lab;             // n: label | flag << 31 from the tensor-core kernel, then the final label
-    uint32_t* perm;           // n: rows grouped by label
+    uint32_t* perm;           // n: rows grouped by label (before that: the rows the tensor-core kernel flagged)
+    int4* cands;              // n: each flagged row's candidate centers (x, y; w = -2: more than two)
+    uint32_t* ovf;            // n: flagged rows with more than two candidates
 };
 // ... and per-pass center operands
 struct CenterSplit {
     unsigned int* cmax_bits;  // max |c| rounded up (float bits)
     int* error;               // set when the tensor-core kernel timed out on a barrier
     unsigned int* nflag;      // rows the tensor-core kernel left to float64 (listed in RowSplit::perm)
+    unsigned int* novf;       // of those, rows with more than two candidates (listed in RowSplit::ovf)
     float* ct;                // d x k: the centers transposed, for the float64 decision's float32 screen
     void* ch;                 // kp x dp bf16
     void* cl;                 // kp x dp bf16
@@ -100,6 +103,7 @@ struct TcSplit {
     const float* cmax;
     int32_t* lab;
     uint32_t* flagged;
+    int4* cands;
     unsigned int* nflag;
     int* error;
 };

@@ -90,7 +90,45 @@ __global__ void __launch_bounds__(kSplitThreads) k_split_centers(const float* __
     }
 }
 
-// The rows the tensor-core kernel could not decide, one CTA per row: a float32 screen of all scores
+// The rows the tensor-core kernel flagged, one thread each: the float64 distance (NumPy-pairwise D64) of each of
+// its (two) candidate centers; the smallest, lowest index on ties, is the label.  Rows with more candidates go
+// on to k_rescore_tc.  (If the tensor-core kernel gave up, k_rescore_tc decides every row.)
+__global__ void __launch_bounds__(kSplitThreads) k_decide_cands(const float* __restrict__ X, int d,
+                                                               const float* __restrict__ C,
+                                                               const uint32_t* __restrict__ list,
+                                                               const int4* __restrict__ cands,
+                                                               const unsigned int* __restrict__ nflag,
+                                                               const int* __restrict__ tc_error,
+                                                               uint32_t* __restrict__ ovf,
+                                                               unsigned int* __restrict__ novf,
+                                                               int32_t* __restrict__ lab,
+                                                               long long* __restrict__ counters) {
+    if (*tc_error) return;
+    const int64_t cnt = *nflag;
+    if (blockIdx.x == 0 && threadIdx.x == 0 && cnt)
+        atomicAdd(reinterpret_cast<unsigned long long*>(&counters[0]), (unsigned long long)cnt);
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; f < cnt; f += stride) {
+        const int64_t row = list[f];
+        const int4 c4 = cands[f];
+        if (c4.w == -2) {
+            ovf[atomicAdd(novf, 1u)] = (uint32_t)row;
+            continue;
+        }
+        const float* x = X + row * d;
+        const int cs[4] = {c4.x, c4.y, c4.z, c4.w};
+        double bv = INFINITY;
+        int bi = c4.x;
+        for (int i = 0; i < 4; i++) {
+            if (cs[i] < 0) continue;
+            const double v = d64_pairwise(x, C + (int64_t)cs[i] * d, d);
+            if (v < bv || (v == bv && cs[i] < bi)) { bv = v; bi = cs[i]; }
+        }
+        lab[row] = bi;
+    }
+}
+
+// The rows the tensor-core kernel could not decide from two candidates, one CTA per row: a float32 screen of all scores
 // hc_c - x.c (an FMA chain from hc over the columns in order: the CUDA-core pass's form and error window;
 // the transposed centers make the loads coalesced), then the float64 distance (NumPy-pairwise D64) of every
 // center within the window of the smallest score; the smallest D64, lowest index on ties, is the label.
@@ -102,7 +140,7 @@ __global__ void __launch_bounds__(kRescoreThreads) k_rescore_tc(const float* __r
                                                                const float* __restrict__ hc, int k,
                                                                const Prep* __restrict__ prep_p,
                                                                const uint32_t* __restrict__ list,
-                                                               const unsigned int* __restrict__ nflag,
+                                                               const unsigned int* __restrict__ nlist,
                                                                const int* __restrict__ tc_error,
                                                                int32_t* __restrict__ lab,
                                                                long long* __restrict__ counters) {
@@ -116,7 +154,7 @@ __global__ void __launch_bounds__(kRescoreThreads) k_rescore_tc(const float* __r
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const Prep prep = *prep_p;
     const bool all = *tc_error != 0;
-    const int64_t cnt = all ? n : (int64_t)*nflag;
+    const int64_t cnt = all ? n : (int64_t)*nlist;
     for (int64_t f = blockIdx.x; f < cnt; f += gridDim.x) {
         const int64_t row = all ? f : (int64_t)list[f];
         const float* x = X + row * d;
@@ -163,7 +201,7 @@ __global__ void __launch_bounds__(kRescoreThreads) k_rescore_tc(const float* __r
         }
         __syncthreads();
     }
-    if (blockIdx.x == 0 && tid == 0 && cnt)
+    if (all && blockIdx.x == 0 && tid == 0 && cnt)
         atomicAdd(reinterpret_cast<unsigned long long*>(&counters[0]), (unsigned long long)cnt);
 }
 
@@ -366,7 +404,7 @@ int split_kp(int k) { return (k + tc_block_n(k) - 1) / tc_block_n(k) * tc_block_
 
 size_t split_rows_bytes(int64_t n, int d) {
     const int64_t nn = n > 0 ? n : 1, dp = split_dp(d);
-    return (size_t)(2 * a256(nn * dp * 2) + 3 * a256(nn * 4));
+    return (size_t)(2 * a256(nn * dp * 2) + 4 * a256(nn * 4) + a256(nn * 16));
 }
 
 size_t split_centers_bytes(int d, int k) {
@@ -383,6 +421,8 @@ RowSplit carve_rows(void* base, int64_t n, int d) {
     s.xn = reinterpret_cast<float*>(p + 2 * a256(nn * dp * 2));
     s.lab = reinterpret_cast<int32_t*>(p + 2 * a256(nn * dp * 2) + a256(nn * 4));
     s.perm = reinterpret_cast<uint32_t*>(p + 2 * a256(nn * dp * 2) + 2 * a256(nn * 4));
+    s.ovf = reinterpret_cast<uint32_t*>(p + 2 * a256(nn * dp * 2) + 3 * a256(nn * 4));
+    s.cands = reinterpret_cast<int4*>(p + 2 * a256(nn * dp * 2) + 4 * a256(nn * 4));
     return s;
 }
 
@@ -393,6 +433,7 @@ CenterSplit carve_centers(void* base, int d, int k) {
     s.cmax_bits = reinterpret_cast<unsigned int*>(p);
     s.error = reinterpret_cast<int*>(p + 4);
     s.nflag = reinterpret_cast<unsigned int*>(p + 8);
+    s.novf = reinterpret_cast<unsigned int*>(p + 12);
     s.ch = p + 256;
     s.cl = p + 256 + a256(kp * dp * 2);
     s.hs = reinterpret_cast<float*>(p + 256 + 2 * a256(kp * dp * 2));
@@ -413,7 +454,7 @@ cudaError_t launch_split_rows(const float* X, int64_t n, int d, const RowSplit& 
 }
 
 cudaError_t launch_split_centers(const float* C, int k, int d, const CenterSplit& s, cudaStream_t st) {
-    cudaError_t e = cudaMemsetAsync(s.cmax_bits, 0, 12, st);   // max |c|, the error flag, the flagged rows
+    cudaError_t e = cudaMemsetAsync(s.cmax_bits, 0, 16, st);   // max |c|, error flag, flagged and overflow counts
     if (e != cudaSuccess) return e;
     const int kp = split_kp(k);
     const int blocks = (kp + kSplitThreads / 32 - 1) / (kSplitThreads / 32);
@@ -434,8 +475,10 @@ cudaError_t launch_accum_split(PassArgs a, const RowSplit& rs, const CenterSplit
         e = cudaFuncSetAttribute(k_rescore_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
         if (e != cudaSuccess) return e;
     }
-    k_rescore_tc<<<num_sms() * 8, kRescoreThreads, rsm, st>>>(a.X, a.n, a.d, a.C, cs.ct, a.hc, a.k, a.prep, rs.perm,
-                                                              cs.nflag, cs.error, rs.lab, a.counters);
+    k_decide_cands<<<num_sms() * 4, kSplitThreads, 0, st>>>(a.X, a.d, a.C, rs.perm, rs.cands, cs.nflag, cs.error,
+                                                             rs.ovf, cs.novf, rs.lab, a.counters);
+    k_rescore_tc<<<num_sms() * 8, kRescoreThreads, rsm, st>>>(a.X, a.n, a.d, a.C, cs.ct, a.hc, a.k, a.prep, rs.ovf,
+                                                              cs.novf, cs.error, rs.lab, a.counters);
     k_fix_labels<<<(int)blocks, kSplitThreads, 0, st>>>(a.X, a.n, a.d, a.C, a.k, rs.lab, cs.hist, a.labels, a.best);
     k_scan_labels<<<1, 1024, 0, st>>>(cs.hist, a.k, cs.cursor);
     int64_t sb = (a.n + kScatterRows - 1) / kScatterRows;

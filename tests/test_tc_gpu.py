@@ -47,7 +47,8 @@ def test_tc_matches_golden(name, cuda_device):
     _check_assign(g["X"], g["C"], out, g["labels"])
 
 
-@pytest.mark.parametrize("name", ["separated_d8_k16", "tiny_n7_d3_k5", "integer_grid_ties_d6_k12", "d1_k7"])
+@pytest.mark.parametrize("name", ["separated_d8_k16", "tiny_n7_d3_k5", "integer_grid_ties_d6_k12", "d1_k7",
+                                  "duplicate_centers_d8_k32", "duplicate_points_d8_k64"])
 def test_tc_forced_at_low_d(name, cuda_device):
     """Columns padded to 64 and tiny n: the tensor-core pass still gives the oracle's labels."""
     import torch
@@ -125,3 +126,18 @@ def test_tc_lloyd_step_and_slices(cuda_device):
             assert np.array_equal(C_new[c], X[row])
         outs.append(C_new)
     assert np.array_equal(outs[0], outs[1])
+
+
+def test_tc_many_equal_centers(cuda_device):
+    """Six copies of one center: rows near it have six exact ties, more candidates than the tensor-core kernel
+    keeps (two), so they take the full float64 decision; the label is the lowest index, as in the oracle."""
+    import torch
+    rng = np.random.default_rng(5)
+    X = rng.standard_normal((5_000, 64)).astype(np.float32)
+    C = rng.standard_normal((40, 64)).astype(np.float32)
+    C[[3, 9, 10, 17, 30, 31]] = 0.05 * rng.standard_normal(64).astype(np.float32)
+    ds = _ds(X, cuda_device)
+    out = ds.assign(torch.from_numpy(C).to(cuda_device), return_labels=True)
+    ref, _, _ = O.assign(X, C)
+    assert np.array_equal(out[3], ref)
+    assert (ref == 3).sum() > 0 and not np.isin(ref, [9, 10, 17, 30, 31]).any()
