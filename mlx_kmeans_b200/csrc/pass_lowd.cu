@@ -48,7 +48,10 @@ constexpr int kStages = 8;             // ring slots per thread of the screening
 #endif
 // rows per thread in flight in the bounded kernel, held in registers: about 128 bytes of rows
 constexpr int bounded_ahead(int d) { return KMC_BOUNDED_AHEAD ? KMC_BOUNDED_AHEAD : d <= 4 ? 8 : 4; }
-constexpr int kRowsPerLane = 128;      // rows per lane between folds (a multiple of 8, < 256)
+#ifndef KMC_ROWS_PER_LANE
+#define KMC_ROWS_PER_LANE 128
+#endif
+constexpr int kRowsPerLane = KMC_ROWS_PER_LANE;   // rows per lane between folds (a multiple of 16, < 256)
 constexpr int kBlockRows = kThreads * kRowsPerLane;   // 16384 rows per block
 constexpr int kQueue = 64;             // queued rows per warp in the bounded kernel (power of two, >= 64)
 static_assert(kRowsPerLane % kStages == 0 && kRowsPerLane % 8 == 0 && kRowsPerLane < 256, "block layout");
@@ -907,9 +910,12 @@ cudaError_t launch_grid(Kern kern, size_t smem, unsigned long long& configured, 
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorNotSupported;
+    // as many CTAs as fit, but no more than it takes to give every CTA the same number of blocks: with few
+    // blocks per CTA (a shard of a multi-GPU run) an uneven last round would otherwise set the pass time
     const int64_t nblk = (a.n + kBlockRows - 1) / kBlockRows;
-    int64_t grid = (int64_t)num_sms() * per_sm;
-    if (grid > nblk) grid = nblk;
+    const int64_t max_grid = (int64_t)num_sms() * per_sm;
+    const int64_t rounds = (nblk + max_grid - 1) / max_grid;
+    int64_t grid = rounds > 0 ? (nblk + rounds - 1) / rounds : 1;
     if (grid < 1) grid = 1;
     kern<<<(int)grid, kThreads, smem, st>>>(a);
     return cudaGetLastError();
