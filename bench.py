@@ -266,8 +266,7 @@ def main():
             _lib.check(L.kmc_pass(X.data_ptr(), X.shape[0], d, Cin.data_ptr(), k, cm.data_ptr(), n_total,
                                   b["totals"].data_ptr(), None, None, flags, b["ws"].data_ptr(), b["wsb"], sp))
         ev[i][1].record(st)
-        if world > 1:
-            dist.all_reduce(b["totals"], op=dist.ReduceOp.SUM, group=group)
+        ds.allreduce_totals(b, k)
         _lib.check(L.kmc_finish(b["totals"].data_ptr(), k, d, None, 0, 1, Cout.data_ptr(), stats[i].data_ptr(),
                                 b["ws"].data_ptr(), b["wsb"], sp))
     t1.record(st)
@@ -341,7 +340,8 @@ def main():
         "config": {"workload": DESCRIPTION[cfg] + ("" if n_total == CONFIGS[cfg]["rows"] else
                                                    f" (rows overridden: {n_total})"),
                    "rows": n_total, "dims": d, "k": k,
-                   "parallelism": f"rows sharded dp{world}, int64 totals all-reduced (NCCL)",
+                   "parallelism": f"rows sharded dp{world}, int64 totals all-reduced " +
+                                  ("(peer memory, kmc_exchange_sum)" if world > 1 and ds._xch.get(k) else "(NCCL)"),
                    "l2": "inputs larger than L2 (%.2f GB per GPU), no flush" % (bytes_per_launch / 1e9),
                    "relocation_steps_in_timed_region": reloc_steps,
                    "rows_rescored_in_float64_per_pass": rescored,

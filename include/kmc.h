@@ -49,7 +49,7 @@ typedef struct kmc_stats {
     int64_t n_empty;       /* clusters that received no row */
     int64_t n_relocated;   /* clusters given a far row by the relocation rule */
     int64_t needs_reloc;   /* 1: clusters emptied and no candidate rows were given; C_new not written */
-    int64_t flags;         /* 1 = non-finite data, centers or distance */
+    int64_t flags;         /* 1 = non-finite data, centers or distance; 2 = kmc_exchange_sum timed out */
     int64_t rescored;      /* rows whose label was decided in float64 (diagnostic) */
     int64_t screened;      /* rows compared with every center (bounded passes: those whose bound failed) */
     int64_t reserved;
@@ -127,6 +127,23 @@ int kmc_pass_split(const float *X, int64_t n, int d, const float *C, int k, cons
                    int64_t n_total, int64_t *totals, int32_t *labels, float *best, unsigned flags, void *split,
                    size_t split_bytes, void *csplit, size_t csplit_bytes, void *workspace, size_t ws_bytes,
                    void *stream);
+
+/* All-reduce of the totals over the GPUs of one node through peer memory (NVLink), one kernel per step: no
+ * counterpart in the reference (single device); it replaces an NCCL all-reduce of the int64 totals.  Set-up once
+ * per (process group, k): each rank kmc_exchange_alloc's a kmc_exchange_bytes(k, d) buffer (device memory the
+ * library allocates, zeroed) and gets its 64-byte CUDA IPC handle; the handles are exchanged (any host
+ * collective); each rank kmc_exchange_open's its peers' buffers.  `peers` is a device array of the world buffer
+ * addresses (own included, at index rank).  Per pass, after the pass on every local slice: kmc_exchange_sum with
+ * a step number that every rank increments the same way (0, 1, 2, ...); on return (stream order) totals hold the
+ * sum over ranks.  A peer that does not arrive within seconds sets stats flag 2 (read by kmc_finish).  All ranks
+ * must call it the same number of times.  kmc_exchange_close(ptr, own) unmaps a peer's buffer (own = 0) or frees
+ * one's own (own = 1). */
+size_t kmc_exchange_bytes(int k, int d);
+int kmc_exchange_alloc(size_t bytes, void **ptr, void *handle);
+int kmc_exchange_open(const void *handle, void **ptr);
+int kmc_exchange_close(void *ptr, int own);
+int kmc_exchange_sum(int64_t *totals, int k, int d, const uint64_t *peers, int world, int rank, uint64_t step,
+                     void *workspace, size_t ws_bytes, void *stream);
 
 /* kmc_pass without a caller workspace.  No counterpart in the reference: it exists for callers that cannot
  * allocate device memory -- a host runtime that owns every device allocation through its own pool, or a

@@ -21,6 +21,7 @@ _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
 _u = ctypes.c_uint
+_u64 = ctypes.c_uint64
 _sz = ctypes.c_size_t
 
 # name -> (restype, argtypes); mirrors include/kmc.h
@@ -37,6 +38,11 @@ SIGNATURES = {
     "kmc_bounds_bytes": (_sz, [_i64, _int, _int]),
     "kmc_bounds_reset": (_int, [_vp, _vp]),
     "kmc_pass_bounded": (_int, [_vp, _i64, _int, _vp, _int, _vp, _i64, _vp, _u, _vp, _sz, _vp, _sz, _vp]),
+    "kmc_exchange_bytes": (_sz, [_int, _int]),
+    "kmc_exchange_alloc": (_int, [_sz, _vp, _vp]),
+    "kmc_exchange_open": (_int, [_vp, _vp]),
+    "kmc_exchange_close": (_int, [_vp, _int]),
+    "kmc_exchange_sum": (_int, [_vp, _int, _int, _vp, _int, _int, _u64, _vp, _sz, _vp]),
     "kmc_split_bytes": (_sz, [_i64, _int]),
     "kmc_split_rows": (_int, [_vp, _i64, _int, _vp, _sz, _vp]),
     "kmc_csplit_bytes": (_sz, [_int, _int]),

@@ -13,6 +13,8 @@ passes the way the reference keeps its per-array caches (core.py:548-578). Multi
 torch.distributed process group holds this rank's contiguous row shard; the per-cluster totals are summed over
 ranks with one all-reduce per pass (int64, exact).
 """
+import ctypes
+import os
 import weakref
 
 import numpy as np
@@ -118,6 +120,7 @@ class Dataset:
         self.tensor_cores = (d >= self.TC_MIN_DIMS) if tensor_cores is None else bool(tensor_cores)
         self._split = None
         self._csplit = {}
+        self._xch = {}                  # per k: peer-memory exchange of the totals (multi-GPU), or False: NCCL
 
     # -- per-dataset state
     @property
@@ -203,6 +206,61 @@ class Dataset:
             for t, _ in bb:
                 _lib.call("kmc_bounds_reset", _ptr(t), _stream())
 
+    # -- the all-reduce of the totals over the ranks
+    def _exchange(self, k):
+        """Peer-memory exchange buffers for k centers: one per rank, mapped by every peer through CUDA IPC
+        (kmc_exchange_*); False when the ranks cannot map each other's memory (then NCCL is used)."""
+        x = self._xch.get(k)
+        if x is not None:
+            return x
+        import torch.distributed as dist
+        L = _lib.load()
+        x = False
+        own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        ok = os.environ.get("KMC_EXCHANGE", "peer") != "nccl" and \
+            L.kmc_exchange_alloc(int(L.kmc_exchange_bytes(k, self.d)), ctypes.byref(own), handle) == 0
+        oks = [None] * self.world
+        dist.all_gather_object(oks, ok, group=self.group)
+        if all(oks):
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle.raw, group=self.group)
+            ptrs, opened = [], []
+            for r in range(self.world):
+                if r == self.rank:
+                    ptrs.append(own.value)
+                    continue
+                p = ctypes.c_void_p()
+                if L.kmc_exchange_open(handles[r], ctypes.byref(p)) != 0:
+                    break
+                ptrs.append(p.value)
+                opened.append(p.value)
+            oks = [None] * self.world
+            dist.all_gather_object(oks, len(ptrs) == self.world, group=self.group)
+            if all(oks):
+                x = dict(dev=torch.tensor(ptrs, dtype=torch.int64, device=self.device), step=0)
+                weakref.finalize(self, _close_exchange, opened, own.value)
+            else:
+                _close_exchange(opened, own.value)
+        elif own.value:
+            L.kmc_exchange_close(own, 1)
+        self._xch[k] = x
+        return x
+
+    def allreduce_totals(self, b, k):
+        """Sum the int64 totals over the ranks: one peer-memory kernel (kmc_exchange_sum) when the ranks can map
+        each other's buffers, else an NCCL all-reduce.  Either way the result is the exact integer sum."""
+        if self.group is None:
+            return
+        x = self._exchange(k)
+        if x:
+            _lib.call("kmc_exchange_sum", _ptr(b["totals"]), k, self.d, _ptr(x["dev"]), self.world, self.rank,
+                      x["step"], _ptr(b["ws"]), b["wsb"], _stream())
+            x["step"] += 1
+        else:
+            import torch.distributed as dist
+            dist.all_reduce(b["totals"], op=dist.ReduceOp.SUM, group=self.group)
+
     # -- one pass
     def run_pass(self, C, labels=False, generic=False, bounded=False):
         """kmc_pass over every local slice, then the all-reduce of the totals. C: (k, d) float32 CUDA.
@@ -231,9 +289,7 @@ class Dataset:
                           _ptr(b["totals"]), _ptr(lab[i]) if labels else None, _ptr(bst[i]) if labels else None,
                           flags, _ptr(b["ws"]), b["wsb"], st)
             flags |= _lib.KMC_PASS_ACCUMULATE
-        if self.group is not None:
-            import torch.distributed as dist
-            dist.all_reduce(b["totals"], op=dist.ReduceOp.SUM, group=self.group)
+        self.allreduce_totals(b, k)
         return b
 
     def read_stats(self, b):
@@ -252,6 +308,8 @@ class Dataset:
         _lib.call("kmc_finish", _ptr(b["totals"]), k, self.d, None, 0, 1, _ptr(b["C_new"]), _ptr(b["stats"]),
                   _ptr(b["ws"]), b["wsb"], _stream())
         s = self.read_stats(b)
+        if s["flags"] & 2:
+            raise RuntimeError("the all-reduce of the totals timed out waiting for a peer GPU")
         if s["needs_reloc"]:
             s = self._relocate(C, b, s["n_empty"], generic)
         return b["C_new"], s
@@ -299,6 +357,14 @@ class Dataset:
         if return_labels:
             out += (torch.cat(b["labels"]).to(torch.int64).cpu().numpy(),)
         return out
+
+
+def _close_exchange(opened, own):
+    L = _lib.load()
+    for p in opened:
+        L.kmc_exchange_close(ctypes.c_void_p(p), 0)
+    if own:
+        L.kmc_exchange_close(ctypes.c_void_p(own), 1)
 
 
 # identity cache, like core.py:548-578: a second array never sees the first one's state

@@ -140,13 +140,14 @@ int pass_impl(const char* who, const float* X, int64_t n, int d, const float* C,
     if (ws_bytes < ws.bytes) return fail(KMC_ERR_INVALID, "%s: workspace of %zu bytes, need %zu", who, ws_bytes, ws.bytes);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e;
-    if (!(flags & KMC_PASS_ACCUMULATE)) {
-        e = cudaMemsetAsync(totals, 0, sizeof(int64_t) * (size_t)k * (d + 2), st);
-        if (e != cudaSuccess) return cuda_fail(e, who);
-        e = cudaMemsetAsync(ws.counters, 0, sizeof(long long) * 8, st);
-        if (e != cudaSuccess) return cuda_fail(e, who);
-    }
-    e = launch_prepare(C, k, d, colmax, n_total, ws.prep, ws.scale_x, ws.hc, st);
+    const bool fused = !(flags & KMC_PASS_GENERIC) && lowd_supports(d, k);
+    const bool bounded = bounds && fused && n > 0;
+    BoundsState b{};
+    if (bounded) b = carve_bounds(bounds, n, d, k);
+    const bool clear = !(flags & KMC_PASS_ACCUMULATE);
+    e = launch_prepare(C, k, d, colmax, n_total, ws.prep, ws.scale_x, ws.hc,
+                       clear ? reinterpret_cast<long long*>(totals) : nullptr, clear ? ws.counters : nullptr,
+                       bounded ? b.meta : nullptr, bounded ? b.cprev : nullptr, st);
     if (e != cudaSuccess) return cuda_fail(e, who);
     if (n == 0) return KMC_OK;
     PassArgs a;
@@ -166,11 +167,7 @@ int pass_impl(const char* who, const float* X, int64_t n, int d, const float* C,
     a.ctile = 0;
     a.key_keep = 0;
     a.brows = nullptr;
-    const bool fused = !(flags & KMC_PASS_GENERIC) && lowd_supports(d, k);
-    if (bounds && fused) {
-        BoundsState b = carve_bounds(bounds, n, d, k);
-        e = launch_bounds_prepare(C, k, d, b.meta, b.cprev, ws.prep, st);
-        if (e != cudaSuccess) return cuda_fail(e, who);
+    if (bounded) {
         a.brows = b.rows;
         a.labels = nullptr;
         a.best = nullptr;
@@ -248,13 +245,10 @@ int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, cons
                     split_centers_bytes(d, k));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e;
-    if (!(flags & KMC_PASS_ACCUMULATE)) {
-        e = cudaMemsetAsync(totals, 0, sizeof(int64_t) * (size_t)k * (d + 2), st);
-        if (e != cudaSuccess) return cuda_fail(e, who);
-        e = cudaMemsetAsync(ws.counters, 0, sizeof(long long) * 8, st);
-        if (e != cudaSuccess) return cuda_fail(e, who);
-    }
-    e = launch_prepare(C, k, d, colmax, n_total, ws.prep, ws.scale_x, ws.hc, st);
+    const bool clear = !(flags & KMC_PASS_ACCUMULATE);
+    e = launch_prepare(C, k, d, colmax, n_total, ws.prep, ws.scale_x, ws.hc,
+                       clear ? reinterpret_cast<long long*>(totals) : nullptr, clear ? ws.counters : nullptr, nullptr,
+                       nullptr, st);
     if (e != cudaSuccess) return cuda_fail(e, who);
     if (n == 0) return KMC_OK;
     const RowSplit rs = carve_rows(split, n, d);
@@ -299,6 +293,56 @@ int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, cons
     a.brows = nullptr;
     e = launch_accum_split(a, rs, cs, st);
     if (e != cudaSuccess) return cuda_fail(e, who);
+    return KMC_OK;
+}
+
+size_t kmc_exchange_bytes(int k, int d) { return exchange_bytes(k, d); }
+
+int kmc_exchange_alloc(size_t bytes, void** ptr, void* handle) {
+    if (!ptr || !handle) return fail(KMC_ERR_INVALID, "kmc_exchange_alloc: null pointer");
+    if (bytes < (size_t)kExchangeHeader) return fail(KMC_ERR_INVALID, "kmc_exchange_alloc: %zu bytes", bytes);
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_exchange_alloc: cudaMalloc");
+    e = cudaMemset(p, 0, bytes);
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail(e, "kmc_exchange_alloc: cudaIpcGetMemHandle");
+    }
+    *ptr = p;
+    return KMC_OK;
+}
+
+int kmc_exchange_open(const void* handle, void** ptr) {
+    if (!ptr || !handle) return fail(KMC_ERR_INVALID, "kmc_exchange_open: null pointer");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_exchange_open: cudaIpcOpenMemHandle");
+    return KMC_OK;
+}
+
+int kmc_exchange_close(void* ptr, int own) {
+    if (!ptr) return KMC_OK;
+    cudaError_t e = own ? cudaFree(ptr) : cudaIpcCloseMemHandle(ptr);
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_exchange_close");
+    return KMC_OK;
+}
+
+int kmc_exchange_sum(int64_t* totals, int k, int d, const uint64_t* peers, int world, int rank, uint64_t step,
+                     void* workspace, size_t ws_bytes, void* stream) {
+    if (int s = check_shape(0, d, k)) return s;
+    if (!totals || !peers || !workspace) return fail(KMC_ERR_INVALID, "kmc_exchange_sum: null pointer");
+    if (world < 1 || world > 64 || rank < 0 || rank >= world)
+        return fail(KMC_ERR_INVALID, "kmc_exchange_sum: rank %d of %d (at most 64 GPUs)", rank, world);
+    Workspace ws = carve(workspace, d, k);
+    if (ws_bytes < ws.bytes)
+        return fail(KMC_ERR_INVALID, "kmc_exchange_sum: workspace of %zu bytes, need %zu", ws_bytes, ws.bytes);
+    cudaError_t e = launch_exchange_sum(reinterpret_cast<long long*>(totals), k, d,
+                                        reinterpret_cast<const unsigned long long*>(peers), world, rank, step,
+                                        ws.counters, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_exchange_sum");
     return KMC_OK;
 }
 

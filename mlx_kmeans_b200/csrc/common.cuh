@@ -36,6 +36,7 @@ struct Prep {
 
 enum : int {
     kFlagNonFinite = 1,     // data or centers hold NaN / inf, or a distance overflowed float32
+    kFlagExchange = 2,      // the peer-memory all-reduce of the totals timed out waiting for a peer
 };
 
 // Device statistics written by the finish kernel; read by the host once per pass.

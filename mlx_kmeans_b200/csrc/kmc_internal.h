@@ -62,11 +62,11 @@ struct FarWorkspace {
 FarWorkspace carve_far(void* base, int64_t cand_rows);
 
 cudaError_t launch_colmax(const float* X, int64_t n, int d, unsigned int* colmax, cudaStream_t st);
+// per-pass constants; optionally clears the totals and counters, and (bmeta != nullptr) prepares a bounded pass
 cudaError_t launch_prepare(const float* C, int k, int d, const unsigned int* colmax, int64_t n_total, Prep* prep,
-                           double* scale_x, float* hc, cudaStream_t st);
+                           double* scale_x, float* hc, long long* zero_totals, long long* zero_counters,
+                           double* bmeta, float* bcprev, cudaStream_t st);
 cudaError_t launch_pass_generic(PassArgs a, cudaStream_t st);
-cudaError_t launch_bounds_prepare(const float* C, int k, int d, double* meta, float* cprev, Prep* prep,
-                                  cudaStream_t st);
 // Specialised low-dimensional fused pass; returns cudaErrorNotSupported when (d, k) has no instance.
 cudaError_t launch_pass_lowd(PassArgs a, cudaStream_t st);
 int64_t lowd_block_rows();
@@ -118,6 +118,12 @@ cudaError_t launch_split_rows(const float* X, int64_t n, int d, const RowSplit& 
 cudaError_t launch_split_centers(const float* C, int k, int d, const CenterSplit& s, cudaStream_t st);
 cudaError_t launch_assign_tc(const TcSplit& s, cudaStream_t st);
 cudaError_t launch_accum_split(PassArgs a, const RowSplit& rs, const CenterSplit& cs, cudaStream_t st);
+
+// Peer-memory all-reduce of the totals (exchange.cu).
+constexpr int kExchangeHeader = 512;      // 64 flags of 8 bytes before the two slots
+size_t exchange_bytes(int k, int d);
+cudaError_t launch_exchange_sum(long long* totals, int k, int d, const unsigned long long* peers, int world, int rank,
+                                unsigned long long step, long long* counters, cudaStream_t st);
 
 cudaError_t launch_far_rows(const float* X, int64_t n, int d, const int32_t* labels, const float* best, int64_t row0,
                             int64_t cand_rows, uint32_t* cands, const FarWorkspace& ws, cudaStream_t st);

@@ -31,8 +31,46 @@ __global__ void k_colmax(const float* __restrict__ X, int64_t total, int d, int6
         if (smax[j]) atomicMax(&colmax[j], smax[j]);
 }
 
+// ---------------------------------------------------------------- per-row bounds: drift of the centers
+// Run by the prepare CTA after the constants.  The drift of center c is |c - c_prev| (float64, rounded up); the
+// bounds lose max_c drift per pass (Hamerly: the distance to any other center shrinks by at most its move).
+// The running total goes to the pass as float32 bounds on both sides; the current centers become c_prev.  When
+// the bounds are not valid yet the pass writes them all, so they are valid afterwards with zero drift.
+__device__ void bounds_prepare_cta(const float* __restrict__ C, int k, int d, double* __restrict__ meta,
+                                   float* __restrict__ cprev, Prep* __restrict__ prep) {
+    __shared__ double s_dmax[32];
+    const bool valid = meta[1] != 0.0;
+    double mx = 0.0;
+    if (valid) {
+        for (int c = threadIdx.x; c < k; c += blockDim.x) {
+            double s = 0.0;
+            for (int j = 0; j < d; j++) {
+                double q = (double)C[(int64_t)c * d + j] - (double)cprev[(int64_t)c * d + j];
+                s = __fma_ru(q, q, s);
+            }
+            mx = fmax(mx, __dsqrt_ru(s));
+        }
+    }
+    for (int o = 16; o; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) s_dmax[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) mx = fmax(mx, s_dmax[w]);
+        const double cum = valid ? __dadd_ru(meta[0], mx) : 0.0;
+        prep->bvalid = valid ? 1 : 0;
+        prep->bcum_lo = __double2float_rd(cum);
+        prep->bcum_up = __double2float_ru(cum);
+        meta[0] = cum;
+        meta[1] = 1.0;
+    }
+    __syncthreads();
+    for (int64_t e = threadIdx.x; e < (int64_t)k * d; e += blockDim.x) cprev[e] = C[e];
+}
+
 // ---------------------------------------------------------------- per-pass constants
-// One CTA.  Screen constants per center, the fixed-point grids, and the window of the float32 screen.
+// One CTA.  Screen constants per center, the fixed-point grids, and the window of the float32 screen; it also
+// clears the pass's totals and counters (when given: small totals, else the caller clears them) and, for a
+// bounded pass, updates the drift of the centers (bounds_prepare_cta).
 //
 // Screen: score_c = |c|^2/2 - x.c, an fma chain of d steps from h_c = |c|^2/2 (itself d fmas).
 // |score_c(fp32) - score_c| <= 1.5 gamma_{d+1} (|x|^2 + |c|^2), gamma_n = n u / (1 - n u), u = 2^-24,
@@ -41,11 +79,16 @@ __global__ void k_colmax(const float* __restrict__ X, int64_t total, int d, int6
 // float32 winner is the float64 winner; otherwise the row is re-scored in float64.
 __global__ void k_prepare(const float* __restrict__ C, int k, int d, const unsigned int* __restrict__ colmax,
                           int64_t n_total, Prep* __restrict__ prep, double* __restrict__ scale_x,
-                          float* __restrict__ hc) {
+                          float* __restrict__ hc, long long* __restrict__ zero_totals, int zero_n,
+                          long long* __restrict__ zero_counters, double* __restrict__ bmeta,
+                          float* __restrict__ bcprev) {
     __shared__ float s_max[32];
     __shared__ float s_cmax2[32];
     __shared__ int s_bad;
     if (threadIdx.x == 0) s_bad = 0;
+    if (zero_totals)
+        for (int e = threadIdx.x; e < zero_n; e += blockDim.x) zero_totals[e] = 0;
+    if (zero_counters && threadIdx.x < 8) zero_counters[threadIdx.x] = 0;
     __syncthreads();
     float mx = 0.0f, cm2 = 0.0f;
     int bad = 0;
@@ -94,6 +137,10 @@ __global__ void k_prepare(const float* __restrict__ C, int k, int d, const unsig
         p.bcum_up = 0.0f;
         p.pad = 0;
         *prep = p;
+    }
+    if (bmeta) {
+        __syncthreads();
+        bounds_prepare_cta(C, k, d, bmeta, bcprev, prep);
     }
 }
 
@@ -203,50 +250,16 @@ cudaError_t launch_colmax(const float* X, int64_t n, int d, unsigned int* colmax
 }
 
 cudaError_t launch_prepare(const float* C, int k, int d, const unsigned int* colmax, int64_t n_total, Prep* prep,
-                           double* scale_x, float* hc, cudaStream_t st) {
-    k_prepare<<<1, 1024, 0, st>>>(C, k, d, colmax, n_total, prep, scale_x, hc);
-    return cudaGetLastError();
-}
-
-// ---------------------------------------------------------------- per-row bounds: drift of the centers
-// One CTA, after k_prepare.  The drift of center c is |c - c_prev| (float64, rounded up); the bounds lose
-// max_c drift per pass (Hamerly: the distance to any other center shrinks by at most its move).  The running
-// total goes to the pass as float32 bounds on both sides; the current centers become c_prev.  When the bounds
-// are not valid yet the pass writes them all, so they are valid afterwards with zero drift.
-__global__ void k_bounds_prepare(const float* __restrict__ C, int k, int d, double* __restrict__ meta,
-                                 float* __restrict__ cprev, Prep* __restrict__ prep) {
-    __shared__ double s_max[32];
-    const bool valid = meta[1] != 0.0;
-    double mx = 0.0;
-    if (valid) {
-        for (int c = threadIdx.x; c < k; c += blockDim.x) {
-            double s = 0.0;
-            for (int j = 0; j < d; j++) {
-                double q = (double)C[(int64_t)c * d + j] - (double)cprev[(int64_t)c * d + j];
-                s = __fma_ru(q, q, s);
-            }
-            mx = fmax(mx, __dsqrt_ru(s));
-        }
+                           double* scale_x, float* hc, long long* zero_totals, long long* zero_counters,
+                           double* bmeta, float* bcprev, cudaStream_t st) {
+    const int64_t zn = (int64_t)k * (d + 2);
+    if (zero_totals && zn > 16384) {           // large totals: a memset is faster than one CTA
+        cudaError_t e = cudaMemsetAsync(zero_totals, 0, sizeof(long long) * (size_t)zn, st);
+        if (e != cudaSuccess) return e;
+        zero_totals = nullptr;
     }
-    for (int o = 16; o; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = mx;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < (int)(blockDim.x >> 5); w++) mx = fmax(mx, s_max[w]);
-        const double cum = valid ? __dadd_ru(meta[0], mx) : 0.0;
-        prep->bvalid = valid ? 1 : 0;
-        prep->bcum_lo = __double2float_rd(cum);
-        prep->bcum_up = __double2float_ru(cum);
-        meta[0] = cum;
-        meta[1] = 1.0;
-    }
-    __syncthreads();
-    for (int64_t e = threadIdx.x; e < (int64_t)k * d; e += blockDim.x) cprev[e] = C[e];
-}
-
-cudaError_t launch_bounds_prepare(const float* C, int k, int d, double* meta, float* cprev, Prep* prep,
-                                  cudaStream_t st) {
-    k_bounds_prepare<<<1, 1024, 0, st>>>(C, k, d, meta, cprev, prep);
+    k_prepare<<<1, 1024, 0, st>>>(C, k, d, colmax, n_total, prep, scale_x, hc, zero_totals, (int)zn, zero_counters,
+                                  bmeta, bcprev);
     return cudaGetLastError();
 }
 
