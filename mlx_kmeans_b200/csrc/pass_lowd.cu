@@ -189,6 +189,47 @@ __device__ __forceinline__ void ldg_row(float (&x)[D], const float* p) {
             asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(x[j]) : "l"(p + j));
     }
 }
+// Rows of an even number of columns as D/2 packed pairs (one 64-bit register pair each), so the packed float32
+// arithmetic of the bounded kernel needs no register moves: 16-byte pieces where the row is 16-byte aligned
+// (D % 4 == 0), else 8-byte pieces.
+template <int D>
+__device__ __forceinline__ void ldg_row2(unsigned long long (&x)[D / 2], const float* p) {
+    if constexpr (D % 4 == 0) {
+#pragma unroll
+        for (int q = 0; q < D / 4; q++)
+            asm volatile("ld.global.nc.L1::no_allocate.v2.u64 {%0, %1}, [%2];" : "=l"(x[2 * q]), "=l"(x[2 * q + 1])
+                         : "l"(p + 4 * q));
+    } else {
+#pragma unroll
+        for (int q = 0; q < D / 2; q++)
+            asm volatile("ld.global.nc.L1::no_allocate.u64 %0, [%1];" : "=l"(x[q]) : "l"(p + 2 * q));
+    }
+}
+template <int D>
+__device__ __forceinline__ void lds_row2(unsigned long long (&x)[D / 2], unsigned saddr) {
+    if constexpr (D % 4 == 0) {
+#pragma unroll
+        for (int q = 0; q < D / 4; q++)
+            asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(x[2 * q]), "=l"(x[2 * q + 1]) : "r"(saddr + 16 * q));
+    } else {
+#pragma unroll
+        for (int q = 0; q < D / 2; q++) asm volatile("ld.shared.u64 %0, [%1];" : "=l"(x[q]) : "r"(saddr + 8 * q));
+    }
+}
+template <int D>
+__device__ __forceinline__ void sts_row2(unsigned saddr, const unsigned long long (&x)[D / 2]) {
+    if constexpr (D % 4 == 0) {
+#pragma unroll
+        for (int q = 0; q < D / 4; q++)
+            asm volatile("st.shared.v2.u64 [%0], {%1, %2};" ::"r"(saddr + 16 * q), "l"(x[2 * q]), "l"(x[2 * q + 1])
+                         : "memory");
+    } else {
+#pragma unroll
+        for (int q = 0; q < D / 2; q++)
+            asm volatile("st.shared.u64 [%0], %1;" ::"r"(saddr + 8 * q), "l"(x[q]) : "memory");
+    }
+}
+
 __device__ __forceinline__ unsigned ldg_u32(const uint32_t* p) {
     unsigned v;
     asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
@@ -714,10 +755,10 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(PlainSmem<D, K>::total) 
 // screened 32 at a time, one per lane, reading the row again (from L2) and the packed centers from shared
 // memory at the point of use, so the screen holds no registers across the row loop.  Before the bounds exist
 // (the first pass after a reset) every row takes that route and gets its word.
-// CTAs per SM of the bounded kernel: four (128 registers) up to five columns, three (168) above, where the
+// CTAs per SM of the bounded kernel: four (128 registers) up to four columns, three (168) above, where the
 // rows in flight and the screen's operands need more registers
 constexpr int bounded_ctas(int d, size_t smem) {
-    const int cap = KMC_BOUNDED_MAX_CTAS ? KMC_BOUNDED_MAX_CTAS : d <= 5 ? 4 : 3;
+    const int cap = KMC_BOUNDED_MAX_CTAS ? KMC_BOUNDED_MAX_CTAS : d <= 4 ? 4 : 3;
     return ctas_per_sm(smem) < cap ? ctas_per_sm(smem) : cap;
 }
 
@@ -761,15 +802,27 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
     const int64_t nblk = (n + kBlockRows - 1) / kBlockRows;
     constexpr int XSTEP = kThreads * D;                 // floats between a thread's consecutive rows
     constexpr int NCH = kRowsPerLane / U;
+    // rows in flight; an even number of columns is kept as packed pairs end to end (PK), so the packed float32
+    // arithmetic needs no register moves
+    constexpr bool PK = D % 2 == 0;
+    constexpr int DH = (D + 1) / 2;
     float xq[P][D];
+    unsigned long long xq2[P][DH];
     unsigned wq[P];
-    auto fetch = [&](float (&x)[D], unsigned& w, const float* px, const uint32_t* pw, bool ok) {
+    auto fetch = [&](float (&x)[D], unsigned long long (&x2)[DH], unsigned& w, const float* px, const uint32_t* pw,
+                     bool ok) {
         if (ok) {
-            ldg_row<D>(x, px);
+            if constexpr (PK) ldg_row2<D>(x2, px);
+            else ldg_row<D>(x, px);
             w = ldg_u32(pw);
         } else {
+            if constexpr (PK) {
 #pragma unroll
-            for (int j = 0; j < D; j++) x[j] = 0.0f;
+                for (int j = 0; j < DH; j++) x2[j] = 0ull;
+            } else {
+#pragma unroll
+                for (int j = 0; j < D; j++) x[j] = 0.0f;
+            }
             w = 0u;
         }
     };
@@ -777,11 +830,14 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
         const int64_t r0 = (int64_t)blockIdx.x * kBlockRows + tid;
 #pragma unroll
         for (int q = 0; q < P; q++)
-            fetch(xq[q], wq[q], a.X + (r0 + q * kThreads) * D, a.brows + r0 + q * kThreads, r0 + q * kThreads < n);
+            fetch(xq[q], xq2[q], wq[q], a.X + (r0 + q * kThreads) * D, a.brows + r0 + q * kThreads,
+                  r0 + q * kThreads < n);
     }
     // the center of the row in flight's stored label (a label past the end is masked: inside the 32-row table)
     float cr[D];
-    load_row<D>(cr, st.cs_s + (wq[0] & MASK) * (unsigned)(D * 4));
+    unsigned long long cr2[DH];
+    if constexpr (PK) lds_row2<D>(cr2, st.cs_s + (wq[0] & MASK) * (unsigned)(D * 4));
+    else load_row<D>(cr, st.cs_s + (wq[0] & MASK) * (unsigned)(D * 4));
 
     int* queue = queue_all + warp * kQueue;
     int qhead = 0, qcount = 0;
@@ -837,15 +893,39 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
                     const int l = (int)(w & MASK);
                     // this lane's slot of the stored label first: its latency overlaps the arithmetic
                     const unsigned sa = st.slot_addr(l);
-                    float sl[D];
-                    load_row<D>(sl, sa);
-                    float t[D];
-                    const float b = st.residual(xq[q], cr, t);
-                    const bool keep = bounded && valid && st.holds(w, b);
-                    load_row<D>(cr, st.cs_s + (wq[(s + 1) % P] & MASK) * (unsigned)(D * 4));   // row r + 1's
+                    bool keep;
+                    float b;
+                    if constexpr (PK) {
+                        // residual t = x - c and best = sum t^2 in column order, as LowdRow::residual, on pairs
+                        unsigned long long sl2[DH], t2[DH];
+                        lds_row2<D>(sl2, sa);
+                        b = 0.0f;
+#pragma unroll
+                        for (int i = 0; i < DH; i++) {
+                            t2[i] = sub2(xq2[q][i], cr2[i]);
+                            const unsigned long long q2 = mul2(t2[i], t2[i]);
+                            b = i == 0 ? lo_of(q2) : __fadd_rn(b, lo_of(q2));
+                            b = __fadd_rn(b, hi_of(q2));
+                        }
+                        keep = bounded && valid && st.holds(w, b);
+                        lds_row2<D>(cr2, st.cs_s + (wq[(s + 1) % P] & MASK) * (unsigned)(D * 4));   // row r + 1's
+                        if (keep) {
+#pragma unroll
+                            for (int i = 0; i < DH; i++) sl2[i] = add2(sl2[i], t2[i]);
+                            sts_row2<D>(sa, sl2);
+                        }
+                    } else {
+                        float sl[D], t[D];
+                        load_row<D>(sl, sa);
+                        b = st.residual(xq[q], cr, t);
+                        keep = bounded && valid && st.holds(w, b);
+                        load_row<D>(cr, st.cs_s + (wq[(s + 1) % P] & MASK) * (unsigned)(D * 4));   // row r + 1's
+                        if (keep) {
+                            add_into<D>(sl, t);
+                            store_row<D>(sa, sl);
+                        }
+                    }
                     if (keep) {
-                        add_into<D>(sl, t);
-                        store_row<D>(sa, sl);
                         red_u32(st.cnt_addr(l), LowdRow<D, K>::cnt_one(l));
                         st.ichunk = __fadd_rn(st.ichunk, b);
                     }
@@ -858,10 +938,10 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
                     }
                     // the refill: row r + P, in this chunk or the next
                     if (s + P < U)                       // resolved at compile time: the loop is unrolled
-                        fetch(xq[q], wq[q], xc + (s + P) * XSTEP, wc + (s + P) * kThreads,
+                        fetch(xq[q], xq2[q], wq[q], xc + (s + P) * XSTEP, wc + (s + P) * kThreads,
                               !CHECK || base + (int64_t)(r + P) * kThreads < n);
                     else
-                        fetch(xq[q], wq[q], xn + (s + P - U) * XSTEP, wn + (s + P - U) * kThreads,
+                        fetch(xq[q], xq2[q], wq[q], xn + (s + P - U) * XSTEP, wn + (s + P - U) * kThreads,
                               !CHECK || nrow + (int64_t)(s + P - U) * kThreads < n);
                     if (s % 8 == 7) st.chunk_done();
                 }
