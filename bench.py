@@ -251,6 +251,7 @@ def main():
     clocks.start()
     time.sleep(0.2)
     t0.record(st)
+    h0 = time.perf_counter()
     for i in range(K):
         Cin, Cout = Cs[i % 2], Cs[(i + 1) % 2]
         ev[i][0].record(st)
@@ -270,6 +271,7 @@ def main():
         _lib.check(L.kmc_finish(b["totals"].data_ptr(), k, d, None, 0, 1, Cout.data_ptr(), stats[i].data_ptr(),
                                 b["ws"].data_ptr(), b["wsb"], sp))
     t1.record(st)
+    host_ms = (time.perf_counter() - h0) * 1e3 / K      # host time to issue one step (the GPU must not wait)
     torch.cuda.synchronize()
     clk = clocks.stop()
     if world > 1:
@@ -360,7 +362,11 @@ def main():
                       "peak_source": (f"{src} bf16_tflops_sustained (MEASURED_PEAKS.json)" if src == "measured"
                                       else "fallback")}),
         "clocks": clk,
-        "gpu_launches": (5 if tc else 4 if bounded else 3) * K,   # prepare (+ split or bounds), pass, finish
+        # per step: k_prepare, the pass (tensor cores: k_split_centers, k_assign_tc and the six kernels of the
+        # float64 decision and the per-cluster reduction), k_exchange_sum when the totals go through peer memory,
+        # k_finish
+        "gpu_launches": ((10 if tc else 3) + (1 if world > 1 and ds._xch.get(k) else 0)) * K,
+        "host_enqueue_ms_per_step": host_ms,
         "e2e": e2e,
     }
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -590,25 +590,33 @@ struct LowdRow {
     }
 
     // End of a block: fold the lanes' slots into the CTA's int64 totals (fixed order => deterministic) and
-    // the block's inertia into acc[1].  Lane L folds columns s = c * D + j (s = L, L + 32, ...): the 32 lanes'
-    // partial sums in float64 in a fixed rotation, the cluster's count, then sum x = sum t + count * c rounded
-    // once to the fixed-point grid.
-    __device__ __forceinline__ void fold_block(long long* acc, const double* scale_x, double scale_i, int kSums,
-                                               int kCnts) {
+    // the block's inertia into acc[1].  Counts first: the even and the odd 8-bit fields of each word are summed
+    // over the warp as 16-bit fields (at most 32 * kRowsPerLane < 2^16 each), and lane j < 4 parks the count of
+    // cluster 4 w + j in its own word.  Then lane L folds columns s = c * D + j (s = L, L + 32, ...): the 32
+    // lanes' partial sums in float64 in a fixed rotation, then sum x = sum t + count * c rounded once to the
+    // fixed-point grid.
+    __device__ __forceinline__ void fold_block(long long* acc, const double* scale_x, double scale_i) {
+        static_assert(32 * kRowsPerLane < 65536, "16-bit count fields");
+        __syncwarp();
+#pragma unroll
+        for (int w = 0; w < (K + 3) / 4; w++) {
+            const unsigned v = cnts[w * 32 + lane];
+            const unsigned ev = __reduce_add_sync(0xffffffffu, v & 0x00ff00ffu);          // fields 0 and 2
+            const unsigned od = __reduce_add_sync(0xffffffffu, (v >> 8) & 0x00ff00ffu);   // fields 1 and 3
+            const unsigned f = (lane & 1) ? od : ev;
+            cnts[w * 32 + lane] = lane < 2 ? (f & 0xffffu) : lane < 4 ? (f >> 16) : 0u;
+        }
         __syncwarp();
         for (int s = lane; s < K * D; s += 32) {
             const int c = s / D, j = s % D;
             const float* col = sums + (size_t)c * 32 * D + j;
-            const unsigned* ccol = cnts + (c >> 2) * 32;
-            const int sh = (c & 3) * 8;
             double sum = 0.0;
-            unsigned cnt = 0;
 #pragma unroll 8
             for (int i = 0; i < 32; i++) {
                 const int li = (i + lane) & 31;
                 sum = __dadd_rn(sum, (double)col[li * D]);
-                cnt += (ccol[li] >> sh) & 255u;
             }
+            const unsigned cnt = cnts[(c >> 2) * 32 + (c & 3)];
             if (c < k && cnt) {
                 const double sxv = __fma_rn((double)cnt, (double)cs[c * D + j], sum);
                 atomicAdd(reinterpret_cast<unsigned long long*>(&acc[c * (D + 2) + 2 + j]),
@@ -617,8 +625,10 @@ struct LowdRow {
             }
         }
         __syncwarp();
-        for (int e = lane; e < kCnts; e += 32) cnts[e] = 0u;
-        for (int e = lane; e < kSums; e += 32) sums[e] = 0.0f;
+        if (lane < 4)
+            for (int w = 0; w < (K + 3) / 4; w++) cnts[w * 32 + lane] = 0u;
+        static_assert((K * D * 32) % 64 == 0, "sums slots zeroed as float2");
+        for (int e = lane; e < K * D * 16; e += 32) reinterpret_cast<float2*>(sums)[e] = make_float2(0.0f, 0.0f);
         // inertia of the block: fixed xor-tree over the warp, one quantised add
         double in = inert;
 #pragma unroll
@@ -741,7 +751,7 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(PlainSmem<D, K>::total) 
         if (clean) steps(std::integral_constant<bool, false>{});
         else steps(std::integral_constant<bool, true>{});
         st.chunk_done();
-        st.fold_block(acc, a.scale_x, prep.scale_i, L::kSums, L::kCnts);
+        st.fold_block(acc, a.scale_x, prep.scale_i);
     }
     cp_wait<0>();
     __syncthreads();
@@ -951,7 +961,7 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
         else steps(std::integral_constant<bool, true>{});
         if (qcount > 0) flush(qcount);
         st.chunk_done();
-        st.fold_block(acc, a.scale_x, prep.scale_i, L::kSums, L::kCnts);
+        st.fold_block(acc, a.scale_x, prep.scale_i);
     }
     __syncthreads();
     st.finish(acc, a, tid);
