@@ -183,6 +183,12 @@ int kmc_stats_read(const kmc_stats *stats_dev, kmc_stats *stats_host, void *stre
 int kmc_totals_unpack(const int64_t *totals, int k, int d, double *sums, int64_t *counts, double *inertia,
                       void *workspace, size_t ws_bytes, void *stream);
 
+/* The float64 distance labels are decided by: out[i] = D64(X[i], C[i]) for m row pairs (X, C: device,
+ * m x d float32; out: device, m float64) -- (double)x_j - (double)c_j, squared, summed in NumPy's pairwise
+ * order, as the reference's accuracy check computes it (tests/accuracy.py:31-51).  One warp per pair, the
+ * same arithmetic the passes re-score near ties with; for auditing labels. */
+int kmc_d64(const float *X, const float *C, int d, int64_t m, double *out, void *stream);
+
 /* ---------------------------------------------------------------- k-means++
  * Replaces core.py:153-192 `kmeans_pp_init(parts, rows, k, rng, sample)` after the host has drawn the
  * sample rows and gathered them into S (m x d, device): greedy k-means++ with 2 + floor(ln k) candidates

@@ -52,6 +52,7 @@ SIGNATURES = {
     "kmc_finish": (_int, [_vp, _int, _int, _vp, _i64, _int, _vp, _vp, _vp, _sz, _vp]),
     "kmc_stats_read": (_int, [_vp, _vp, _vp]),
     "kmc_totals_unpack": (_int, [_vp, _int, _int, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "kmc_d64": (_int, [_vp, _vp, _int, _i64, _vp, _vp]),
     "kmc_pp_workspace_bytes": (_sz, [_i64, _int, _int]),
     "kmc_pp_init": (_int, [_vp, _i64, _int, _int, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "kmc_gen": (_int, [_int, _vp, _i64, _int, _i64, ctypes.c_uint64, _vp, _vp, _int, ctypes.c_float,

@@ -153,6 +153,7 @@ int pass_impl(const char* who, const float* X, int64_t n, int d, const float* C,
     PassArgs a;
     a.X = X;
     a.n = n;
+    a.n_total = n_total;
     a.d = d;
     a.k = k;
     a.C = C;
@@ -277,6 +278,7 @@ int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, cons
     PassArgs a;
     a.X = X;
     a.n = n;
+    a.n_total = n_total;
     a.d = d;
     a.k = k;
     a.C = C;
@@ -392,6 +394,15 @@ int kmc_totals_unpack(const int64_t* totals, int k, int d, double* sums, int64_t
     cudaError_t e = launch_unpack(reinterpret_cast<const long long*>(totals), k, d, ws.scale_x, ws.prep, ws.counters, sums, counts,
                                   inertia, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "kmc_totals_unpack");
+    return KMC_OK;
+}
+
+int kmc_d64(const float* X, const float* C, int d, int64_t m, double* out, void* stream) {
+    if (int s = check_shape(m, d, 1)) return s;
+    if (m > 0 && (!X || !C || !out)) return fail(KMC_ERR_INVALID, "kmc_d64: null pointer");
+    if (m == 0) return KMC_OK;
+    cudaError_t e = launch_d64(X, C, d, m, out, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_d64");
     return KMC_OK;
 }
 

@@ -149,6 +149,100 @@ __device__ inline double d64_pairwise(const float* x, const float* c, int d) {
     return __dadd_rn(0.0, ret);
 }
 
+// D64 by one warp, bit-identical to d64_pairwise (every lane returns the value).  The leaves of the split tree
+// (left to right) are listed by lane 0; leaf L's eight running partials are chains 8 L + r, spread over the
+// lanes 32 at a time; a leaf's partials meet in the reference's order ((r0 + r1) + (r2 + r3)) + ((r4 + r5) +
+// (r6 + r7)) through xor shuffles inside eight-lane groups (float64 addition commutes exactly), its tail terms
+// follow in order, and lane 0 joins the leaves by the tree's post-order walk.  Scratch: kD64WarpScratch bytes of
+// shared memory per warp, 8-byte aligned.
+constexpr int kD64MaxLeaves = 64;                               // d <= kMaxDims: leaves of more than 64 terms
+constexpr int kD64WarpScratch = kD64MaxLeaves * (8 + 8);
+__device__ inline double d64_warp(const float* x, const float* c, int d, void* scratch) {
+    const int lane = threadIdx.x & 31;
+    if (d < 8) {
+        double v = 0.0;
+        if (lane == 0) v = d64_pairwise(x, c, d);
+        return __shfl_sync(0xffffffffu, v, 0);
+    }
+    double* leafv = static_cast<double*>(scratch);
+    int2* leaf = reinterpret_cast<int2*>(leafv + kD64MaxLeaves);     // (lo, n)
+    int nleaf = 0;
+    if (lane == 0) {
+        int2 st[16];
+        int sp = 0;
+        st[0] = make_int2(0, d);
+        while (sp >= 0) {
+            const int2 f = st[sp--];
+            if (f.y <= 128) {
+                leaf[nleaf++] = f;
+                continue;
+            }
+            int n2 = f.y / 2;
+            n2 -= n2 % 8;
+            st[++sp] = make_int2(f.x + n2, f.y - n2);               // right after left
+            st[++sp] = make_int2(f.x, n2);
+        }
+    }
+    nleaf = __shfl_sync(0xffffffffu, nleaf, 0);
+    __syncwarp();
+    for (int base = 0; base < 8 * nleaf; base += 32) {
+        const int q = base + lane;
+        const bool live = q < 8 * nleaf;
+        const int L = live ? q >> 3 : 0, r = q & 7;
+        const int2 lf = leaf[L];
+        double p = 0.0;
+        if (live) {
+            p = d64_term(x, c, lf.x + r);
+            for (int i = 8 + r; i < lf.y - (lf.y % 8); i += 8) p = __dadd_rn(p, d64_term(x, c, lf.x + i));
+        }
+        p = __dadd_rn(p, __shfl_xor_sync(0xffffffffu, p, 1));
+        p = __dadd_rn(p, __shfl_xor_sync(0xffffffffu, p, 2));
+        p = __dadd_rn(p, __shfl_xor_sync(0xffffffffu, p, 4));
+        if (live && r == 0) {
+            for (int i = lf.y - (lf.y % 8); i < lf.y; i++) p = __dadd_rn(p, d64_term(x, c, lf.x + i));
+            leafv[L] = p;
+        }
+    }
+    __syncwarp();
+    double ret = 0.0;
+    if (lane == 0) {
+        if (d <= 128) {
+            ret = leafv[0];
+        } else {
+            struct Frame { int n, state; double left; };
+            Frame st[16];
+            int sp = 0, next = 0;
+            st[0] = {d, 0, 0.0};
+            while (true) {
+                Frame& f = st[sp];
+                if (f.n <= 128) {
+                    ret = leafv[next++];
+                    if (sp == 0) break;
+                    sp--;
+                    continue;
+                }
+                int n2 = f.n / 2;
+                n2 -= n2 % 8;
+                if (f.state == 0) {
+                    f.state = 1;
+                    st[++sp] = {n2, 0, 0.0};
+                } else if (f.state == 1) {
+                    f.left = ret;
+                    f.state = 2;
+                    st[++sp] = {f.n - n2, 0, 0.0};
+                } else {
+                    ret = __dadd_rn(f.left, ret);
+                    if (sp == 0) break;
+                    sp--;
+                }
+            }
+        }
+        ret = __dadd_rn(0.0, ret);
+    }
+    __syncwarp();
+    return __shfl_sync(0xffffffffu, ret, 0);
+}
+
 // ---------------------------------------------------------------- Philox4x32-10
 
 // Salmon, Moraes, Dror, Shaw, SC'11: ten rounds of two 32x32->64 multiplies with a Weyl key schedule.

@@ -119,7 +119,11 @@ cudaError_t launch_far_rows(const float* X, int64_t n, int d, const int32_t* lab
 }
 
 // ---------------------------------------------------------------- finish
-// One CTA of 1024 threads.  totals are updated in place by the relocation (counts and sums move).
+// One CTA of 1024 threads.  totals are updated in place by the relocation (counts and sums move).  Above
+// kFinishOneCta center values the divide (steps 4 and 5) runs on a grid instead (k_finish_centers): the CTA
+// leaves the largest cluster in counters[3] and whether to write the centers in counters[4].
+constexpr int64_t kFinishOneCta = 32768;
+
 struct FinishArgs {
     long long* totals;
     int k, d;
@@ -133,7 +137,16 @@ struct FinishArgs {
     long long* counters;
     int* reloc;
     long long* empty;
+    bool grid_centers;
 };
+
+// center c, column j of the new centers (cnt = the cluster's count, > 0): sums / counts in float64, rounded
+// once to float32; a cluster relocated into from a single row is that row
+__device__ __forceinline__ float new_center(const FinishArgs& a, int c, int j, long long cnt) {
+    if (a.reloc[c] >= 0 && cnt == 1) return __uint_as_float(a.cands[(int64_t)a.reloc[c] * (a.d + 4) + 4 + j]);
+    const double s = __dmul_rn((double)a.totals[(size_t)c * (a.d + 2) + 2 + j], 1.0 / a.scale_x[j]);
+    return __double2float_rn(__ddiv_rn(s, (double)cnt));
+}
 
 __global__ void __launch_bounds__(1024) k_finish(FinishArgs a) {
     const int k = a.k, d = a.d, W = d + 2;
@@ -215,6 +228,7 @@ __global__ void __launch_bounds__(1024) k_finish(FinishArgs a) {
     }
     __syncthreads();
     if (!sh_write) {
+        if (tid == 0 && a.grid_centers) a.counters[4] = 0;
         if (tid == 0) {
             Stats s;
             s.inertia = (double)sh_inert * a.prep->inv_scale_i;
@@ -249,28 +263,25 @@ __global__ void __launch_bounds__(1024) k_finish(FinishArgs a) {
         for (int w = 1; w < nt / 32; w++)
             if (s_bigc[w] > b || (s_bigc[w] == b && s_bigi[w] < i)) { b = s_bigc[w]; i = s_bigi[w]; }
         sh_big = i;
-    }
-    // 4. C_new = sums / counts (float64, rounded once to float32); a relocated cluster is its row
-    const int R = d + 4;
-    for (int64_t e = tid; e < (int64_t)k * d; e += nt) {
-        const int c = (int)(e / d), j = (int)(e % d);
-        const long long cnt = a.totals[(size_t)c * W];
-        if (cnt <= 0) continue;
-        float v;
-        if (a.reloc[c] >= 0 && cnt == 1) {
-            v = __uint_as_float(a.cands[(int64_t)a.reloc[c] * R + 4 + j]);
-        } else {
-            double s = __dmul_rn((double)a.totals[(size_t)c * W + 2 + j], 1.0 / a.scale_x[j]);
-            v = __double2float_rn(__ddiv_rn(s, (double)cnt));
+        if (a.grid_centers) {
+            a.counters[3] = i;
+            a.counters[4] = 1;
         }
-        a.C_new[e] = v;
     }
-    __syncthreads();
-    // 5. a cluster still empty takes the largest cluster's center (core.py:2241)
-    const int big = sh_big;
-    for (int64_t e = tid; e < (int64_t)k * d; e += nt) {
-        const int c = (int)(e / d), j = (int)(e % d);
-        if (a.totals[(size_t)c * W] <= 0) a.C_new[e] = a.C_new[(int64_t)big * d + j];
+    if (!a.grid_centers) {
+        // 4. C_new = sums / counts (float64, rounded once to float32); a relocated cluster is its row
+        for (int64_t e = tid; e < (int64_t)k * d; e += nt) {
+            const int c = (int)(e / d), j = (int)(e % d);
+            const long long cnt = a.totals[(size_t)c * W];
+            if (cnt > 0) a.C_new[e] = new_center(a, c, j, cnt);
+        }
+        __syncthreads();
+        // 5. a cluster still empty takes the largest cluster's center (core.py:2241)
+        const int big = sh_big;
+        for (int64_t e = tid; e < (int64_t)k * d; e += nt) {
+            const int c = (int)(e / d), j = (int)(e % d);
+            if (a.totals[(size_t)c * W] <= 0) a.C_new[e] = a.C_new[(int64_t)big * d + j];
+        }
     }
     if (tid == 0) {
         Stats s;
@@ -283,6 +294,23 @@ __global__ void __launch_bounds__(1024) k_finish(FinishArgs a) {
         s.screened = a.counters[2];
         s.pad = 0;
         *a.stats = s;
+    }
+}
+
+// Steps 4 and 5 of k_finish over a grid (many center values): every value computed from the totals, an empty
+// cluster's from the largest cluster's, so no value waits for another thread's.
+__global__ void __launch_bounds__(256) k_finish_centers(FinishArgs a) {
+    if (a.counters[4] == 0) return;                  // relocation pending: the centers are not written
+    const int k = a.k, d = a.d, W = d + 2;
+    const int big = (int)a.counters[3];
+    const long long cb = a.totals[(size_t)big * W];
+    const int64_t total = (int64_t)k * d;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(e / d), j = (int)(e % d);
+        const long long cnt = a.totals[(size_t)c * W];
+        if (cnt > 0) a.C_new[e] = new_center(a, c, j, cnt);
+        else a.C_new[e] = cb > 0 ? new_center(a, big, j, cb) : a.C_new[(int64_t)big * d + j];
     }
 }
 
@@ -302,7 +330,14 @@ cudaError_t launch_finish(long long* totals, int k, int d, const uint32_t* cands
     a.counters = ws.counters;
     a.reloc = ws.reloc;
     a.empty = ws.empty;
+    const int64_t total = (int64_t)k * d;
+    a.grid_centers = total > kFinishOneCta;
     k_finish<<<1, 1024, 0, st>>>(a);
+    if (a.grid_centers) {
+        int64_t blocks = (total + 255) / 256;
+        if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
+        k_finish_centers<<<(int)blocks, 256, 0, st>>>(a);
+    }
     return cudaGetLastError();
 }
 

@@ -27,6 +27,7 @@ struct PassArgs {
     int ctile;                // generic kernel: centers per shared tile
     unsigned key_keep;        // fused low-d kernel: ~(center index bits) of a key
     uint32_t* brows;          // bounded pass: one bound word per row (nullptr: plain pass)
+    int64_t n_total;          // rows of the whole dataset (all slices and GPUs): sets the fixed-point grids
 };
 
 // Bounds state of one slice (caller memory): [meta: double drift, int64 valid][centers of the last pass].
@@ -43,7 +44,8 @@ bool lowd_supports(int d, int k);
 // kmc_finish and kmc_totals_unpack read them.
 struct Workspace {
     Prep* prep;
-    long long* counters;      // 8: [0] rows re-scored, [1] flags
+    long long* counters;      // 8: [0] rows re-scored, [1] flags, [2] rows screened, [3] largest cluster and
+                              // [4] centers to write (k_finish -> k_finish_centers)
     double* scale_x;          // d
     float* hc;                // k
     int* reloc;               // k: candidate slot relocated into cluster c, or -1
@@ -61,6 +63,7 @@ struct FarWorkspace {
 };
 FarWorkspace carve_far(void* base, int64_t cand_rows);
 
+cudaError_t launch_d64(const float* X, const float* C, int d, int64_t m, double* out, cudaStream_t st);
 cudaError_t launch_colmax(const float* X, int64_t n, int d, unsigned int* colmax, cudaStream_t st);
 // per-pass constants; optionally clears the totals and counters, and (bmeta != nullptr) prepares a bounded pass
 cudaError_t launch_prepare(const float* C, int k, int d, const unsigned int* colmax, int64_t n_total, Prep* prep,

@@ -99,16 +99,39 @@ __global__ void k_prepare(const float* __restrict__ C, int k, int d, const unsig
         mx = fmaxf(mx, v);
         scale_x[j] = ldexp(1.0, column_shift(v, n_total));
     }
-    for (int c = threadIdx.x; c < k; c += blockDim.x) {
-        float s = 0.0f;
-        for (int j = 0; j < d; j++) {
-            float v = C[(int64_t)c * d + j];
-            if (!isfinite(v)) bad = 1;
-            mx = fmaxf(mx, fabsf(v));
-            s = __fmaf_rn(v, v, s);
+    if (d >= 32) {
+        // a warp per center, coalesced: lane chains of ceil(d/32) fmas and a five-level tree, within the
+        // error of a d-step chain for every d >= 32
+        const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+        for (int c = threadIdx.x >> 5; c < k; c += nw) {
+            float s = 0.0f, m = 0.0f;
+            for (int j = lane; j < d; j += 32) {
+                const float v = C[(int64_t)c * d + j];
+                if (!isfinite(v)) bad = 1;
+                m = fmaxf(m, fabsf(v));
+                s = __fmaf_rn(v, v, s);
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {          // xor tree: every lane ends with the same sum
+                s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            }
+            if (lane == 0) hc[c] = 0.5f * s;
+            mx = fmaxf(mx, m);
+            cm2 = fmaxf(cm2, s);
         }
-        hc[c] = 0.5f * s;
-        cm2 = fmaxf(cm2, s);
+    } else {
+        for (int c = threadIdx.x; c < k; c += blockDim.x) {
+            float s = 0.0f;
+            for (int j = 0; j < d; j++) {
+                float v = C[(int64_t)c * d + j];
+                if (!isfinite(v)) bad = 1;
+                mx = fmaxf(mx, fabsf(v));
+                s = __fmaf_rn(v, v, s);
+            }
+            hc[c] = 0.5f * s;
+            cm2 = fmaxf(cm2, s);
+        }
     }
     for (int o = 16; o; o >>= 1) {
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));

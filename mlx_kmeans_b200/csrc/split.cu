@@ -90,9 +90,11 @@ __global__ void __launch_bounds__(kSplitThreads) k_split_centers(const float* __
     }
 }
 
-// The rows the tensor-core kernel flagged, one thread each: the float64 distance (NumPy-pairwise D64) of each of
-// its (two) candidate centers; the smallest, lowest index on ties, is the label.  Rows with more candidates go
-// on to k_rescore_tc.  (If the tensor-core kernel gave up, k_rescore_tc decides every row.)
+// The rows the tensor-core kernel flagged, one warp each: the float64 distance (NumPy-pairwise D64, summed by
+// the warp, d64_warp) of each of its (two) candidate centers; the smallest, lowest index on ties, is the label.
+// Rows with more candidates go on to k_rescore_tc.  (If the tensor-core kernel gave up, k_rescore_tc decides
+// every row.)
+constexpr int kSplitWarps = kSplitThreads / 32;
 __global__ void __launch_bounds__(kSplitThreads) k_decide_cands(const float* __restrict__ X, int d,
                                                                const float* __restrict__ C,
                                                                const uint32_t* __restrict__ list,
@@ -103,28 +105,31 @@ __global__ void __launch_bounds__(kSplitThreads) k_decide_cands(const float* __r
                                                                unsigned int* __restrict__ novf,
                                                                int32_t* __restrict__ lab,
                                                                long long* __restrict__ counters) {
+    __shared__ __align__(8) unsigned char scratch[kSplitWarps][kD64WarpScratch];
     if (*tc_error) return;
     const int64_t cnt = *nflag;
     if (blockIdx.x == 0 && threadIdx.x == 0 && cnt)
         atomicAdd(reinterpret_cast<unsigned long long*>(&counters[0]), (unsigned long long)cnt);
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; f < cnt; f += stride) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t stride = (int64_t)gridDim.x * kSplitWarps;
+    for (int64_t f = (int64_t)blockIdx.x * kSplitWarps + warp; f < cnt; f += stride) {
         const int64_t row = list[f];
         const int4 c4 = cands[f];
         if (c4.w == -2) {
-            ovf[atomicAdd(novf, 1u)] = (uint32_t)row;
+            if (lane == 0) ovf[atomicAdd(novf, 1u)] = (uint32_t)row;
             continue;
         }
         const float* x = X + row * d;
         const int cs[4] = {c4.x, c4.y, c4.z, c4.w};
         double bv = INFINITY;
         int bi = c4.x;
+#pragma unroll
         for (int i = 0; i < 4; i++) {
             if (cs[i] < 0) continue;
-            const double v = d64_pairwise(x, C + (int64_t)cs[i] * d, d);
+            const double v = d64_warp(x, C + (int64_t)cs[i] * d, d, scratch[warp]);
             if (v < bv || (v == bv && cs[i] < bi)) { bv = v; bi = cs[i]; }
         }
-        lab[row] = bi;
+        if (lane == 0) lab[row] = bi;
     }
 }
 
@@ -134,6 +139,7 @@ __global__ void __launch_bounds__(kSplitThreads) k_decide_cands(const float* __r
 // center within the window of the smallest score; the smallest D64, lowest index on ties, is the label.
 // If the tensor-core kernel gave up, every row is decided here.
 constexpr int kRescoreThreads = 256;
+constexpr int kRescoreList = 1024;       // window candidates decided a warp each; more: a thread each
 __global__ void __launch_bounds__(kRescoreThreads) k_rescore_tc(const float* __restrict__ X, int64_t n, int d,
                                                                const float* __restrict__ C,
                                                                const float* __restrict__ ct,
@@ -147,6 +153,9 @@ __global__ void __launch_bounds__(kRescoreThreads) k_rescore_tc(const float* __r
     extern __shared__ __align__(16) unsigned char smem_raw[];
     float* xs = reinterpret_cast<float*>(smem_raw);                 // d
     float* sc = xs + d;                                              // k scores
+    __shared__ int cl[kRescoreList];                                 // the centers inside the window
+    __shared__ __align__(8) unsigned char scratch[kRescoreThreads / 32][kD64WarpScratch];
+    __shared__ int s_nc;
     __shared__ float rmin[kRescoreThreads / 32];
     __shared__ double rbv[kRescoreThreads / 32];
     __shared__ int rbi[kRescoreThreads / 32];
@@ -179,12 +188,31 @@ __global__ void __launch_bounds__(kRescoreThreads) k_rescore_tc(const float* __r
         m = rmin[0];
         for (int w = 1; w < kRescoreThreads / 32; w++) m = fminf(m, rmin[w]);
         const float lim = m + __fmaf_rn(prep.win_coef, sx2 + prep.cmax2, prep.win_abs);
+        if (tid == 0) s_nc = 0;
+        __syncthreads();
+        for (int c = tid; c < k; c += kRescoreThreads) {
+            if (!(sc[c] > lim)) {                                      // (a NaN score is a candidate too)
+                const int e = atomicAdd(&s_nc, 1);
+                if (e < kRescoreList) cl[e] = c;
+            }
+        }
+        __syncthreads();
+        const int nc = s_nc;
         double bv = INFINITY;
         int bi = 0x7fffffff;
-        for (int c = tid; c < k; c += kRescoreThreads) {
-            if (!(sc[c] <= lim)) continue;     // (a NaN score is a candidate too)
-            const double v = d64_pairwise(xs, C + (int64_t)c * d, d);
-            if (v < bv || (v == bv && c < bi)) { bv = v; bi = c; }
+        if (nc <= kRescoreList) {
+            // a warp per candidate (the list's order does not matter: smallest D64, then lowest index)
+            for (int e = warp; e < nc; e += kRescoreThreads / 32) {
+                const int c = cl[e];
+                const double v = d64_warp(xs, C + (int64_t)c * d, d, scratch[warp]);
+                if (v < bv || (v == bv && c < bi)) { bv = v; bi = c; }
+            }
+        } else {
+            for (int c = tid; c < k; c += kRescoreThreads) {
+                if (sc[c] > lim) continue;
+                const double v = d64_pairwise(xs, C + (int64_t)c * d, d);
+                if (v < bv || (v == bv && c < bi)) { bv = v; bi = c; }
+            }
         }
 #pragma unroll
         for (int o = 16; o; o >>= 1) {
@@ -272,14 +300,20 @@ constexpr int kScatterRows = 8192;
 constexpr int kScatterMax = 4096;
 __global__ void __launch_bounds__(kSplitThreads) k_scatter_rows(const int32_t* __restrict__ lab, int64_t n, int k,
                                                                unsigned int* __restrict__ cursor,
-                                                               uint32_t* __restrict__ perm) {
+                                                               uint32_t* __restrict__ perm,
+                                                               int32_t* __restrict__ glab) {
     __shared__ unsigned int cnt[kScatterMax];
     __shared__ unsigned int at[kScatterMax];
     const bool local = k <= kScatterMax;
     for (int64_t c0 = (int64_t)blockIdx.x * kScatterRows; c0 < n; c0 += (int64_t)gridDim.x * kScatterRows) {
         const int64_t c1 = min(n, c0 + kScatterRows);
         if (!local) {
-            for (int64_t i = c0 + threadIdx.x; i < c1; i += blockDim.x) perm[atomicAdd(&cursor[lab[i]], 1u)] = (uint32_t)i;
+            for (int64_t i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
+                const int l = lab[i];
+                const unsigned pos = atomicAdd(&cursor[l], 1u);
+                perm[pos] = (uint32_t)i;
+                glab[pos] = l;
+            }
             continue;
         }
         for (int c = threadIdx.x; c < k; c += blockDim.x) cnt[c] = 0u;
@@ -293,7 +327,9 @@ __global__ void __launch_bounds__(kSplitThreads) k_scatter_rows(const int32_t* _
         __syncthreads();
         for (int64_t i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
             const int l = lab[i];
-            perm[at[l] + atomicAdd(&cnt[l], 1u)] = (uint32_t)i;
+            const unsigned pos = at[l] + atomicAdd(&cnt[l], 1u);
+            perm[pos] = (uint32_t)i;
+            glab[pos] = l;
         }
         __syncthreads();
     }
@@ -395,6 +431,188 @@ __global__ void __launch_bounds__(32 * kReduceWarps) k_reduce_rows(const float* 
         atomicOr(reinterpret_cast<unsigned long long*>(&counters[1]), (unsigned long long)kFlagNonFinite);
 }
 
+// Rows of d % 4 == 0 columns (X 16-byte aligned) as float4 groups.  A work item is a stretch of G * kSlabRows
+// grouped rows and a slab of SW = 4 LPR V columns: LPR lanes per row and G = 32 / LPR rows side by side (group g
+// takes the g-th kSlabRows rows of the stretch); lane i of a group owns the column groups i + LPR t (t < V) of
+// the slab.  The rows' values stream into shared memory by cp.async, kSlabStages chunks of U rows ahead (each
+// lane copies and later reads only its own float4s; the grouped labels go through a per-warp table).  Per
+// group: the current label's center in registers (float64), lane-private int64 sums in registers, flushed to
+// the totals when the label changes and at the end of the item.  Each value is quantised on its own, as in
+// k_reduce_rows, so the totals are the same integers.  MAGIC (n_total >= 2048: every quantised value is below
+// 2^50 in magnitude): v * 2^s is rounded to an integer by adding 1.5 * 2^52 inside the fma and the bits of the
+// sum are accumulated; the count times the constant's bits comes off at the flush (modulo 2^64, the true sum
+// being below 2^61).  The inertia is each (row, lane) float64 partial, quantised the same way.
+constexpr int kSlabRows = 256;
+constexpr int kSlabStages = 4;
+constexpr int kSlabThreads = 128;
+constexpr double kMagic = 6755399441055744.0;                  // 1.5 * 2^52
+constexpr unsigned long long kMagicBits = 0x4338000000000000ull;
+
+constexpr int slab_rows_in_flight(int lpr, int v) { return v == 1 ? (lpr < 8 ? lpr : 8) : 4; }
+constexpr size_t slab_smem(int lpr, int v) {
+    return (size_t)(kSlabThreads / 32) * kSlabStages * slab_rows_in_flight(lpr, v) * v * 32 * 16;
+}
+
+__device__ __forceinline__ void cp_async16(unsigned dst, const void* src, int bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ float f4_at(const float4& v, int e) { return e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w; }
+
+template <int LPR, int V, bool MAGIC>
+__global__ void __launch_bounds__(kSlabThreads) k_reduce_slab(const float* __restrict__ X, int64_t n, int d,
+                                                              const float* __restrict__ C,
+                                                              const int32_t* __restrict__ glab,
+                                                              const uint32_t* __restrict__ perm,
+                                                              const double* __restrict__ scale_x,
+                                                              const Prep* __restrict__ prep,
+                                                              long long* __restrict__ totals,
+                                                              long long* __restrict__ counters) {
+    constexpr int G = 32 / LPR;
+    constexpr int U = slab_rows_in_flight(LPR, V);             // rows per group and chunk
+    constexpr int P = kSlabStages;
+    constexpr int NCH = kSlabRows / U;
+    constexpr int SW = 4 * LPR * V;
+    static_assert(G * U <= 32 && kSlabRows % U == 0, "slab layout");
+    extern __shared__ __align__(16) float4 slab_buf[];
+    __shared__ int s_lbl[kSlabThreads / 32][P][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane / LPR, i = lane % LPR;
+    float4* xs = slab_buf + (size_t)warp * P * U * V * 32;
+    const unsigned xs_s = (unsigned)__cvta_generic_to_shared(xs);
+    const int W = d + 2;
+    const double scale_i = prep->scale_i;
+    const int nslab = (d + SW - 1) / SW;
+    const int64_t span = (int64_t)G * kSlabRows;
+    const int64_t items = (n + span - 1) / span * nslab;
+    const int64_t nwarps = ((int64_t)gridDim.x * kSlabThreads) >> 5;
+    bool bad = false;
+    for (int64_t item = ((int64_t)blockIdx.x * kSlabThreads + threadIdx.x) >> 5; item < items; item += nwarps) {
+        const int z = (int)(item % nslab);
+        const int64_t s0 = (item / nslab) * span + (int64_t)g * kSlabRows;
+        const int64_t s1 = min(n, s0 + kSlabRows);
+        int jc[V];
+        double sc[V][4], cd[V][4];
+        unsigned long long acc[V][4];
+#pragma unroll
+        for (int t = 0; t < V; t++) {
+            jc[t] = z * SW + 4 * (i + LPR * t);
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                sc[t][e] = jc[t] < d ? scale_x[jc[t] + e] : 0.0;
+                cd[t][e] = 0.0;
+                acc[t][e] = 0ull;
+            }
+        }
+        int cur = -1;
+        long long cnt = 0, iq = 0;
+        auto flush = [&]() {
+            if (cur < 0) return;
+            long long* tt = totals + (size_t)cur * W;
+#pragma unroll
+            for (int t = 0; t < V; t++) {
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const long long v = MAGIC ? (long long)(acc[t][e] - (unsigned long long)cnt * kMagicBits)
+                                              : (long long)acc[t][e];
+                    if (jc[t] < d && v) atomicAdd(reinterpret_cast<unsigned long long*>(tt + 2 + jc[t] + e),
+                                                  (unsigned long long)v);
+                    acc[t][e] = 0ull;
+                }
+            }
+            if (z == 0 && i == 0) atomicAdd(reinterpret_cast<unsigned long long*>(tt), (unsigned long long)cnt);
+            if (iq) atomicAdd(reinterpret_cast<unsigned long long*>(tt + 1), (unsigned long long)iq);
+            cnt = 0;
+            iq = 0;
+        };
+        // lane i < U of a group holds the index and label of row i of a chunk
+        auto load_idx = [&](int c, uint32_t& pr, int& pl) {
+            const int64_t pos = s0 + (int64_t)c * U + i;
+            const bool ok = i < U && c < NCH && pos < s1;
+            pr = ok ? perm[pos] : 0u;
+            pl = ok ? glab[pos] : -1;
+        };
+        // chunk c into stage c % P (an empty group past the last chunk keeps the group count uniform)
+        auto issue = [&](int c, uint32_t pr, int pl) {
+            const int st = c % P;
+            if (i < U) s_lbl[warp][st][g * U + i] = pl;
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int64_t row = __shfl_sync(0xffffffffu, pr, g * LPR + u);
+                const bool valid = c < NCH && s0 + (int64_t)c * U + u < s1;
+#pragma unroll
+                for (int t = 0; t < V; t++) {
+                    const bool live = valid && jc[t] < d;
+                    cp_async16(xs_s + (unsigned)((((st * U + u) * V + t) * 32 + lane) * 16),
+                               live ? (const void*)(X + row * d + jc[t]) : (const void*)X, live ? 16 : 0);
+                }
+            }
+            cp_async_commit();
+        };
+        {
+            uint32_t pr0[P + 1];
+            int pl0[P + 1];
+#pragma unroll
+            for (int c = 0; c <= P; c++) load_idx(c, pr0[c], pl0[c]);
+            __syncwarp();                      // the previous item's last reads of the label table are done
+#pragma unroll
+            for (int c = 0; c < P; c++) issue(c, pr0[c], pl0[c]);
+            uint32_t pr = pr0[P];
+            int pl = pl0[P];
+            for (int c = 0; c < NCH; c++) {
+                cp_async_wait<P - 1>();        // this lane's copies of chunk c have landed
+                __syncwarp();                  // and every lane's labels of it
+                const int st = c % P;
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    if (!(s0 + (int64_t)c * U + u < s1)) continue;
+                    const int l = s_lbl[warp][st][g * U + u];
+                    if (l != cur) {
+                        flush();
+                        cur = l;
+#pragma unroll
+                        for (int t = 0; t < V; t++)
+#pragma unroll
+                            for (int e = 0; e < 4; e++)
+                                cd[t][e] = jc[t] < d ? (double)C[(int64_t)l * d + jc[t] + e] : 0.0;
+                    }
+                    double b = 0.0;
+#pragma unroll
+                    for (int t = 0; t < V; t++) {
+                        const float4 xv = xs[((st * U + u) * V + t) * 32 + lane];
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const double v = (double)f4_at(xv, e);
+                            if constexpr (MAGIC)
+                                acc[t][e] += (unsigned long long)__double_as_longlong(__fma_rn(v, sc[t][e], kMagic));
+                            else
+                                acc[t][e] += (unsigned long long)__double2ll_rn(__dmul_rn(v, sc[t][e]));
+                            const double q = __dsub_rn(v, cd[t][e]);
+                            b = __fma_rn(q, q, b);
+                        }
+                    }
+                    if (!(b <= 1.0e300)) bad = true;
+                    else if constexpr (MAGIC)
+                        iq += (long long)((unsigned long long)__double_as_longlong(__fma_rn(b, scale_i, kMagic)) -
+                                          kMagicBits);
+                    else
+                        iq += __double2ll_rn(__dmul_rn(b, scale_i));
+                    cnt++;
+                }
+                __syncwarp();                  // stage c % P is read: it takes chunk c + P
+                issue(c + P, pr, pl);
+                load_idx(c + P + 1, pr, pl);
+            }
+            cp_async_wait<0>();                // (the trailing empty chunks) before the next item's copies
+        }
+        flush();
+    }
+    cp_async_wait<0>();
+    if (__any_sync(0xffffffffu, bad) && lane == 0)
+        atomicOr(reinterpret_cast<unsigned long long*>(&counters[1]), (unsigned long long)kFlagNonFinite);
+}
+
 int64_t a256(int64_t v) { return (v + 255) / 256 * 256; }
 
 }  // namespace
@@ -443,6 +661,26 @@ CenterSplit carve_centers(void* base, int d, int k) {
     return s;
 }
 
+// kmc_d64: one warp per (row, center) pair
+__global__ void __launch_bounds__(kSplitThreads) k_d64_pairs(const float* __restrict__ X,
+                                                            const float* __restrict__ C, int d, int64_t m,
+                                                            double* __restrict__ out) {
+    __shared__ __align__(8) unsigned char scratch[kSplitWarps][kD64WarpScratch];
+    const int warp = threadIdx.x >> 5;
+    const int64_t stride = (int64_t)gridDim.x * kSplitWarps;
+    for (int64_t i = (int64_t)blockIdx.x * kSplitWarps + warp; i < m; i += stride) {
+        const double v = d64_warp(X + i * d, C + i * d, d, scratch[warp]);
+        if ((threadIdx.x & 31) == 0) out[i] = v;
+    }
+}
+
+cudaError_t launch_d64(const float* X, const float* C, int d, int64_t m, double* out, cudaStream_t st) {
+    int64_t blocks = (m + kSplitWarps - 1) / kSplitWarps;
+    if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
+    k_d64_pairs<<<(int)blocks, kSplitThreads, 0, st>>>(X, C, d, m, out);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_split_rows(const float* X, int64_t n, int d, const RowSplit& s, cudaStream_t st) {
     if (n == 0) return cudaSuccess;
     int64_t blocks = (n + kSplitThreads / 32 - 1) / (kSplitThreads / 32);
@@ -471,7 +709,7 @@ cudaError_t launch_accum_split(PassArgs a, const RowSplit& rs, const CenterSplit
     const int64_t cap = (int64_t)num_sms() * 8;
     if (blocks > cap) blocks = cap;
     const size_t rsm = sizeof(float) * ((size_t)a.d + a.k);
-    if (rsm > 48 * 1024) {
+    if (rsm > 32 * 1024) {                   // (12 KB of static shared memory besides)
         e = cudaFuncSetAttribute(k_rescore_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
         if (e != cudaSuccess) return e;
     }
@@ -483,7 +721,38 @@ cudaError_t launch_accum_split(PassArgs a, const RowSplit& rs, const CenterSplit
     k_scan_labels<<<1, 1024, 0, st>>>(cs.hist, a.k, cs.cursor);
     int64_t sb = (a.n + kScatterRows - 1) / kScatterRows;
     if (sb > cap) sb = cap;
-    k_scatter_rows<<<(int)sb, kSplitThreads, 0, st>>>(rs.lab, a.n, a.k, cs.cursor, rs.perm);
+    // grouped labels (the scatter's second output) in the overflow list's space, free from here on
+    int32_t* glab = reinterpret_cast<int32_t*>(rs.ovf);
+    k_scatter_rows<<<(int)sb, kSplitThreads, 0, st>>>(rs.lab, a.n, a.k, cs.cursor, rs.perm, glab);
+    if (a.d % 4 == 0 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0) {
+        const int d4 = a.d / 4;
+        const int lpr = d4 <= 4 ? 4 : d4 <= 8 ? 8 : d4 <= 16 ? 16 : 32;
+        const int v = d4 > 32 ? 2 : 1;
+        const int64_t span = (int64_t)(32 / lpr) * kSlabRows;
+        const int64_t items = (a.n + span - 1) / span * ((a.d + 4 * lpr * v - 1) / (4 * lpr * v));
+        const int64_t want = (items + kSlabThreads / 32 - 1) / (kSlabThreads / 32);
+        const bool magic = a.n_total >= 2048;
+        const size_t ssm = slab_smem(lpr, v);
+        cudaError_t e3 = cudaSuccess;
+        auto slab = [&](auto kern) {
+            e3 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm);
+            int per_sm = 0;
+            if (e3 == cudaSuccess)
+                e3 = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kSlabThreads, ssm);
+            if (e3 != cudaSuccess) return;
+            const int64_t cap = (int64_t)num_sms() * (per_sm > 0 ? per_sm : 1);   // one resident wave
+            const int64_t blocks = want < cap ? want : cap;
+            kern<<<(int)blocks, kSlabThreads, ssm, st>>>(a.X, a.n, a.d, a.C, glab, rs.perm, a.scale_x, a.prep,
+                                                         a.totals, a.counters);
+        };
+        if (lpr == 4) magic ? slab(k_reduce_slab<4, 1, true>) : slab(k_reduce_slab<4, 1, false>);
+        else if (lpr == 8) magic ? slab(k_reduce_slab<8, 1, true>) : slab(k_reduce_slab<8, 1, false>);
+        else if (lpr == 16) magic ? slab(k_reduce_slab<16, 1, true>) : slab(k_reduce_slab<16, 1, false>);
+        else if (v == 1) magic ? slab(k_reduce_slab<32, 1, true>) : slab(k_reduce_slab<32, 1, false>);
+        else magic ? slab(k_reduce_slab<32, 2, true>) : slab(k_reduce_slab<32, 2, false>);
+        if (e3 != cudaSuccess) return e3;
+        return cudaGetLastError();
+    }
     const size_t smem = (size_t)kReduceWarps * a.d * 8;
     const int64_t runs = (a.n + kRun - 1) / kRun;
     int64_t rb = (runs + kReduceWarps - 1) / kReduceWarps;

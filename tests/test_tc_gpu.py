@@ -141,3 +141,24 @@ def test_tc_many_equal_centers(cuda_device):
     ref, _, _ = O.assign(X, C)
     assert np.array_equal(out[3], ref)
     assert (ref == 3).sum() > 0 and not np.isin(ref, [9, 10, 17, 30, 31]).any()
+
+
+@pytest.mark.parametrize("d", [3, 7, 8, 31, 32, 100, 128, 129, 136, 200, 255, 513, 768, 1000, 4096])
+def test_d64_warp_bit_identical(d, cuda_device):
+    """kmc_d64 (a warp per pair: the leaves' partial chains across lanes, the reference's combination order)
+    returns the float64 bits of the oracle's NumPy-pairwise D64, at leaf-only, split and ragged-tail sizes."""
+    import torch
+    from mlx_kmeans_b200 import _lib
+    rng = np.random.default_rng(d)
+    m = 64
+    X = rng.standard_normal((m, d)).astype(np.float32) * rng.uniform(0.01, 100.0, size=(m, 1)).astype(np.float32)
+    C = X + rng.standard_normal((m, d)).astype(np.float32) * np.float32(1e-3)
+    C[::7] = X[::7]                                     # zero distances
+    Xt, Ct = torch.from_numpy(X).to(cuda_device), torch.from_numpy(C).to(cuda_device)
+    out = torch.empty(m, dtype=torch.float64, device=cuda_device)
+    L = _lib.load()
+    _lib.check(L.kmc_d64(Xt.data_ptr(), Ct.data_ptr(), d, m, out.data_ptr(),
+                         torch.cuda.current_stream().cuda_stream))
+    got = out.cpu().numpy()
+    want = np.array([O.d64(X[i], C[i]) for i in range(m)])
+    assert np.array_equal(got.view(np.int64), want.view(np.int64))
