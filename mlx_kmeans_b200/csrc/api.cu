@@ -269,9 +269,7 @@ int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, cons
     ts.xn = rs.xn;
     ts.cmax = reinterpret_cast<const float*>(cs.cmax_bits);
     ts.lab = rs.lab;
-    ts.flagged = rs.perm;                  // the list of flagged rows, until the rows are grouped by label
     ts.cands = rs.cands;
-    ts.nflag = cs.nflag;
     ts.error = cs.error;
     e = launch_assign_tc(ts, st);
     if (e != cudaSuccess) return cuda_fail(e, who);

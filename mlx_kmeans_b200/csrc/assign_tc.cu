@@ -18,9 +18,11 @@
 //            and ch, cl (BN x 64 bf16), 128-byte swizzled, two stages in flight.
 //   warp 1   MMA issuer: 3 x 4 tcgen05.mma (M=128, N=BN, K=16) per stage into one of two TMEM accumulators;
 //            tcgen05.commit frees the stage and, after the last chunk, hands the accumulator to the epilogue.
-//   warps 2-5  epilogue: each thread owns one row (TMEM lane), reads its BN scores 32 columns at a time
-//            (tcgen05.ld), keeps the best and second-best score with the lowest index, and at the end of the
-//            row tile writes label | flag << 31.
+//   warps 2-9  epilogue: two warps per TMEM lane quarter, one per half of the accumulator's columns; a thread
+//            owns one row (TMEM lane), reads its scores 32 columns at a time (tcgen05.ld) and keeps the two
+//            best scores with their centers (lowest index first on ties) and the third best score, in two
+//            interleaved branch-free trackers; at the end of the row tile the pair merges its halves through
+//            shared memory and writes label | flag << 31 and, for a flagged row, its candidates.
 // Every wait on an mbarrier is bounded; on a timeout the CTA records an error, stops its loops and frees TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -35,17 +37,24 @@ namespace {
 constexpr int BM = 128;                  // rows per tile (UMMA M)
 constexpr int BK = 64;                   // bf16 columns per chunk: one 128-byte swizzle row
 constexpr int kTcStages = 2;
-constexpr int kTcThreads = 192;          // producer warp, MMA warp, four epilogue warps
+constexpr int kTcThreads = 320;          // producer warp, MMA warp, eight epilogue warps
+constexpr int kEpiWarps = 8;
 constexpr uint32_t kSpinLimit = 1u << 22;
 
-template <int BN>
+// Shared memory.  AR (rows resident, dp <= 128): the row tile's xh / xl chunks stay for all center tiles and the
+// stages carry only ch / cl; otherwise every stage carries a chunk of each.
+constexpr int kResidentChunks = 2;       // dp <= 128
+template <int BN, bool AR>
 struct TcSmem {
     static constexpr int A = BM * BK * 2;             // one 128 x 64 bf16 operand chunk (16 KB)
     static constexpr int B = BN * BK * 2;             // one BN x 64 bf16 chunk
-    static constexpr int STAGE = 2 * A + 2 * B;       // hi and lo of each
+    static constexpr int AREG = AR ? kResidentChunks * 2 * A : 0;
+    static constexpr int STAGE = AR ? 2 * B : 2 * A + 2 * B;   // hi and lo of each operand it carries
     static constexpr int BAR = 256;                   // barriers, TMEM address, abort flag
-    static constexpr int total = kTcStages * STAGE + BAR + 1024;   // + slack to align the stages to 1024 B
+    static constexpr int EPI = 2 * 4 * 32 * 5 * 4;    // the column halves' trackers: [tile parity][quarter][lane]
+    static constexpr int total = AREG + kTcStages * STAGE + BAR + EPI + 1024;   // + slack to align to 1 KB
     static_assert(A % 1024 == 0 && B % 1024 == 0, "swizzle atoms are 1024-byte aligned");
+    static_assert(total <= 227 * 1024, "shared memory per CTA");
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -136,6 +145,39 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
 }
 
+// The two smallest scores with their centers and the third smallest score.  push() takes centers in increasing
+// index order (a strict less keeps the lower index first on ties); merge() takes another tracker's entries,
+// ordered by (score, index).  A NaN score is never taken.
+struct Top3 {
+    float m0, m1, m2;
+    int l0, l1;
+    __device__ __forceinline__ void init() {
+        m0 = m1 = m2 = INFINITY;
+        l0 = l1 = 0;
+    }
+    __device__ __forceinline__ void push(float s, int c) {
+        const bool a0 = s < m0, a1 = s < m1, a2 = s < m2;
+        m2 = a1 ? m1 : (a2 ? s : m2);
+        m1 = a0 ? m0 : (a1 ? s : m1);
+        l1 = a0 ? l0 : (a1 ? c : l1);
+        m0 = a0 ? s : m0;
+        l0 = a0 ? c : l0;
+    }
+    __device__ __forceinline__ void push_ordered(float s, int c) {
+        const bool a0 = s < m0 || (s == m0 && c < l0), a1 = s < m1 || (s == m1 && c < l1), a2 = s < m2;
+        m2 = a1 ? m1 : (a2 ? s : m2);
+        m1 = a0 ? m0 : (a1 ? s : m1);
+        l1 = a0 ? l0 : (a1 ? c : l1);
+        m0 = a0 ? s : m0;
+        l0 = a0 ? c : l0;
+    }
+    __device__ __forceinline__ void merge(float n0, int k0, float n1, int k1, float n2) {
+        push_ordered(n0, k0);
+        push_ordered(n1, k1);
+        if (n2 < m2) m2 = n2;      // a third best of the other set is at best third here
+    }
+};
+
 struct TcArgs {
     int64_t n;
     int dp;                  // padded dims (multiple of 64)
@@ -144,32 +186,34 @@ struct TcArgs {
     const float* hs;         // kp: |c|^2 / 2 (padding centers: 2^126)
     const float* xn;         // n: |x| rounded up
     const float* cmax;       // max |c| rounded up (one value)
-    int32_t* lab;            // n: label | flag << 31
-    uint32_t* flagged;       // rows to decide in float64
-    int4* cands;             // their candidate centers (-1: none, w = -2: more than four)
-    unsigned int* nflag;     // their number (zeroed by the caller)
+    int32_t* lab;            // n: label | flag << 31 (flag: decide the row in float64)
+    int4* cands;             // n: a flagged row's candidate centers (-1: none, w = -2: more than two)
     int* error;              // set on a barrier timeout
 };
 
-template <int BN>
+template <int BN, bool AR>
 __global__ void __launch_bounds__(kTcThreads, 1)
     k_assign_tc(const __grid_constant__ CUtensorMap mxh, const __grid_constant__ CUtensorMap mxl,
                 const __grid_constant__ CUtensorMap mch, const __grid_constant__ CUtensorMap mcl, TcArgs a) {
-    using S = TcSmem<BN>;
+    using S = TcSmem<BN, AR>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    // stages at the first 1024-byte boundary, then the barrier block
+    // (resident rows,) stages at the first 1024-byte boundary, then the barrier block
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
+    const uint32_t sbase = base + S::AREG;
     unsigned char* gbase = smem_raw + (base - raw);
-    const uint32_t bars = base + kTcStages * S::STAGE;
-    unsigned char* gbars = gbase + kTcStages * S::STAGE;
-    // barrier block: full[2] empty[2] accf[2] acce[2] (8 B each), TMEM base (4 B), abort flag (4 B)
+    const uint32_t bars = sbase + kTcStages * S::STAGE;
+    unsigned char* gbars = gbase + S::AREG + kTcStages * S::STAGE;
+    // barrier block: full[2] empty[2] accf[2] acce[2] (8 B each), TMEM base (4 B), abort flag (4 B), and for
+    // resident rows afull, aempty (8 B each)
     auto full = [&](int s) { return bars + 8u * s; };
     auto empty = [&](int s) { return bars + 16u + 8u * s; };
     auto accf = [&](int b) { return bars + 32u + 8u * b; };
     auto acce = [&](int b) { return bars + 48u + 8u * b; };
+    const uint32_t afull = bars + 72u, aempty = bars + 80u;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbars + 64);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbars + 68);
+    float* epi = reinterpret_cast<float*>(gbars + S::BAR);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t tiles = (a.n + BM - 1) / BM;
@@ -182,7 +226,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(accf(b), 1);
-            mbar_init(acce(b), 4 * 32);
+            mbar_init(acce(b), kEpiWarps * 32);
+        }
+        if (AR) {
+            mbar_init(afull, 1);
+            mbar_init(aempty, 1);
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -201,30 +249,52 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // ---- TMA producer
         if (lane == 0) {
             int stage = 0;
-            uint32_t phase = 0;
+            uint32_t phase = 0, tph = 0;
             bool ok = true;
-            for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x)
+            for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                if constexpr (AR) {
+                    // the row tile, once: after the previous tile's last MMA has read the resident chunks
+                    ok = mbar_wait(aempty, tph ^ 1u, abort_flag);
+                    if (!ok) break;
+                    mbar_expect_tx(afull, (uint32_t)(kchunks * 2 * S::A));
+                    for (int kc = 0; kc < kchunks; kc++) {
+                        tma_load_2d(base + kc * 2 * S::A, &mxh, kc * BK, (int)(t * BM), afull);
+                        tma_load_2d(base + kc * 2 * S::A + S::A, &mxl, kc * BK, (int)(t * BM), afull);
+                    }
+                    tph ^= 1u;
+                }
                 for (int nt = 0; nt < ntiles && ok; nt++)
                     for (int kc = 0; kc < kchunks && ok; kc++) {
                         ok = mbar_wait(empty(stage), phase ^ 1u, abort_flag);
                         if (!ok) break;
-                        const uint32_t st = base + stage * S::STAGE;
+                        const uint32_t st = sbase + stage * S::STAGE;
                         mbar_expect_tx(full(stage), S::STAGE);
-                        tma_load_2d(st, &mxh, kc * BK, (int)(t * BM), full(stage));
-                        tma_load_2d(st + S::A, &mxl, kc * BK, (int)(t * BM), full(stage));
-                        tma_load_2d(st + 2 * S::A, &mch, kc * BK, nt * BN, full(stage));
-                        tma_load_2d(st + 2 * S::A + S::B, &mcl, kc * BK, nt * BN, full(stage));
+                        if constexpr (AR) {
+                            tma_load_2d(st, &mch, kc * BK, nt * BN, full(stage));
+                            tma_load_2d(st + S::B, &mcl, kc * BK, nt * BN, full(stage));
+                        } else {
+                            tma_load_2d(st, &mxh, kc * BK, (int)(t * BM), full(stage));
+                            tma_load_2d(st + S::A, &mxl, kc * BK, (int)(t * BM), full(stage));
+                            tma_load_2d(st + 2 * S::A, &mch, kc * BK, nt * BN, full(stage));
+                            tma_load_2d(st + 2 * S::A + S::B, &mcl, kc * BK, nt * BN, full(stage));
+                        }
                         if (++stage == kTcStages) { stage = 0; phase ^= 1u; }
                     }
+            }
         }
     } else if (warp == 1) {
         // ---- MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_bf16<BN>();
             int stage = 0;
-            uint32_t phase = 0, abuf = 0, aphase = 0;
+            uint32_t phase = 0, abuf = 0, aphase = 0, tph = 0;
             bool ok = true;
-            for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x)
+            for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                if constexpr (AR) {
+                    ok = mbar_wait(afull, tph, abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                }
                 for (int nt = 0; nt < ntiles && ok; nt++) {
                     ok = mbar_wait(acce(abuf), aphase ^ 1u, abort_flag);
                     if (!ok) break;
@@ -234,9 +304,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         ok = mbar_wait(full(stage), phase, abort_flag);
                         if (!ok) break;
                         tc_fence_after();
-                        const uint32_t st = base + stage * S::STAGE;
-                        const uint64_t ah = sw128_desc(st), al = sw128_desc(st + S::A);
-                        const uint64_t bh = sw128_desc(st + 2 * S::A), bl = sw128_desc(st + 2 * S::A + S::B);
+                        const uint32_t st = sbase + stage * S::STAGE;
+                        const uint32_t sa = AR ? base + kc * 2 * S::A : st;
+                        const uint32_t sb = AR ? st : st + 2 * S::A;
+                        const uint64_t ah = sw128_desc(sa), al = sw128_desc(sa + S::A);
+                        const uint64_t bh = sw128_desc(sb), bl = sw128_desc(sb + S::B);
 #pragma unroll
                         for (int kk = 0; kk < BK / 16; kk++) {
                             const uint64_t off = (uint64_t)((kk * 32) >> 4);   // 16 bf16 = 32 B along K
@@ -252,10 +324,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     abuf ^= 1u;
                     if (abuf == 0) aphase ^= 1u;
                 }
+                if constexpr (AR) {
+                    if (!ok) break;
+                    mma_commit(aempty);                    // the resident rows are free once these MMAs are done
+                    tph ^= 1u;
+                }
+            }
         }
     } else {
-        // ---- epilogue: thread = one row of the tile (TMEM lane 32 * (warp % 4) + lane)
-        const int q = warp & 3;
+        // ---- epilogue: warp w reads TMEM lane quarter q = w % 4 (its rows 32 q + lane of the tile) and column
+        // half h of every accumulator; the h = 1 warp hands its tracker to the h = 0 warp of the same quarter
+        // through shared memory (named barrier 1 + q, 64 threads, once per tile on both warps, abort or not)
+        const int q = warp & 3, h = (warp - 2) >> 2;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
         const float cmax = *a.cmax;
         // Window on the gap between the two best scores: each score is off by at most E |x| |c| (the dropped
@@ -263,30 +343,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // the subtraction); two of them, with |c| <= cmax, and a 2^-10 margin for the float32 evaluation of the
         // window itself.  The float64 rounding of D64, which defines the label, adds 2^-40 (|x| + cmax)^2.
         const float E2 = (float)(2.0 * (3.1 / 65536.0 + 3.0 * a.dp / 16777216.0));
+        constexpr int HALF = BN / 2;
         uint32_t abuf = 0, aphase = 0;
         bool ok = true;
-        for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-            // the two smallest scores with their centers (equal scores keep the lower index first) and the third
-            // smallest score
-            float m0 = INFINITY, m1 = INFINITY, m2 = INFINITY;
-            int l0 = 0, l1 = 0;
+        int it = 0;                                       // tiles done: the hand-over slot alternates with it
+        for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, it++) {
+            const int64_t row = t * BM + 32 * q + lane;
+            const float xr = (h == 0 && row < a.n) ? __ldg(a.xn + row) : 0.0f;   // in flight meanwhile
+            Top3 ev, od;                                  // even and odd columns: two independent chains
+            ev.init();
+            od.init();
             for (int nt = 0; nt < ntiles && ok; nt++) {
                 ok = mbar_wait(accf(abuf), aphase, abort_flag);
                 if (!ok) break;
                 tc_fence_after();
 #pragma unroll 1
-                for (int cc = 0; cc < BN; cc += 32) {
+                for (int cc = h * HALF; cc < (h + 1) * HALF; cc += 32) {
                     float v[32];
                     tmem_ld32(lane_base + abuf * BN + cc, v);
                     const int c0 = nt * BN + cc;
 #pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        const float s = __ldg(a.hs + c0 + j) - v[j];
-                        if (s < m1) {
-                            m2 = m1;
-                            if (s < m0) { m1 = m0; l1 = l0; m0 = s; l0 = c0 + j; }
-                            else { m1 = s; l1 = c0 + j; }
-                        } else if (s < m2) m2 = s;
+                    for (int j = 0; j < 32; j += 2) {
+                        ev.push(__ldg(a.hs + c0 + j) - v[j], c0 + j);
+                        od.push(__ldg(a.hs + c0 + j + 1) - v[j + 1], c0 + j + 1);
                     }
                 }
                 tc_fence_before();
@@ -294,32 +373,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 abuf ^= 1u;
                 if (abuf == 0) aphase ^= 1u;
             }
-            if (!ok) break;
-            const int64_t row = t * BM + 32 * q + lane;
-            bool flag = false;
-            int4 cand = make_int4(l0, -1, -1, -1);
+            ev.merge(od.m0, od.l0, od.m1, od.l1, od.m2);
+            float* slot = epi + ((((it & 1) * 4 + q) * 32 + lane) * 5);
+            if (h == 1) {
+                slot[0] = ev.m0;
+                slot[1] = ev.m1;
+                slot[2] = ev.m2;
+                slot[3] = __int_as_float(ev.l0);
+                slot[4] = __int_as_float(ev.l1);
+            }
+            asm volatile("bar.sync %0, %1;" ::"r"(1 + q), "r"(64) : "memory");
+            if (h == 1 || !ok) continue;
+            ev.merge(slot[0], __float_as_int(slot[3]), slot[1], __float_as_int(slot[4]), slot[2]);
+            const float m0 = ev.m0, m1 = ev.m1, m2 = ev.m2;
+            const int l0 = ev.l0, l1 = ev.l1;
             if (row < a.n) {
-                const float xr = __ldg(a.xn + row), r = xr + cmax;
+                const float r = xr + cmax;
                 const float win = (E2 * xr * cmax + cmax * (cmax + xr) * (1.0f / 8388608.0f)) * (1.0f + 1.0f / 1024.0f) +
                                   r * r * (1.0f / 1099511627776.0f);
-                flag = !(m1 - m0 > win) || l0 >= a.k;
+                const bool flag = !(m1 - m0 > win) || l0 >= a.k;
                 a.lab[row] = (int32_t)((uint32_t)l0 | (flag ? 0x80000000u : 0u));
                 // candidates: the centers whose score is within the window of the smallest; when the third is
                 // too (or a score is not finite), there may be more than two: -2 sends the row to the full decision
-                if (!(m1 - m0 > win)) cand.y = l1;
-                if (!(m2 - m0 > win) || !(m0 <= 3.0e38f) || l0 >= a.k) cand.w = -2;
-            }
-            // flagged rows join the list the float64 decision works through (one atomic per warp)
-            const unsigned fm = __ballot_sync(0xffffffffu, flag);
-            if (fm) {
-                const int leader = __ffs(fm) - 1;
-                unsigned at = 0;
-                if (lane == leader) at = atomicAdd(a.nflag, (unsigned)__popc(fm));
-                at = __shfl_sync(0xffffffffu, at, leader);
                 if (flag) {
-                    const unsigned f = at + __popc(fm & ((1u << lane) - 1u));
-                    a.flagged[f] = (uint32_t)row;
-                    a.cands[f] = cand;
+                    int4 cand = make_int4(l0, -1, -1, -1);
+                    if (!(m1 - m0 > win)) cand.y = l1;
+                    if (!(m2 - m0 > win) || !(m0 <= 3.0e38f) || l0 >= a.k) cand.w = -2;
+                    a.cands[row] = cand;
                 }
             }
         }
@@ -364,7 +444,7 @@ bool make_map(CUtensorMap* m, const void* base, int64_t rows, int dp, int box_ro
     return r == CUDA_SUCCESS;
 }
 
-template <int BN>
+template <int BN, bool AR>
 cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
     CUtensorMap mxh, mxl, mch, mcl;
     if (!make_map(&mxh, s.xh, s.n, s.dp, BM) || !make_map(&mxl, s.xl, s.n, s.dp, BM) ||
@@ -373,9 +453,9 @@ cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
     static unsigned long long configured = 0;
     int dev = 0;
     cudaGetDevice(&dev);
-    const size_t smem = TcSmem<BN>::total;
+    const size_t smem = TcSmem<BN, AR>::total;
     if (!(configured >> (dev & 63) & 1ull)) {
-        cudaError_t e = cudaFuncSetAttribute(k_assign_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(k_assign_tc<BN, AR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         configured |= 1ull << (dev & 63);
     }
@@ -388,15 +468,13 @@ cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
     a.xn = s.xn;
     a.cmax = s.cmax;
     a.lab = s.lab;
-    a.flagged = s.flagged;
     a.cands = s.cands;
-    a.nflag = s.nflag;
     a.error = s.error;
     const int64_t tiles = (s.n + BM - 1) / BM;
     int64_t grid = num_sms();
     if (grid > tiles) grid = tiles;
     if (grid < 1) grid = 1;
-    k_assign_tc<BN><<<(int)grid, kTcThreads, smem, st>>>(mxh, mxl, mch, mcl, a);
+    k_assign_tc<BN, AR><<<(int)grid, kTcThreads, smem, st>>>(mxh, mxl, mch, mcl, a);
     return cudaGetLastError();
 }
 
@@ -405,10 +483,12 @@ cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
 int tc_block_n(int k) { return k <= 64 ? 64 : k <= 128 ? 128 : 256; }
 
 cudaError_t launch_assign_tc(const TcSplit& s, cudaStream_t st) {
+    // the row tile stays resident when it fits (dp <= 128) and is used for more than one center tile
+    const bool ar = s.dp <= kResidentChunks * BK && s.kp / tc_block_n(s.k) > 1;
     switch (tc_block_n(s.k)) {
-        case 64: return run_tc<64>(s, st);
-        case 128: return run_tc<128>(s, st);
-        default: return run_tc<256>(s, st);
+        case 64: return ar ? run_tc<64, true>(s, st) : run_tc<64, false>(s, st);
+        case 128: return ar ? run_tc<128, true>(s, st) : run_tc<128, false>(s, st);
+        default: return ar ? run_tc<256, true>(s, st) : run_tc<256, false>(s, st);
     }
 }
 

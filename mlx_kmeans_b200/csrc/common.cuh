@@ -192,8 +192,23 @@ __device__ inline double d64_warp(const float* x, const float* c, int d, void* s
         const int2 lf = leaf[L];
         double p = 0.0;
         if (live) {
-            p = d64_term(x, c, lf.x + r);
-            for (int i = 8 + r; i < lf.y - (lf.y % 8); i += 8) p = __dadd_rn(p, d64_term(x, c, lf.x + i));
+            // a chain has at most 16 terms (leaves of at most 128): its values are loaded before any is used
+            const int nfull = lf.y - (lf.y % 8);
+            float xv[16], cv[16];
+#pragma unroll
+            for (int m = 0; m < 16; m++) {
+                const int i = r + 8 * m;
+                xv[m] = i < nfull ? x[lf.x + i] : 0.0f;
+                cv[m] = i < nfull ? c[lf.x + i] : 0.0f;
+            }
+            double q = __dsub_rn((double)xv[0], (double)cv[0]);
+            p = __dmul_rn(q, q);
+#pragma unroll
+            for (int m = 1; m < 16; m++) {
+                if (r + 8 * m >= nfull) break;
+                q = __dsub_rn((double)xv[m], (double)cv[m]);
+                p = __dadd_rn(p, __dmul_rn(q, q));
+            }
         }
         p = __dadd_rn(p, __shfl_xor_sync(0xffffffffu, p, 1));
         p = __dadd_rn(p, __shfl_xor_sync(0xffffffffu, p, 2));

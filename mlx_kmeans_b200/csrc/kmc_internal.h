@@ -105,9 +105,7 @@ struct TcSplit {
     const float* xn;
     const float* cmax;
     int32_t* lab;
-    uint32_t* flagged;
     int4* cands;
-    unsigned int* nflag;
     int* error;
 };
 int split_dp(int d);

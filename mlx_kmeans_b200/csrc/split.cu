@@ -4,15 +4,17 @@
 //                    multiple of 64 with zeros) and |x| rounded up, for assign_tc.cu
 //   k_split_centers  once per pass: the same split of the centers (rows padded to the MMA tile), |c|^2/2 and
 //                    max |c| (rounded up)
-//   k_fix_labels     per row: the label from assign_tc.cu; rows it flagged are decided here in float64
-//                    (NumPy-pairwise D64 over all centers, lowest index on ties, one warp per flagged row); the
-//                    histogram of the labels; the optional labels / best outputs (best: the reference's
-//                    float32 distance, each operation rounded on its own, in column order)
-//   k_scan_labels, k_scatter_rows   the rows grouped by label (a counting sort)
-//   k_reduce_rows    one warp per run of 256 grouped rows: every value quantised on its own into int64
-//                    lane-private shared-memory sums, flushed to the global totals when the label changes, so the
-//                    totals are exact integers whatever the order (and equal to the CUDA-core pass's); inertia
-//                    from the float64 distance of each row (float64 per lane, fixed reduction tree)
+//   k_decide_cands   the rows assign_tc.cu flagged (label bit 31): float64 (NumPy-pairwise D64, one warp per
+//                    row) of their two candidate centers, lowest index on ties; rows with more candidates:
+//   k_rescore_tc     one CTA per row: a float32 screen of every center, then D64 of each center in its window
+//   k_fix_labels     per row: the histogram of the labels; the optional labels / best outputs (best: the
+//                    reference's float32 distance, each operation rounded on its own, in column order)
+//   k_scan_labels, k_scatter_rows   the rows grouped by label (a counting sort; the labels in grouped order too)
+//   k_reduce_slab    d % 4 == 0: the grouped rows streamed by cp.async in column slabs, every value quantised on
+//                    its own into lane-private int64 sums, flushed to the global totals when the label changes, so
+//                    the totals are exact integers whatever the order (and equal to the CUDA-core pass's); inertia
+//                    from each (row, lane) float64 partial distance, quantised the same way
+//   k_reduce_rows    the same for any d, one warp per run of 256 grouped rows
 //
 // Reference: the high-d exact path of core.py:289-377 / 675-844, its sorted accumulation for large k
 // (core.py:1292-1441, mx.argsort grouping at 976-987), and the label rule of core.py:263-274.
@@ -90,35 +92,62 @@ __global__ void __launch_bounds__(kSplitThreads) k_split_centers(const float* __
     }
 }
 
-// The rows the tensor-core kernel flagged, one warp each: the float64 distance (NumPy-pairwise D64, summed by
-// the warp, d64_warp) of each of its (two) candidate centers; the smallest, lowest index on ties, is the label.
-// Rows with more candidates go on to k_rescore_tc.  (If the tensor-core kernel gave up, k_rescore_tc decides
-// every row.)
+// The rows the tensor-core kernel flagged (label bit 31), listed by a coalesced scan of the labels (one atomic
+// per warp with flagged rows); the rows with more than two candidates go straight to the overflow list.
 constexpr int kSplitWarps = kSplitThreads / 32;
+__global__ void __launch_bounds__(kSplitThreads) k_flag_list(const int32_t* __restrict__ lab, int64_t n,
+                                                            const int4* __restrict__ cands,
+                                                            const int* __restrict__ tc_error,
+                                                            uint32_t* __restrict__ list, unsigned int* __restrict__ nlist,
+                                                            uint32_t* __restrict__ ovf, unsigned int* __restrict__ novf,
+                                                            long long* __restrict__ counters) {
+    if (*tc_error) return;
+    const int lane = threadIdx.x & 31;
+    const int64_t stride = (int64_t)gridDim.x * kSplitThreads;
+    unsigned long long flagged = 0;
+    for (int64_t base = (int64_t)blockIdx.x * kSplitThreads + (threadIdx.x & ~31); base < n; base += stride) {
+        const int64_t row = base + lane;
+        const bool f = row < n && lab[row] < 0;
+        const bool over = f && cands[row].w == -2;
+        const unsigned fm = __ballot_sync(0xffffffffu, f && !over), om = __ballot_sync(0xffffffffu, over);
+        flagged += __popc(fm) + __popc(om);
+        const unsigned below = (1u << lane) - 1u;
+        if (fm) {
+            unsigned at = 0;
+            if (lane == 0) at = atomicAdd(nlist, (unsigned)__popc(fm));
+            at = __shfl_sync(0xffffffffu, at, 0);
+            if (f && !over) list[at + __popc(fm & below)] = (uint32_t)row;
+        }
+        if (om) {
+            unsigned at = 0;
+            if (lane == 0) at = atomicAdd(novf, (unsigned)__popc(om));
+            at = __shfl_sync(0xffffffffu, at, 0);
+            if (over) ovf[at + __popc(om & below)] = (uint32_t)row;
+        }
+    }
+    if (lane == 0 && flagged) atomicAdd(reinterpret_cast<unsigned long long*>(&counters[0]), flagged);
+}
+
+// The listed rows: the float64 distance (NumPy-pairwise D64) of each of a row's (two) candidate centers; the
+// smallest, lowest index on ties, is the label.  d <= 128 (one leaf of the pairwise tree): a thread per row;
+// longer rows: a warp per row (d64_warp).
 __global__ void __launch_bounds__(kSplitThreads) k_decide_cands(const float* __restrict__ X, int d,
                                                                const float* __restrict__ C,
                                                                const uint32_t* __restrict__ list,
+                                                               const unsigned int* __restrict__ nlist,
                                                                const int4* __restrict__ cands,
-                                                               const unsigned int* __restrict__ nflag,
                                                                const int* __restrict__ tc_error,
-                                                               uint32_t* __restrict__ ovf,
-                                                               unsigned int* __restrict__ novf,
-                                                               int32_t* __restrict__ lab,
-                                                               long long* __restrict__ counters) {
+                                                               int32_t* __restrict__ lab) {
     __shared__ __align__(8) unsigned char scratch[kSplitWarps][kD64WarpScratch];
     if (*tc_error) return;
-    const int64_t cnt = *nflag;
-    if (blockIdx.x == 0 && threadIdx.x == 0 && cnt)
-        atomicAdd(reinterpret_cast<unsigned long long*>(&counters[0]), (unsigned long long)cnt);
+    const int64_t cnt = *nlist;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t stride = (int64_t)gridDim.x * kSplitWarps;
-    for (int64_t f = (int64_t)blockIdx.x * kSplitWarps + warp; f < cnt; f += stride) {
+    const bool wide = d > 128;
+    const int64_t per = wide ? (int64_t)gridDim.x * kSplitWarps : (int64_t)gridDim.x * kSplitThreads;
+    const int64_t first = wide ? (int64_t)blockIdx.x * kSplitWarps + warp : (int64_t)blockIdx.x * kSplitThreads + threadIdx.x;
+    for (int64_t f = first; f < cnt; f += per) {
         const int64_t row = list[f];
-        const int4 c4 = cands[f];
-        if (c4.w == -2) {
-            if (lane == 0) ovf[atomicAdd(novf, 1u)] = (uint32_t)row;
-            continue;
-        }
+        const int4 c4 = cands[row];
         const float* x = X + row * d;
         const int cs[4] = {c4.x, c4.y, c4.z, c4.w};
         double bv = INFINITY;
@@ -126,10 +155,11 @@ __global__ void __launch_bounds__(kSplitThreads) k_decide_cands(const float* __r
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             if (cs[i] < 0) continue;
-            const double v = d64_warp(x, C + (int64_t)cs[i] * d, d, scratch[warp]);
+            const double v = wide ? d64_warp(x, C + (int64_t)cs[i] * d, d, scratch[warp])
+                                  : d64_pairwise(x, C + (int64_t)cs[i] * d, d);
             if (v < bv || (v == bv && cs[i] < bi)) { bv = v; bi = cs[i]; }
         }
-        if (lane == 0) lab[row] = bi;
+        if (!wide || lane == 0) lab[row] = bi;
     }
 }
 
@@ -250,10 +280,18 @@ __global__ void __launch_bounds__(kSplitThreads) k_fix_labels(const float* __res
         for (int c = threadIdx.x; c < k; c += blockDim.x) sh[c] = 0u;
     __syncthreads();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-        const int l = lab[i];
-        if (local) atomicAdd(&sh[l], 1u);
-        else atomicAdd(&hist[l], 1u);
+    // (the loop runs whole warps: the lanes with the same label add once, so a run of equal labels does not
+    // serialise on one counter)
+    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); i0 < n; i0 += stride) {
+        const int64_t i = i0 + (threadIdx.x & 31);
+        const bool in = i < n;
+        const int l = in ? lab[i] : -1;
+        const unsigned same = __match_any_sync(0xffffffffu, l);
+        if (in && (threadIdx.x & 31) == __ffs(same) - 1) {
+            if (local) atomicAdd(&sh[l], (unsigned)__popc(same));
+            else atomicAdd(&hist[l], (unsigned)__popc(same));
+        }
+        if (!in) continue;
         if (labels_out) labels_out[i] = l;
         if (best_out) {
             const float* xr = X + i * d;
@@ -713,18 +751,27 @@ cudaError_t launch_accum_split(PassArgs a, const RowSplit& rs, const CenterSplit
         e = cudaFuncSetAttribute(k_rescore_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
         if (e != cudaSuccess) return e;
     }
-    k_decide_cands<<<num_sms() * 4, kSplitThreads, 0, st>>>(a.X, a.d, a.C, rs.perm, rs.cands, cs.nflag, cs.error,
-                                                             rs.ovf, cs.novf, rs.lab, a.counters);
+    int64_t fb = (a.n + kSplitThreads - 1) / kSplitThreads;
+    if (fb > (int64_t)num_sms() * 8) fb = (int64_t)num_sms() * 8;
+    k_flag_list<<<(int)fb, kSplitThreads, 0, st>>>(rs.lab, a.n, rs.cands, cs.error, rs.perm, cs.nflag, rs.ovf,
+                                                   cs.novf, a.counters);
+    k_decide_cands<<<num_sms() * 4, kSplitThreads, 0, st>>>(a.X, a.d, a.C, rs.perm, cs.nflag, rs.cands, cs.error,
+                                                             rs.lab);
     k_rescore_tc<<<num_sms() * 8, kRescoreThreads, rsm, st>>>(a.X, a.n, a.d, a.C, cs.ct, a.hc, a.k, a.prep, rs.ovf,
                                                               cs.novf, cs.error, rs.lab, a.counters);
-    k_fix_labels<<<(int)blocks, kSplitThreads, 0, st>>>(a.X, a.n, a.d, a.C, a.k, rs.lab, cs.hist, a.labels, a.best);
+    // each CTA flushes up to k counters: enough rows per CTA that the flush stays small
+    int64_t hb = (a.n + 4 * (int64_t)a.k - 1) / (4 * (int64_t)a.k);
+    if (hb > blocks) hb = blocks;
+    if (hb < 1) hb = 1;
+    k_fix_labels<<<(int)hb, kSplitThreads, 0, st>>>(a.X, a.n, a.d, a.C, a.k, rs.lab, cs.hist, a.labels, a.best);
+    const bool aligned4 = a.d % 4 == 0 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0;
     k_scan_labels<<<1, 1024, 0, st>>>(cs.hist, a.k, cs.cursor);
     int64_t sb = (a.n + kScatterRows - 1) / kScatterRows;
     if (sb > cap) sb = cap;
     // grouped labels (the scatter's second output) in the overflow list's space, free from here on
     int32_t* glab = reinterpret_cast<int32_t*>(rs.ovf);
     k_scatter_rows<<<(int)sb, kSplitThreads, 0, st>>>(rs.lab, a.n, a.k, cs.cursor, rs.perm, glab);
-    if (a.d % 4 == 0 && (reinterpret_cast<uintptr_t>(a.X) & 15) == 0) {
+    if (aligned4) {
         const int d4 = a.d / 4;
         const int lpr = d4 <= 4 ? 4 : d4 <= 8 ? 8 : d4 <= 16 ? 16 : 32;
         const int v = d4 > 32 ? 2 : 1;
