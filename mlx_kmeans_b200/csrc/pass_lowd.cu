@@ -14,7 +14,7 @@
 //            lane, NumPy-pairwise D64, lowest index on ties -- so a label is never decided by rounding.
 //   totals   residual t = x - c_label (the float32 `best` is built from it, square and add rounded on their
 //            own); lane-private float32 sums per (cluster, column) and 8-bit counts in shared memory; every
-//            block of kRowsPerLane rows per lane the warp folds the 32 lanes in float64 in a fixed order,
+//            block of kRowsPerLane rows per lane the warp folds the 32 lanes in a fixed order (fold_block),
 //            adds count * c back (sum x = sum t + n c), rounds once to the fixed-point grid and adds the
 //            integers into the CTA's int64 totals.  Inertia: float64 per lane, folded per block likewise.
 // A block is a fixed range of kBlockRows local rows, so results are bit-reproducible; with shard starts that
@@ -49,10 +49,10 @@ constexpr int kStages = 8;             // ring slots per thread of the screening
 // rows per thread in flight in the bounded kernel, held in registers: about 128 bytes of rows
 constexpr int bounded_ahead(int d) { return KMC_BOUNDED_AHEAD ? KMC_BOUNDED_AHEAD : d <= 4 ? 8 : 4; }
 #ifndef KMC_ROWS_PER_LANE
-#define KMC_ROWS_PER_LANE 128
+#define KMC_ROWS_PER_LANE 64
 #endif
 constexpr int kRowsPerLane = KMC_ROWS_PER_LANE;   // rows per lane between folds (a multiple of 16, < 256)
-constexpr int kBlockRows = kThreads * kRowsPerLane;   // 16384 rows per block
+constexpr int kBlockRows = kThreads * kRowsPerLane;   // 8192 rows per block
 constexpr int kQueue = 64;             // queued rows per warp in the bounded kernel (power of two, >= 64)
 static_assert(kRowsPerLane % kStages == 0 && kRowsPerLane % 8 == 0 && kRowsPerLane < 256, "block layout");
 
@@ -592,9 +592,11 @@ struct LowdRow {
     // End of a block: fold the lanes' slots into the CTA's int64 totals (fixed order => deterministic) and
     // the block's inertia into acc[1].  Counts first: the even and the odd 8-bit fields of each word are summed
     // over the warp as 16-bit fields (at most 32 * kRowsPerLane < 2^16 each), and lane j < 4 parks the count of
-    // cluster 4 w + j in its own word.  Then lane L folds columns s = c * D + j (s = L, L + 32, ...): the 32
-    // lanes' partial sums in float64 in a fixed rotation, then sum x = sum t + count * c rounded once to the
-    // fixed-point grid.
+    // cluster 4 w + j in its own word.  Then the columns: the 32 lanes' partial sums of a column in a fixed
+    // order (even D: columns j, j + 1 of a cluster as one packed float32 pair, a five-level tree; odd D: one
+    // column in float64), then sum x = sum t + count * c in float64, rounded once to the fixed-point grid.  (The
+    // lanes' partials are sequential float32 sums of kRowsPerLane residuals already; five more levels of float32
+    // addition keep the error of the same order.)
     __device__ __forceinline__ void fold_block(long long* acc, const double* scale_x, double scale_i) {
         static_assert(32 * kRowsPerLane < 65536, "16-bit count fields");
         __syncwarp();
@@ -607,21 +609,45 @@ struct LowdRow {
             cnts[w * 32 + lane] = lane < 2 ? (f & 0xffffu) : lane < 4 ? (f >> 16) : 0u;
         }
         __syncwarp();
-        for (int s = lane; s < K * D; s += 32) {
-            const int c = s / D, j = s % D;
-            const float* col = sums + (size_t)c * 32 * D + j;
-            double sum = 0.0;
-#pragma unroll 8
-            for (int i = 0; i < 32; i++) {
-                const int li = (i + lane) & 31;
-                sum = __dadd_rn(sum, (double)col[li * D]);
-            }
+        auto put = [&](int c, int j, double sum) {
             const unsigned cnt = cnts[(c >> 2) * 32 + (c & 3)];
             if (c < k && cnt) {
                 const double sxv = __fma_rn((double)cnt, (double)cs[c * D + j], sum);
                 atomicAdd(reinterpret_cast<unsigned long long*>(&acc[c * (D + 2) + 2 + j]),
                           (unsigned long long)__double2ll_rn(__dmul_rn(sxv, scale_x[j])));
                 if (j == 0) atomicAdd(reinterpret_cast<unsigned long long*>(&acc[c * (D + 2)]), (unsigned long long)cnt);
+            }
+        };
+        if constexpr (D % 2 == 0) {
+            // columns j, j + 1 of a cluster side by side: the 32 lanes' pairs summed in packed float32 by a
+            // fixed five-level tree (four eight-leaf trees, then their pairs)
+            for (int p = lane; p < K * D / 2; p += 32) {
+                const int c = (2 * p) / D, j = (2 * p) % D;
+                const float* col = sums + (size_t)c * 32 * D + j;
+                unsigned long long part[4];
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    unsigned long long v[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++)
+                        v[e] = *reinterpret_cast<const unsigned long long*>(col + ((8 * q + e + lane) & 31) * D);
+                    part[q] = add2(add2(add2(v[0], v[1]), add2(v[2], v[3])), add2(add2(v[4], v[5]), add2(v[6], v[7])));
+                }
+                const unsigned long long s2 = add2(add2(part[0], part[1]), add2(part[2], part[3]));
+                put(c, j, (double)lo_of(s2));
+                put(c, j + 1, (double)hi_of(s2));
+            }
+        } else {
+            for (int s = lane; s < K * D; s += 32) {
+                const int c = s / D, j = s % D;
+                const float* col = sums + (size_t)c * 32 * D + j;
+                double sum = 0.0;
+#pragma unroll 8
+                for (int i = 0; i < 32; i++) {
+                    const int li = (i + lane) & 31;
+                    sum = __dadd_rn(sum, (double)col[li * D]);
+                }
+                put(c, j, sum);
             }
         }
         __syncwarp();

@@ -250,8 +250,8 @@ def torch_int32():
 @pytest.mark.parametrize("cfg,n", [(3, 1_000_000), (1, 100_000)])
 def test_bounded_steps_match_full_steps(cfg, n, cuda_device):
     """Lloyd steps with per-row bounds against full steps from the same start: identical counts, empties,
-    labels (read back from the bound words), inertia within 1e-7 relative and centers within 1e-7 of the data
-    RMS at every step."""
+    labels (read back from the bound words), inertia within 1e-7 relative and centers within one float32 ulp
+    (plus 1e-7 of the data RMS) at every step."""
     import mlx_kmeans_b200 as km
     from mlx_kmeans_b200.data import CONFIGS, generate
     torch = _torch()
@@ -272,8 +272,11 @@ def test_bounded_steps_match_full_steps(cfg, n, cuda_device):
         lab_full = b.assign(Cb, return_labels=True)[3]
         assert np.array_equal(_word_labels(a, k), lab_full), f"step {step}: labels differ"
         assert np.array_equal(a.assign(Ca)[1], b.assign(Cb)[1])
-        # the same holds for the per-lane partial sums of x: the last float32 bit of a center may move
-        assert float((Na - Nb).abs().max()) <= 1e-7 * rms
+        # the same holds for the per-lane partial sums of x (and the float32 fold of the lanes): the last
+        # float32 bit of a center may move -- one unit in the last place of the center, or 1e-7 of the data RMS
+        # for a center near zero
+        tol = torch.abs(Nb).double() * 2.0 ** -23 + 1e-7 * rms
+        assert bool(((Na - Nb).abs().double() <= tol).all())
         screened.append(sa["screened"])
         Ca, Cb = Na.clone(), Nb.clone()
     assert screened[0] == n                       # the first pass compares every row
