@@ -147,7 +147,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 // The two smallest scores with their centers and the third smallest score.  push() takes centers in increasing
 // index order (a strict less keeps the lower index first on ties); merge() takes another tracker's entries,
-// ordered by (score, index).  A NaN score is never taken.
+// ordered by (score, index).
 struct Top3 {
     float m0, m1, m2;
     int l0, l1;
@@ -155,13 +155,16 @@ struct Top3 {
         m0 = m1 = m2 = INFINITY;
         l0 = l1 = 0;
     }
+    // values by a min / max insertion network (equal values keep their order), centers by two selects; a NaN
+    // score leaves the centers alone and can only pull m1 and m2 down to m0 (a wider window: the row goes to
+    // the float64 decision)
     __device__ __forceinline__ void push(float s, int c) {
-        const bool a0 = s < m0, a1 = s < m1, a2 = s < m2;
-        m2 = a1 ? m1 : (a2 ? s : m2);
-        m1 = a0 ? m0 : (a1 ? s : m1);
+        const bool a0 = s < m0, a1 = s < m1;
         l1 = a0 ? l0 : (a1 ? c : l1);
-        m0 = a0 ? s : m0;
         l0 = a0 ? c : l0;
+        m2 = fminf(m2, fmaxf(m1, s));
+        m1 = fminf(m1, fmaxf(m0, s));
+        m0 = fminf(m0, s);
     }
     __device__ __forceinline__ void push_ordered(float s, int c) {
         const bool a0 = s < m0 || (s == m0 && c < l0), a1 = s < m1 || (s == m1 && c < l1), a2 = s < m2;

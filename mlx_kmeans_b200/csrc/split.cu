@@ -92,40 +92,64 @@ __global__ void __launch_bounds__(kSplitThreads) k_split_centers(const float* __
     }
 }
 
-// The rows the tensor-core kernel flagged (label bit 31), listed by a coalesced scan of the labels (one atomic
-// per warp with flagged rows); the rows with more than two candidates go straight to the overflow list.
+// The rows the tensor-core kernel flagged (label bit 31), listed by a coalesced scan of the labels: each CTA
+// takes kFlagRows rows, stages its flagged rows in shared memory (room for all of them) and reserves their
+// places in the global lists with one atomic per list; the rows with more than two candidates go straight to
+// the overflow list.
 constexpr int kSplitWarps = kSplitThreads / 32;
+constexpr int kFlagRows = 4096;
 __global__ void __launch_bounds__(kSplitThreads) k_flag_list(const int32_t* __restrict__ lab, int64_t n,
                                                             const int4* __restrict__ cands,
                                                             const int* __restrict__ tc_error,
                                                             uint32_t* __restrict__ list, unsigned int* __restrict__ nlist,
                                                             uint32_t* __restrict__ ovf, unsigned int* __restrict__ novf,
                                                             long long* __restrict__ counters) {
+    __shared__ uint32_t s_list[kFlagRows], s_ovf[kFlagRows];
+    __shared__ unsigned s_nl, s_no, s_at_l, s_at_o;
     if (*tc_error) return;
-    const int lane = threadIdx.x & 31;
-    const int64_t stride = (int64_t)gridDim.x * kSplitThreads;
-    unsigned long long flagged = 0;
-    for (int64_t base = (int64_t)blockIdx.x * kSplitThreads + (threadIdx.x & ~31); base < n; base += stride) {
-        const int64_t row = base + lane;
-        const bool f = row < n && lab[row] < 0;
-        const bool over = f && cands[row].w == -2;
-        const unsigned fm = __ballot_sync(0xffffffffu, f && !over), om = __ballot_sync(0xffffffffu, over);
-        flagged += __popc(fm) + __popc(om);
-        const unsigned below = (1u << lane) - 1u;
-        if (fm) {
-            unsigned at = 0;
-            if (lane == 0) at = atomicAdd(nlist, (unsigned)__popc(fm));
-            at = __shfl_sync(0xffffffffu, at, 0);
-            if (f && !over) list[at + __popc(fm & below)] = (uint32_t)row;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) s_nl = s_no = 0u;
+    __syncthreads();
+    constexpr int kPerWarp = kFlagRows / kSplitWarps;       // 512 rows: 16 chunks of 32, loaded 4 at a time
+    const int64_t w0 = (int64_t)blockIdx.x * kFlagRows + (int64_t)warp * kPerWarp;
+    for (int c0 = 0; c0 < kPerWarp; c0 += 4 * 32) {
+        int32_t lv[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int64_t row = w0 + c0 + q * 32 + lane;
+            lv[q] = row < n ? lab[row] : 0;
         }
-        if (om) {
-            unsigned at = 0;
-            if (lane == 0) at = atomicAdd(novf, (unsigned)__popc(om));
-            at = __shfl_sync(0xffffffffu, at, 0);
-            if (over) ovf[at + __popc(om & below)] = (uint32_t)row;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int64_t row = w0 + c0 + q * 32 + lane;
+            const bool f = lv[q] < 0;
+            const bool over = f && cands[row].w == -2;
+            const unsigned fm = __ballot_sync(0xffffffffu, f && !over), om = __ballot_sync(0xffffffffu, over);
+            const unsigned below = (1u << lane) - 1u;
+            if (fm) {
+                unsigned at = 0;
+                if (lane == 0) at = atomicAdd(&s_nl, (unsigned)__popc(fm));
+                at = __shfl_sync(0xffffffffu, at, 0);
+                if (f && !over) s_list[at + __popc(fm & below)] = (uint32_t)row;
+            }
+            if (om) {
+                unsigned at = 0;
+                if (lane == 0) at = atomicAdd(&s_no, (unsigned)__popc(om));
+                at = __shfl_sync(0xffffffffu, at, 0);
+                if (over) s_ovf[at + __popc(om & below)] = (uint32_t)row;
+            }
         }
     }
-    if (lane == 0 && flagged) atomicAdd(reinterpret_cast<unsigned long long*>(&counters[0]), flagged);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        s_at_l = s_nl ? atomicAdd(nlist, s_nl) : 0u;
+        s_at_o = s_no ? atomicAdd(novf, s_no) : 0u;
+        if (s_nl + s_no)
+            atomicAdd(reinterpret_cast<unsigned long long*>(&counters[0]), (unsigned long long)(s_nl + s_no));
+    }
+    __syncthreads();
+    for (unsigned e = threadIdx.x; e < s_nl; e += kSplitThreads) list[s_at_l + e] = s_list[e];
+    for (unsigned e = threadIdx.x; e < s_no; e += kSplitThreads) ovf[s_at_o + e] = s_ovf[e];
 }
 
 // The listed rows: the float64 distance (NumPy-pairwise D64) of each of a row's (two) candidate centers; the
@@ -205,11 +229,33 @@ __global__ void __launch_bounds__(kRescoreThreads) k_rescore_tc(const float* __r
             sx2 = x2;
         }
         float m = INFINITY;
-        for (int c = tid; c < k; c += kRescoreThreads) {
-            float v = hc[c];
-            for (int j = 0; j < d; j++) v = __fmaf_rn(-xs[j], ct[(int64_t)j * k + c], v);
-            sc[c] = v;
-            m = fminf(m, v);
+        // four of the thread's centers at a time: four independent chains (each in column order from hc, as the
+        // window assumes) and four coalesced loads per column
+        for (int c0 = tid; c0 < k; c0 += 4 * kRescoreThreads) {
+            float v[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int c = c0 + i * kRescoreThreads;
+                v[i] = c < k ? hc[c] : 0.0f;
+            }
+#pragma unroll 4
+            for (int j = 0; j < d; j++) {
+                const float xj = -xs[j];
+                const float* row = ct + (int64_t)j * k;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int c = c0 + i * kRescoreThreads;
+                    if (c < k) v[i] = __fmaf_rn(xj, row[c], v[i]);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int c = c0 + i * kRescoreThreads;
+                if (c < k) {
+                    sc[c] = v[i];
+                    m = fminf(m, v[i]);
+                }
+            }
         }
 #pragma unroll
         for (int o = 16; o; o >>= 1) m = fminf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -280,25 +326,25 @@ __global__ void __launch_bounds__(kSplitThreads) k_fix_labels(const float* __res
         for (int c = threadIdx.x; c < k; c += blockDim.x) sh[c] = 0u;
     __syncthreads();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    // (the loop runs whole warps: the lanes with the same label add once, so a run of equal labels does not
-    // serialise on one counter)
-    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); i0 < n; i0 += stride) {
-        const int64_t i = i0 + (threadIdx.x & 31);
-        const bool in = i < n;
-        const int l = in ? lab[i] : -1;
-        const unsigned same = __match_any_sync(0xffffffffu, l);
-        if (in && (threadIdx.x & 31) == __ffs(same) - 1) {
-            if (local) atomicAdd(&sh[l], (unsigned)__popc(same));
-            else atomicAdd(&hist[l], (unsigned)__popc(same));
-        }
-        if (!in) continue;
-        if (labels_out) labels_out[i] = l;
-        if (best_out) {
-            const float* xr = X + i * d;
-            const float* cr = C + (int64_t)l * d;
-            float b = 0.0f;
-            for (int j = 0; j < d; j++) b = best32_term(b, xr[j], cr[j]);
-            best_out[i] = b;
+    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n; i0 += 4 * stride) {
+        int lv[4];                                  // four rows' labels loaded before any is counted
+#pragma unroll
+        for (int q = 0; q < 4; q++) lv[q] = i0 + q * stride < n ? lab[i0 + q * stride] : -1;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int64_t i = i0 + q * stride;
+            const int l = lv[q];
+            if (l < 0) continue;
+            if (local) atomicAdd(&sh[l], 1u);
+            else atomicAdd(&hist[l], 1u);
+            if (labels_out) labels_out[i] = l;
+            if (best_out) {
+                const float* xr = X + i * d;
+                const float* cr = C + (int64_t)l * d;
+                float b = 0.0f;
+                for (int j = 0; j < d; j++) b = best32_term(b, xr[j], cr[j]);
+                best_out[i] = b;
+            }
         }
     }
     __syncthreads();
@@ -751,8 +797,7 @@ cudaError_t launch_accum_split(PassArgs a, const RowSplit& rs, const CenterSplit
         e = cudaFuncSetAttribute(k_rescore_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
         if (e != cudaSuccess) return e;
     }
-    int64_t fb = (a.n + kSplitThreads - 1) / kSplitThreads;
-    if (fb > (int64_t)num_sms() * 8) fb = (int64_t)num_sms() * 8;
+    const int64_t fb = (a.n + kFlagRows - 1) / kFlagRows;
     k_flag_list<<<(int)fb, kSplitThreads, 0, st>>>(rs.lab, a.n, rs.cands, cs.error, rs.perm, cs.nflag, rs.ovf,
                                                    cs.novf, a.counters);
     k_decide_cands<<<num_sms() * 4, kSplitThreads, 0, st>>>(a.X, a.d, a.C, rs.perm, cs.nflag, rs.cands, cs.error,

@@ -69,7 +69,8 @@ def _embeddings(n, d, k_true, seed):
     return X.astype(np.float32)
 
 
-@pytest.mark.parametrize("n,d,k", [(20_000, 768, 300), (3_001, 100, 600), (50_000, 128, 512), (4_000, 64, 64)])
+@pytest.mark.parametrize("n,d,k", [(20_000, 768, 300), (3_001, 100, 600), (50_000, 128, 512), (4_000, 64, 64),
+                                   (30_000, 32, 64), (5_000, 20, 40)])
 def test_tc_matches_cuda_core_pass(n, d, k, cuda_device):
     """Ragged row tiles, padded columns, several (padded) center tiles: labels and totals identical to the
     CUDA-core pass, labels identical to the float64 oracle."""
