@@ -72,6 +72,13 @@ class Clocks:
         self.proc = None
         self.path = os.path.join("/tmp", f"kmc_clocks_{os.getpid()}.csv")
 
+    def _lines(self):
+        try:
+            with open(self.path) as f:
+                return f.read().count("\n")
+        except OSError:
+            return 0
+
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
@@ -79,10 +86,20 @@ class Clocks:
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        # nvidia-smi can take a while to start (several ranks start it at once): the timed region (short at
+        # 8 GPUs) begins only once sampling runs, at most 5 s later
+        t = time.time()
+        while self._lines() == 0 and time.time() - t < 5.0 and self.proc.poll() is None:
+            time.sleep(0.01)
 
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        # one sample after the timed region too
+        n, t = self._lines(), time.time()
+        while self._lines() <= n and time.time() - t < 0.5 and self.proc.poll() is None:
+            time.sleep(0.01)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -240,6 +257,7 @@ def main():
     if tc:
         (spl, splb), (csp, cspb) = ds.split()[0], ds.csplit(k)
     flags = _lib.KMC_PASS_GENERIC if args.generic else 0
+    xch = ds._exchange(k) if world > 1 else False
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
@@ -267,9 +285,15 @@ def main():
             _lib.check(L.kmc_pass(X.data_ptr(), X.shape[0], d, Cin.data_ptr(), k, cm.data_ptr(), n_total,
                                   b["totals"].data_ptr(), None, None, flags, b["ws"].data_ptr(), b["wsb"], sp))
         ev[i][1].record(st)
-        ds.allreduce_totals(b, k)
-        _lib.check(L.kmc_finish(b["totals"].data_ptr(), k, d, None, 0, 1, Cout.data_ptr(), stats[i].data_ptr(),
-                                b["ws"].data_ptr(), b["wsb"], sp))
+        if xch:      # the all-reduce over peer memory and the finish in one launch
+            _lib.check(L.kmc_exchange_finish(b["totals"].data_ptr(), k, d, xch["dev"].data_ptr(), world, rank,
+                                             xch["step"], Cout.data_ptr(), stats[i].data_ptr(), b["ws"].data_ptr(),
+                                             b["wsb"], sp))
+            xch["step"] += 1
+        else:
+            ds.allreduce_totals(b, k)
+            _lib.check(L.kmc_finish(b["totals"].data_ptr(), k, d, None, 0, 1, Cout.data_ptr(), stats[i].data_ptr(),
+                                    b["ws"].data_ptr(), b["wsb"], sp))
     t1.record(st)
     host_ms = (time.perf_counter() - h0) * 1e3 / K      # host time to issue one step (the GPU must not wait)
     torch.cuda.synchronize()
@@ -343,7 +367,7 @@ def main():
                                                    f" (rows overridden: {n_total})"),
                    "rows": n_total, "dims": d, "k": k,
                    "parallelism": f"rows sharded dp{world}, int64 totals all-reduced " +
-                                  ("(peer memory, kmc_exchange_sum)" if world > 1 and ds._xch.get(k) else "(NCCL)"),
+                                  ("(peer memory, kmc_exchange_finish)" if world > 1 and ds._xch.get(k) else "(NCCL)"),
                    "l2": "inputs larger than L2 (%.2f GB per GPU), no flush" % (bytes_per_launch / 1e9),
                    "relocation_steps_in_timed_region": reloc_steps,
                    "rows_rescored_in_float64_per_pass": rescored,
@@ -362,10 +386,11 @@ def main():
                       "peak_source": (f"{src} bf16_tflops_sustained (MEASURED_PEAKS.json)" if src == "measured"
                                       else "fallback")}),
         "clocks": clk,
-        # per step: k_prepare, the pass (tensor cores: k_split_centers, k_assign_tc and the six kernels of the
-        # float64 decision and the per-cluster reduction), k_exchange_sum when the totals go through peer memory,
-        # k_finish
-        "gpu_launches": ((10 if tc else 3) + (1 if world > 1 and ds._xch.get(k) else 0)) * K,
+        # per step: k_prepare, the pass (tensor cores: k_split_centers, k_assign_tc and the seven kernels of the
+        # float64 decision and the per-cluster reduction), k_finish (it runs the all-reduce over peer memory first
+        # on several GPUs; with NCCL instead, NCCL's own kernel, not counted) and, above 32768 center values,
+        # k_finish_centers
+        "gpu_launches": ((11 + (1 if k * d > 32768 else 0)) if tc else 3) * K,
         "host_enqueue_ms_per_step": host_ms,
         "e2e": e2e,
     }

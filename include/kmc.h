@@ -145,6 +145,12 @@ int kmc_exchange_close(void *ptr, int own);
 int kmc_exchange_sum(int64_t *totals, int k, int d, const uint64_t *peers, int world, int rank, uint64_t step,
                      void *workspace, size_t ws_bytes, void *stream);
 
+/* kmc_exchange_sum then kmc_finish without relocation candidates, in one launch (the step's tail when rows are
+ * sharded over GPUs): the same exchange protocol and step count (`step` as for kmc_exchange_sum; a timeout sets
+ * stats flag 2 and leaves this rank's own totals), then the divide, empties and statistics of kmc_finish. */
+int kmc_exchange_finish(int64_t *totals, int k, int d, const uint64_t *peers, int world, int rank, uint64_t step,
+                        float *C_new, kmc_stats *stats, void *workspace, size_t ws_bytes, void *stream);
+
 /* kmc_pass without a caller workspace.  No counterpart in the reference: it exists for callers that cannot
  * allocate device memory -- a host runtime that owns every device allocation through its own pool, or a
  * phase of a program in which calling an allocator is not allowed -- and so cannot provide the workspace

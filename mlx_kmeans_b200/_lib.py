@@ -43,6 +43,7 @@ SIGNATURES = {
     "kmc_exchange_open": (_int, [_vp, _vp]),
     "kmc_exchange_close": (_int, [_vp, _int]),
     "kmc_exchange_sum": (_int, [_vp, _int, _int, _vp, _int, _int, _u64, _vp, _sz, _vp]),
+    "kmc_exchange_finish": (_int, [_vp, _int, _int, _vp, _int, _int, _u64, _vp, _vp, _vp, _sz, _vp]),
     "kmc_split_bytes": (_sz, [_i64, _int]),
     "kmc_split_rows": (_int, [_vp, _i64, _int, _vp, _sz, _vp]),
     "kmc_csplit_bytes": (_sz, [_int, _int]),

@@ -262,8 +262,8 @@ class Dataset:
             dist.all_reduce(b["totals"], op=dist.ReduceOp.SUM, group=self.group)
 
     # -- one pass
-    def run_pass(self, C, labels=False, generic=False, bounded=False):
-        """kmc_pass over every local slice, then the all-reduce of the totals. C: (k, d) float32 CUDA.
+    def run_pass(self, C, labels=False, generic=False, bounded=False, reduce=True):
+        """kmc_pass over every local slice, then (reduce) the all-reduce of the totals. C: (k, d) float32 CUDA.
         bounded: use and refresh the per-row bounds (kmc_pass_bounded; no labels)."""
         k = C.shape[0]
         b = self.buffers(k)
@@ -289,7 +289,8 @@ class Dataset:
                           _ptr(b["totals"]), _ptr(lab[i]) if labels else None, _ptr(bst[i]) if labels else None,
                           flags, _ptr(b["ws"]), b["wsb"], st)
             flags |= _lib.KMC_PASS_ACCUMULATE
-        self.allreduce_totals(b, k)
+        if reduce:
+            self.allreduce_totals(b, k)
         return b
 
     def read_stats(self, b):
@@ -304,9 +305,16 @@ class Dataset:
         steps so rows whose label cannot have changed skip the comparison with every center (the labels are
         those of a full pass; the totals agree to the float32 rounding of the per-lane partial sums)."""
         k = C.shape[0]
-        b = self.run_pass(C, generic=generic, bounded=bounded)
-        _lib.call("kmc_finish", _ptr(b["totals"]), k, self.d, None, 0, 1, _ptr(b["C_new"]), _ptr(b["stats"]),
-                  _ptr(b["ws"]), b["wsb"], _stream())
+        x = self._exchange(k) if self.group is not None else False
+        b = self.run_pass(C, generic=generic, bounded=bounded, reduce=not x)
+        if x:
+            # the all-reduce over peer memory and the finish in one launch
+            _lib.call("kmc_exchange_finish", _ptr(b["totals"]), k, self.d, _ptr(x["dev"]), self.world, self.rank,
+                      x["step"], _ptr(b["C_new"]), _ptr(b["stats"]), _ptr(b["ws"]), b["wsb"], _stream())
+            x["step"] += 1
+        else:
+            _lib.call("kmc_finish", _ptr(b["totals"]), k, self.d, None, 0, 1, _ptr(b["C_new"]), _ptr(b["stats"]),
+                      _ptr(b["ws"]), b["wsb"], _stream())
         s = self.read_stats(b)
         if s["flags"] & 2:
             raise RuntimeError("the all-reduce of the totals timed out waiting for a peer GPU")

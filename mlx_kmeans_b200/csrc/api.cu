@@ -346,6 +346,23 @@ int kmc_exchange_sum(int64_t* totals, int k, int d, const uint64_t* peers, int w
     return KMC_OK;
 }
 
+int kmc_exchange_finish(int64_t* totals, int k, int d, const uint64_t* peers, int world, int rank, uint64_t step,
+                        float* C_new, kmc_stats* stats, void* workspace, size_t ws_bytes, void* stream) {
+    if (int s = check_shape(0, d, k)) return s;
+    if (!totals || !peers || !C_new || !stats || !workspace)
+        return fail(KMC_ERR_INVALID, "kmc_exchange_finish: null pointer");
+    if (world < 1 || world > 64 || rank < 0 || rank >= world)
+        return fail(KMC_ERR_INVALID, "kmc_exchange_finish: rank %d of %d (at most 64 GPUs)", rank, world);
+    Workspace ws = carve(workspace, d, k);
+    if (ws_bytes < ws.bytes)
+        return fail(KMC_ERR_INVALID, "kmc_exchange_finish: workspace of %zu bytes, need %zu", ws_bytes, ws.bytes);
+    cudaError_t e = launch_finish(reinterpret_cast<long long*>(totals), k, d, nullptr, 0, 1, C_new, stats, ws,
+                                  static_cast<cudaStream_t>(stream), reinterpret_cast<const unsigned long long*>(peers),
+                                  world, rank, step);
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_exchange_finish");
+    return KMC_OK;
+}
+
 int kmc_far_rows(const float* X, int64_t n, int d, const int32_t* labels, const float* best, int64_t row0,
                  int64_t cand_rows, uint32_t* cands, void* workspace, size_t ws_bytes, void* stream) {
     if (int s = check_shape(n, d, 1)) return s;

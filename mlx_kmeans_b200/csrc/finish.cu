@@ -3,6 +3,7 @@
 // totals into the float64 sums / int64 counts that core.py:2200-2206 `assign_mlx` returns.
 #include "common.cuh"
 #include "kmc_internal.h"
+#include "exchange.cuh"
 
 namespace kmc {
 
@@ -138,6 +139,9 @@ struct FinishArgs {
     int* reloc;
     long long* empty;
     bool grid_centers;
+    const unsigned long long* peers;   // the all-reduce over peer memory first (nullptr: none)
+    int world, rank;
+    unsigned long long step;
 };
 
 // center c, column j of the new centers (cnt = the cluster's count, > 0): sums / counts in float64, rounded
@@ -156,7 +160,9 @@ __global__ void __launch_bounds__(1024) k_finish(FinishArgs a) {
     __shared__ long long s_bigc[32];
     __shared__ int s_bigi[32];
     __shared__ long long sh_n_empty, sh_inert, sh_nreloc;
-    __shared__ int sh_big, sh_write;
+    __shared__ int sh_big, sh_write, sh_xfail;
+    // 0. (fused step tail) the totals summed over the ranks
+    if (a.peers) exchange_cta(a.totals, (int64_t)k * W, a.peers, a.world, a.rank, a.step, a.counters, &sh_xfail);
     // 1. inertia (exact int64 sum) and empty count, before any relocation (core.py:2223)
     long long in = 0, ne = 0;
     for (int c = tid; c < k; c += nt) {
@@ -315,7 +321,8 @@ __global__ void __launch_bounds__(256) k_finish_centers(FinishArgs a) {
 }
 
 cudaError_t launch_finish(long long* totals, int k, int d, const uint32_t* cands, int64_t cand_rows, int ranks,
-                          float* C_new, void* stats, const Workspace& ws, cudaStream_t st) {
+                          float* C_new, void* stats, const Workspace& ws, cudaStream_t st,
+                          const unsigned long long* peers, int world, int rank, unsigned long long step) {
     FinishArgs a;
     a.totals = totals;
     a.k = k;
@@ -330,6 +337,10 @@ cudaError_t launch_finish(long long* totals, int k, int d, const uint32_t* cands
     a.counters = ws.counters;
     a.reloc = ws.reloc;
     a.empty = ws.empty;
+    a.peers = peers;
+    a.world = world;
+    a.rank = rank;
+    a.step = step;
     const int64_t total = (int64_t)k * d;
     a.grid_centers = total > kFinishOneCta;
     k_finish<<<1, 1024, 0, st>>>(a);

@@ -129,7 +129,9 @@ cudaError_t launch_exchange_sum(long long* totals, int k, int d, const unsigned 
 cudaError_t launch_far_rows(const float* X, int64_t n, int d, const int32_t* labels, const float* best, int64_t row0,
                             int64_t cand_rows, uint32_t* cands, const FarWorkspace& ws, cudaStream_t st);
 cudaError_t launch_finish(long long* totals, int k, int d, const uint32_t* cands, int64_t cand_rows, int ranks,
-                          float* C_new, void* stats, const Workspace& ws, cudaStream_t st);
+                          float* C_new, void* stats, const Workspace& ws, cudaStream_t st,
+                          const unsigned long long* peers = nullptr, int world = 1, int rank = 0,
+                          unsigned long long step = 0);
 cudaError_t launch_unpack(const long long* totals, int k, int d, const double* scale_x, const Prep* prep,
                           const long long* counters, double* sums, int64_t* counts, double* inertia, cudaStream_t st);
 
