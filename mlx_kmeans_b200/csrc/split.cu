@@ -4,8 +4,9 @@
 //                    multiple of 64 with zeros) and |x| rounded up, for assign_tc.cu
 //   k_split_centers  once per pass: the same split of the centers (rows padded to the MMA tile), |c|^2/2 and
 //                    max |c| (rounded up)
-//   k_decide_cands   the rows assign_tc.cu flagged (label bit 31): float64 (NumPy-pairwise D64, one warp per
-//                    row) of their two candidate centers, lowest index on ties; rows with more candidates:
+//   k_flag_list      the rows assign_tc.cu flagged (label bit 31), listed (staged per CTA in shared memory)
+//   k_decide_cands   their float64 decision (NumPy-pairwise D64 of the two candidate centers, a thread per row
+//                    for d <= 128, a warp per row beyond), lowest index on ties; rows with more candidates:
 //   k_rescore_tc     one CTA per row: a float32 screen of every center, then D64 of each center in its window
 //   k_fix_labels     per row: the histogram of the labels; the optional labels / best outputs (best: the
 //                    reference's float32 distance, each operation rounded on its own, in column order)
