@@ -71,7 +71,9 @@ def test_duplicate_centers_never_use_the_higher_copy():
     assert labels.max() < 16
 
 
-@pytest.mark.parametrize("d", [1, 2, 3, 7, 8, 9, 15, 16, 17, 31, 64, 100, 127, 128, 129, 200, 256, 768, 960, 1537])
+# (includes every length tests/test_tc_gpu.py::test_d64_warp_bit_identical compares the GPU's D64 at)
+@pytest.mark.parametrize("d", [1, 2, 3, 7, 8, 9, 15, 16, 17, 31, 32, 64, 100, 127, 128, 129, 136, 200, 255, 256,
+                               513, 768, 960, 1000, 1537, 4096])
 def test_d64_is_numpy_pairwise(d):
     rng = np.random.default_rng(d)
     for _ in range(40):
