@@ -209,10 +209,23 @@ class Dataset:
     # -- the all-reduce of the totals over the ranks
     def _exchange(self, k):
         """Peer-memory exchange buffers for k centers: one per rank, mapped by every peer through CUDA IPC
-        (kmc_exchange_*); False when the ranks cannot map each other's memory (then NCCL is used)."""
+        (kmc_exchange_*); False when the ranks cannot map each other's memory (then NCCL is used).  One set per
+        (process group, k, d), shared by every Dataset of that group and held until the process exits: a peer
+        may still be reading this rank's buffer when a Dataset goes away, so a buffer is never freed mid-run."""
         x = self._xch.get(k)
         if x is not None:
             return x
+        key = (id(self.group), k, self.d)
+        hit = _exchanges.get(key)
+        if hit is not None:
+            self._xch[k] = hit[1]
+            return hit[1]
+        x = self._open_exchange(k)
+        _exchanges[key] = (self.group, x)          # (the group is kept so that its id is not reused)
+        self._xch[k] = x
+        return x
+
+    def _open_exchange(self, k):
         import torch.distributed as dist
         L = _lib.load()
         x = False
@@ -239,12 +252,10 @@ class Dataset:
             dist.all_gather_object(oks, len(ptrs) == self.world, group=self.group)
             if all(oks):
                 x = dict(dev=torch.tensor(ptrs, dtype=torch.int64, device=self.device), step=0)
-                weakref.finalize(self, _close_exchange, opened, own.value)
             else:
                 _close_exchange(opened, own.value)
         elif own.value:
             L.kmc_exchange_close(own, 1)
-        self._xch[k] = x
         return x
 
     def allreduce_totals(self, b, k):
@@ -365,6 +376,10 @@ class Dataset:
         if return_labels:
             out += (torch.cat(b["labels"]).to(torch.int64).cpu().numpy(),)
         return out
+
+
+# (process-group id, k, d) -> (group, exchange): see Dataset._exchange
+_exchanges = {}
 
 
 def _close_exchange(opened, own):

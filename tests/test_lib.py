@@ -54,3 +54,31 @@ def test_invalid_arguments_are_reported_not_thrown():
     assert L.kmc_finish(None, 4, 4, None, 0, 1, None, None, None, 0, None) == _lib.KMC_ERR_INVALID
     with pytest.raises(ValueError):
         _lib.call("kmc_pass", None, 10, 0, None, 4, None, 10, None, None, None, 0, None, 0, None)
+
+
+def test_exchange_buffers_shared_per_group(monkeypatch):
+    """Datasets of one process group share one set of peer-memory exchange buffers per (k, d) and never free
+    them mid-run (a peer may still read a buffer when a Dataset goes away): a second Dataset reuses the first
+    one's buffers and step count instead of opening new ones.  Host logic only (the opening is stubbed)."""
+    from mlx_kmeans_b200 import core
+    opened = []
+
+    def fake_open(self, k):
+        opened.append((k, self.d))
+        return dict(dev=None, step=0)
+
+    monkeypatch.setattr(core.Dataset, "_open_exchange", fake_open)
+    monkeypatch.setattr(core, "_exchanges", {})
+    group = object()
+
+    def ds(d):
+        x = object.__new__(core.Dataset)
+        x.group, x.d, x._xch = group, d, {}
+        return x
+
+    a, b, c = ds(4), ds(4), ds(8)
+    xa = a._exchange(16)
+    xa["step"] += 3
+    assert b._exchange(16) is xa and b._exchange(16)["step"] == 3
+    assert c._exchange(16) is not xa
+    assert opened == [(16, 4), (16, 8)]
