@@ -136,8 +136,9 @@ int kmc_pass_split(const float *X, int64_t n, int d, const float *C, int k, cons
  * addresses (own included, at index rank).  Per pass, after the pass on every local slice: kmc_exchange_sum with
  * a step number that every rank increments the same way (0, 1, 2, ...); on return (stream order) totals hold the
  * sum over ranks.  A peer that does not arrive within seconds sets stats flag 2 (read by kmc_finish).  All ranks
- * must call it the same number of times.  kmc_exchange_close(ptr, own) unmaps a peer's buffer (own = 0) or frees
- * one's own (own = 1). */
+ * must call it the same number of times (kmc_exchange_sum and kmc_exchange_finish share the step count).
+ * kmc_exchange_close(ptr, own) unmaps a peer's buffer (own = 0) or frees one's own (own = 1): only once every
+ * rank is done with the buffers, since a peer may still be reading one after its owner's call returned. */
 size_t kmc_exchange_bytes(int k, int d);
 int kmc_exchange_alloc(size_t bytes, void **ptr, void *handle);
 int kmc_exchange_open(const void *handle, void **ptr);
