@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Generate the golden fixtures in tests/golden/ from the reference's own Python oracle.
 
-Run in a container where the reference checkout is mounted (REFERENCE_ROOT, default /root/reference):
+Run where the reference checkout is mounted (its directory in REFERENCE_ROOT, or the default below):
 
     python tests/golden/make_golden.py
 
