@@ -25,3 +25,25 @@ def test_reference_arm_prints_one_contract_line():
     cb = j["cpu_baseline"]
     assert cb["value"] == j["value"] and cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"]
     assert "config3" in j["config"]["workload"]
+
+
+def test_clock_sampler_waits_for_its_first_sample(tmp_path, monkeypatch):
+    """The clock record of a short timed region: sampling starts before the region (nvidia-smi may take a
+    while to start) and takes one more sample after it.  A stand-in nvidia-smi prints the query's CSV rows."""
+    import importlib.util
+    import time
+    fake = tmp_path / "nvidia-smi"
+    fake.write_text("#!/bin/bash\nsleep 0.3\nwhile true; do\n"
+                    "  echo '0, 1965, 1965, 700.0, 0x0, Not Active, Not Active, Not Active, Active'\n"
+                    "  sleep 0.05\ndone\n")
+    fake.chmod(0o755)
+    monkeypatch.setenv("PATH", f"{tmp_path}:{os.environ.get('PATH', '')}")
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    c = bench.Clocks("0")
+    c.start()
+    time.sleep(0.01)                                    # a timed region shorter than the sampling interval
+    rec = c.stop()
+    assert rec["samples"] >= 2 and rec["sm_mhz"] == 1965.0 and rec["sm_max_mhz"] == 1965.0
+    assert rec["reasons"] == ["sw_power_cap"]
