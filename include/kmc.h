@@ -128,6 +128,13 @@ int kmc_pass_split(const float *X, int64_t n, int d, const float *C, int k, cons
                    size_t split_bytes, void *csplit, size_t csplit_bytes, void *workspace, size_t ws_bytes,
                    void *stream);
 
+/* The tensor-core pass's raw scores, for auditing its error window (no counterpart in the reference): out
+ * (device, n x k float32) = x.c for every row of the split (kmc_split_rows) and every center, exactly as the
+ * tcgen05 MMAs of kmc_pass_split accumulate them (xh.ch + xh.cl + xl.ch in float32), before any decision.
+ * error (device, one int) is set to 1 if the kernel gave up on a barrier (out is then incomplete). */
+int kmc_tc_dot(const float *C, int64_t n, int d, int k, void *split, size_t split_bytes, void *csplit,
+               size_t csplit_bytes, float *out, int *error, void *stream);
+
 /* All-reduce of the totals over the GPUs of one node through peer memory (NVLink), one kernel per step: no
  * counterpart in the reference (single device); it replaces an NCCL all-reduce of the int64 totals.  Set-up once
  * per (process group, k): each rank kmc_exchange_alloc's a kmc_exchange_bytes(k, d) buffer (device memory the
@@ -135,7 +142,8 @@ int kmc_pass_split(const float *X, int64_t n, int d, const float *C, int k, cons
  * collective); each rank kmc_exchange_open's its peers' buffers.  `peers` is a device array of the world buffer
  * addresses (own included, at index rank).  Per pass, after the pass on every local slice: kmc_exchange_sum with
  * a step number that every rank increments the same way (0, 1, 2, ...); on return (stream order) totals hold the
- * sum over ranks.  A peer that does not arrive within seconds sets stats flag 2 (read by kmc_finish).  All ranks
+ * sum over ranks.  A peer that does not arrive within KMC_EXCHANGE_TIMEOUT_MS milliseconds (an environment variable read on
+ * every call; 30 s when unset) sets stats flag 2 (read by kmc_finish) and the totals keep this rank's own values.  All ranks
  * must call it the same number of times (kmc_exchange_sum and kmc_exchange_finish share the step count).
  * kmc_exchange_close(ptr, own) unmaps a peer's buffer (own = 0) or frees one's own (own = 1): only once every
  * rank is done with the buffers, since a peer may still be reading one after its owner's call returned. */
@@ -155,13 +163,17 @@ int kmc_exchange_finish(int64_t *totals, int k, int d, const uint64_t *peers, in
 /* kmc_pass without a caller workspace.  No counterpart in the reference: it exists for callers that cannot
  * allocate device memory -- a host runtime that owns every device allocation through its own pool, or a
  * phase of a program in which calling an allocator is not allowed -- and so cannot provide the workspace
- * kmc_pass asks for.  Its scratch is a file-scope device array of KMC_STATIC_SCRATCH_BYTES per GPU, held from
- * the library's load until the process exits; shapes needing more (kmc_workspace_bytes(d, k) above it, e.g.
- * k above ~4000 at d = 64) are refused with KMC_ERR_UNSUPPORTED.  It calls no allocator.  The first call on a
- * device looks up that device's copy of the array (cudaGetSymbolAddress); make that first call before any
- * stream capture.  All calls share the one array and it keeps the last call's contents: calls whose work
- * overlaps on the GPU race, so issue them in one stream (or order them).  The pass clears what must start at
- * zero itself (totals and counters, unless KMC_PASS_ACCUMULATE).  Arguments, outputs and errors as kmc_pass. */
+ * kmc_pass asks for.  Its scratch is a file-scope device array of KMC_STATIC_SCRATCH_BYTES, one copy in every
+ * CUDA context that loads the library, held until the process exits; shapes needing more
+ * (kmc_workspace_bytes(d, k) above it, e.g. k above ~4000 at d = 64) are refused with KMC_ERR_UNSUPPORTED.  It
+ * calls no allocator.  The first call in a context looks up that context's copy of the array
+ * (cudaGetSymbolAddress) and caches it; make that first call before any stream capture.  All calls in a
+ * context share the one array and it keeps the last call's contents: calls whose work overlaps on the GPU
+ * race, so issue them in one stream (or order them).  The pass clears what must start at zero itself (totals
+ * and counters, unless KMC_PASS_ACCUMULATE).  The array also holds the fixed-point grid of the totals, so
+ * finish the step with kmc_finish or kmc_totals_unpack given workspace = NULL: they then read the same array,
+ * and must follow the kmc_pass_static that made the totals in stream order, before the next one.
+ * Arguments, outputs and errors as kmc_pass. */
 #define KMC_STATIC_SCRATCH_BYTES (64 * 1024)
 int kmc_pass_static(const float *X, int64_t n, int d, const float *C, int k, const uint32_t *colmax,
                     int64_t n_total, int64_t *totals, int32_t *labels, float *best, unsigned flags, void *stream);
@@ -174,7 +186,7 @@ int kmc_far_rows(const float *X, int64_t n, int d, const int32_t *labels, const 
                  int64_t cand_rows, uint32_t *cands, void *workspace, size_t ws_bytes, void *stream);
 
 /* Finish a Lloyd step from the (global) totals, on the workspace of the kmc_pass that made them (its
- * fixed-point grid lives there): relocation of empty clusters to the farthest rows (candidate lists of
+ * fixed-point grid lives there; workspace = NULL: the static scratch of kmc_pass_static, ws_bytes ignored): relocation of empty clusters to the farthest rows (candidate lists of
  * `ranks` ranks, each from kmc_far_rows, concatenated; NULL when none were gathered), then
  * C_new = sums / counts rounded to float32, a still-empty cluster takes the largest cluster's center,
  * and kmc_stats.  totals are updated in place by the relocation.  C_new (device, k x d).
@@ -186,7 +198,8 @@ int kmc_finish(int64_t *totals, int k, int d, const uint32_t *cands, int64_t can
 int kmc_stats_read(const kmc_stats *stats_dev, kmc_stats *stats_host, void *stream);
 
 /* Convert totals to float64 sums (k x d), int64 counts (k) and the inertia (all device), as
- * core.py:2200-2206 `assign_mlx` returns them; same workspace as the kmc_pass that made the totals. */
+ * core.py:2200-2206 `assign_mlx` returns them; same workspace as the kmc_pass that made the totals
+ * (workspace = NULL: the static scratch of kmc_pass_static, ws_bytes ignored). */
 int kmc_totals_unpack(const int64_t *totals, int k, int d, double *sums, int64_t *counts, double *inertia,
                       void *workspace, size_t ws_bytes, void *stream);
 

@@ -49,6 +49,7 @@ SIGNATURES = {
     "kmc_csplit_bytes": (_sz, [_int, _int]),
     "kmc_pass_split": (_int, [_vp, _i64, _int, _vp, _int, _vp, _i64, _vp, _vp, _vp, _u, _vp, _sz, _vp, _sz, _vp, _sz,
                               _vp]),
+    "kmc_tc_dot": (_int, [_vp, _i64, _int, _int, _vp, _sz, _vp, _sz, _vp, _vp, _vp]),
     "kmc_far_rows": (_int, [_vp, _i64, _int, _vp, _vp, _i64, _i64, _vp, _vp, _sz, _vp]),
     "kmc_finish": (_int, [_vp, _int, _int, _vp, _i64, _int, _vp, _vp, _vp, _sz, _vp]),
     "kmc_stats_read": (_int, [_vp, _vp, _vp]),

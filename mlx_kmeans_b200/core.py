@@ -103,14 +103,7 @@ class Dataset:
         self.group = group
         self.n_local = sum(p.shape[0] for p in self.parts)
         if group is not None:
-            import torch.distributed as dist
-            self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
-            counts = torch.tensor([self.n_local], dtype=torch.int64, device=self.device)
-            allc = [torch.zeros_like(counts) for _ in range(self.world)]
-            dist.all_gather(allc, counts, group=group)
-            allc = [int(c.item()) for c in allc]
-            self.row0 = sum(allc[:self.rank])
-            self.n_total = sum(allc)
+            self.rank, self.world, self.row0, self.n_total = shard_plan(self.n_local, group, self.device)
         else:
             self.rank, self.world, self.row0, self.n_total = 0, 1, 0, self.n_local
         self._ws = {}
@@ -133,8 +126,7 @@ class Dataset:
                 _lib.call("kmc_colmax", _ptr(p), p.shape[0], self.d, _ptr(cm), flags, _stream())
                 flags = _lib.KMC_PASS_ACCUMULATE
             if self.group is not None:
-                import torch.distributed as dist
-                dist.all_reduce(cm, op=dist.ReduceOp.MAX, group=self.group)
+                allreduce_colmax(cm, self.group)
             self._colmax = cm
         return self._colmax
 
@@ -352,12 +344,9 @@ class Dataset:
         local = torch.cat(lists, 0) if len(lists) > 1 else lists[0]
         nlists = len(lists)
         if self.group is not None:
-            import torch.distributed as dist
             if len(self.parts) != 1:
                 raise ValueError("a sharded Dataset holds one slice per rank")
-            gathered = [torch.empty_like(local) for _ in range(self.world)]
-            dist.all_gather(gathered, local, group=self.group)
-            local = torch.cat(gathered, 0)
+            local = gather_candidates(local, self.group, self.world)
             nlists = self.world
         _lib.call("kmc_finish", _ptr(b["totals"]), k, self.d, _ptr(local), E, nlists, _ptr(b["C_new"]),
                   _ptr(b["stats"]), _ptr(b["ws"]), b["wsb"], _stream())
@@ -380,6 +369,36 @@ class Dataset:
 
 # (process-group id, k, d) -> (group, exchange): see Dataset._exchange
 _exchanges = {}
+
+
+# ---------------------------------------------------------------- multi-rank host steps (any torch.distributed
+# backend: NCCL with CUDA tensors in the product, gloo with CPU tensors in the CPU tests)
+
+def shard_plan(n_local, group, device):
+    """(rank, world, row0, n_total) of a rank holding n_local contiguous rows: the rows of lower ranks come first."""
+    import torch.distributed as dist
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    counts = torch.tensor([n_local], dtype=torch.int64, device=device)
+    allc = [torch.zeros_like(counts) for _ in range(world)]
+    dist.all_gather(allc, counts, group=group)
+    allc = [int(c.item()) for c in allc]
+    return rank, world, sum(allc[:rank]), sum(allc)
+
+
+def allreduce_colmax(cm, group):
+    """The global per-column max |x| from every rank's (float bits as int32: they order like the values)."""
+    import torch.distributed as dist
+    dist.all_reduce(cm, op=dist.ReduceOp.MAX, group=group)
+    return cm
+
+
+def gather_candidates(local, group, world):
+    """Every rank's far-row candidate list (E records each, kmc_far_rows' layout), concatenated in rank order: the
+    layout kmc_finish merges (farthest first, lower global row on ties) with ranks = world."""
+    import torch.distributed as dist
+    gathered = [torch.empty_like(local) for _ in range(world)]
+    dist.all_gather(gathered, local, group=group)
+    return torch.cat(gathered, 0)
 
 
 def _close_exchange(opened, own):

@@ -7,6 +7,8 @@
 #include <mutex>
 #include <string>
 
+#include <cuda.h>
+
 #include "../../include/kmc.h"
 #include "kmc_internal.h"
 
@@ -92,6 +94,80 @@ BoundsState carve_bounds(void* base, int64_t n, int d, int k) {
 size_t bounds_bytes(int64_t n, int d, int k) {
     return 256 + a256(sizeof(float) * (size_t)k * d) + a256(sizeof(uint32_t) * (size_t)(n > 0 ? n : 1));
 }
+
+// ---------------------------------------------------------------- kmc_pass_static
+// The pass with its scratch in a file-scope device array instead of a caller buffer, for callers that
+// cannot allocate device memory.  Every context that loads the library's module holds one copy
+// (KMC_STATIC_SCRATCH_BYTES) until the process exits.  Host code cannot hand the array's name to a kernel (on
+// the host it is only a stand-in symbol), so the address of the current context's copy is looked up with
+// cudaGetSymbolAddress, with that context current, and cached per context: a __device__ variable has its own
+// address in every context (a runtime that drives the GPU through a driver-API context of its own gets a copy
+// separate from the primary context's).
+static __device__ __align__(256) unsigned char g_static_scratch[KMC_STATIC_SCRATCH_BYTES];
+
+namespace {
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+std::mutex g_static_mu;
+struct StaticSlot {
+    CUcontext ctx;
+    void* addr;
+};
+constexpr int kStaticSlots = 64;
+StaticSlot g_static_slots[kStaticSlots];
+int g_static_used = 0;
+
+// cuCtxGetCurrent through the runtime's driver entry point (the library does not link libcuda itself)
+CtxGetCurrentFn ctx_get_current() {
+    static CtxGetCurrentFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    }
+    return fn;
+}
+
+// The current context's copy of g_static_scratch (the first call in a context looks it up).
+int static_scratch(const char* who, void** out) {
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    CtxGetCurrentFn get = ctx_get_current();
+    if (!get) return fail(KMC_ERR_CUDA, "%s: cuCtxGetCurrent is not available from the driver", who);
+    CUcontext ctx = nullptr;
+    if (get(&ctx) != CUDA_SUCCESS) return fail(KMC_ERR_CUDA, "%s: cuCtxGetCurrent failed", who);
+    if (ctx)
+        for (int i = 0; i < g_static_used; i++)
+            if (g_static_slots[i].ctx == ctx) {
+                *out = g_static_slots[i].addr;
+                return KMC_OK;
+            }
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);   // makes the device's primary context current
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress");
+    if (p == nullptr) return fail(KMC_ERR_CUDA, "%s: cudaGetSymbolAddress returned a null address", who);
+    if (!ctx && (get(&ctx) != CUDA_SUCCESS || !ctx))
+        return fail(KMC_ERR_CUDA, "%s: no current CUDA context after cudaGetSymbolAddress", who);
+    if (g_static_used == kStaticSlots) return fail(KMC_ERR_UNSUPPORTED, "%s: more than %d CUDA contexts", who, kStaticSlots);
+    g_static_slots[g_static_used++] = StaticSlot{ctx, p};
+    *out = p;
+    return KMC_OK;
+}
+
+// kmc_finish / kmc_totals_unpack given no workspace: the static scratch kmc_pass_static left its grid in
+int static_workspace(const char* who, int d, int k, void** workspace, size_t* ws_bytes) {
+    if (*workspace) return KMC_OK;
+    const size_t need = carve(nullptr, d, k).bytes;
+    if (need > (size_t)KMC_STATIC_SCRATCH_BYTES)
+        return fail(KMC_ERR_UNSUPPORTED, "%s: d=%d, k=%d need %zu bytes of workspace, above the fixed %d bytes of "
+                    "the static scratch", who, d, k, need, (int)KMC_STATIC_SCRATCH_BYTES);
+    if (int s = static_scratch(who, workspace)) return s;
+    *ws_bytes = (size_t)KMC_STATIC_SCRATCH_BYTES;
+    return KMC_OK;
+}
+}  // namespace
 
 }  // namespace kmc
 
@@ -271,6 +347,7 @@ int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, cons
     ts.lab = rs.lab;
     ts.cands = rs.cands;
     ts.error = cs.error;
+    ts.dump = nullptr;
     e = launch_assign_tc(ts, st);
     if (e != cudaSuccess) return cuda_fail(e, who);
     PassArgs a;
@@ -292,6 +369,42 @@ int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, cons
     a.key_keep = 0;
     a.brows = nullptr;
     e = launch_accum_split(a, rs, cs, st);
+    if (e != cudaSuccess) return cuda_fail(e, who);
+    return KMC_OK;
+}
+
+int kmc_tc_dot(const float* C, int64_t n, int d, int k, void* split, size_t split_bytes, void* csplit,
+               size_t csplit_bytes, float* out, int* error, void* stream) {
+    const char* who = "kmc_tc_dot";
+    if (int s = check_shape(n, d, k)) return s;
+    if (!C || !split || !csplit || !out || !error) return fail(KMC_ERR_INVALID, "%s: null pointer", who);
+    if (n > (int64_t)UINT32_MAX) return fail(KMC_ERR_INVALID, "%s: %lld rows in one call", who, (long long)n);
+    if (split_bytes < split_rows_bytes(n, d) || csplit_bytes < split_centers_bytes(d, k))
+        return fail(KMC_ERR_INVALID, "%s: split buffers too small", who);
+    if (n == 0) return KMC_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const RowSplit rs = carve_rows(split, n, d);
+    const CenterSplit cs = carve_centers(csplit, d, k);
+    cudaError_t e = launch_split_centers(C, k, d, cs, st);
+    if (e != cudaSuccess) return cuda_fail(e, who);
+    TcSplit ts;
+    ts.n = n;
+    ts.dp = split_dp(d);
+    ts.kp = split_kp(k);
+    ts.k = k;
+    ts.xh = rs.xh;
+    ts.xl = rs.xl;
+    ts.ch = cs.ch;
+    ts.cl = cs.cl;
+    ts.hs = cs.hs;
+    ts.xn = rs.xn;
+    ts.cmax = reinterpret_cast<const float*>(cs.cmax_bits);
+    ts.lab = rs.lab;
+    ts.cands = rs.cands;
+    ts.error = cs.error;
+    ts.dump = out;
+    e = launch_assign_tc(ts, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(error, cs.error, sizeof(int), cudaMemcpyDeviceToDevice, st);
     if (e != cudaSuccess) return cuda_fail(e, who);
     return KMC_OK;
 }
@@ -380,9 +493,10 @@ int kmc_far_rows(const float* X, int64_t n, int d, const int32_t* labels, const 
 int kmc_finish(int64_t* totals, int k, int d, const uint32_t* cands, int64_t cand_rows, int ranks, float* C_new,
                kmc_stats* stats, void* workspace, size_t ws_bytes, void* stream) {
     if (int s = check_shape(0, d, k)) return s;
-    if (!totals || !C_new || !stats || !workspace) return fail(KMC_ERR_INVALID, "kmc_finish: null pointer");
+    if (!totals || !C_new || !stats) return fail(KMC_ERR_INVALID, "kmc_finish: null pointer");
     if (cands && (cand_rows < 1 || ranks < 1 || ranks > 64))
         return fail(KMC_ERR_INVALID, "kmc_finish: cand_rows %lld / ranks %d", (long long)cand_rows, ranks);
+    if (int s = static_workspace("kmc_finish", d, k, &workspace, &ws_bytes)) return s;
     Workspace ws = carve(workspace, d, k);
     if (ws_bytes < ws.bytes) return fail(KMC_ERR_INVALID, "kmc_finish: workspace of %zu bytes, need %zu", ws_bytes, ws.bytes);
     cudaError_t e = launch_finish(reinterpret_cast<long long*>(totals), k, d, cands, cand_rows, ranks, C_new, stats, ws,
@@ -403,7 +517,8 @@ int kmc_stats_read(const kmc_stats* stats_dev, kmc_stats* stats_host, void* stre
 int kmc_totals_unpack(const int64_t* totals, int k, int d, double* sums, int64_t* counts, double* inertia,
                       void* workspace, size_t ws_bytes, void* stream) {
     if (int s = check_shape(0, d, k)) return s;
-    if (!totals || !sums || !counts || !inertia || !workspace) return fail(KMC_ERR_INVALID, "kmc_totals_unpack: null pointer");
+    if (!totals || !sums || !counts || !inertia) return fail(KMC_ERR_INVALID, "kmc_totals_unpack: null pointer");
+    if (int s = static_workspace("kmc_totals_unpack", d, k, &workspace, &ws_bytes)) return s;
     Workspace ws = carve(workspace, d, k);
     if (ws_bytes < ws.bytes) return fail(KMC_ERR_INVALID, "kmc_totals_unpack: workspace of %zu bytes, need %zu", ws_bytes, ws.bytes);
     cudaError_t e = launch_unpack(reinterpret_cast<const long long*>(totals), k, d, ws.scale_x, ws.prep, ws.counters, sums, counts,
@@ -466,19 +581,6 @@ int kmc_standardize(float* X, int64_t n, int d, const int64_t* sums, const uint3
 }
 
 
-// ---------------------------------------------------------------- kmc_pass_static
-// The pass with its scratch in a file-scope device array instead of a caller buffer, for callers that
-// cannot allocate device memory.  Every GPU that loads the library holds one copy (KMC_STATIC_SCRATCH_BYTES)
-// until the process exits.  Host code cannot hand the array's name to a kernel (on the host it is only a
-// stand-in symbol), so each device's address is looked up once with cudaGetSymbolAddress, with that device
-// current, and cached.
-static __device__ __align__(256) unsigned char g_static_scratch[KMC_STATIC_SCRATCH_BYTES];
-
-namespace {
-std::mutex g_static_mu;
-void* g_static_addr[256] = {};
-}  // namespace
-
 int kmc_pass_static(const float* X, int64_t n, int d, const float* C, int k, const uint32_t* colmax, int64_t n_total,
                     int64_t* totals, int32_t* labels, float* best, unsigned flags, void* stream) {
     if (int s = check_shape(n, d, k)) return s;
@@ -487,21 +589,8 @@ int kmc_pass_static(const float* X, int64_t n, int d, const float* C, int k, con
         return fail(KMC_ERR_UNSUPPORTED,
                     "kmc_pass_static: d=%d, k=%d need %zu bytes of scratch, above the fixed %d bytes; "
                     "use kmc_pass with a caller workspace", d, k, need, (int)KMC_STATIC_SCRATCH_BYTES);
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return cuda_fail(e, "kmc_pass_static: cudaGetDevice");
-    if (dev < 0 || dev >= 256) return fail(KMC_ERR_UNSUPPORTED, "kmc_pass_static: device ordinal %d", dev);
     void* ws = nullptr;
-    {
-        std::lock_guard<std::mutex> lock(g_static_mu);
-        if (!g_static_addr[dev]) {
-            void* p = nullptr;
-            e = cudaGetSymbolAddress(&p, g_static_scratch);
-            if (e != cudaSuccess || p == nullptr) return cuda_fail(e, "kmc_pass_static: cudaGetSymbolAddress");
-            g_static_addr[dev] = p;
-        }
-        ws = g_static_addr[dev];
-    }
+    if (int s = static_scratch("kmc_pass_static", &ws)) return s;
     return kmc_pass(X, n, d, C, k, colmax, n_total, totals, labels, best, flags, ws, (size_t)KMC_STATIC_SCRATCH_BYTES,
                     stream);
 }

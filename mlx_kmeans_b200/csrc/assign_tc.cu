@@ -192,6 +192,7 @@ struct TcArgs {
     int32_t* lab;            // n: label | flag << 31 (flag: decide the row in float64)
     int4* cands;             // n: a flagged row's candidate centers (-1: none, w = -2: more than two)
     int* error;              // set on a barrier timeout
+    float* dump;             // (kmc_tc_dot) n x k: every accumulated x.c as read from TMEM, or nullptr
 };
 
 template <int BN, bool AR>
@@ -365,6 +366,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     float v[32];
                     tmem_ld32(lane_base + abuf * BN + cc, v);
                     const int c0 = nt * BN + cc;
+                    if (a.dump != nullptr && row < a.n) {          // diagnostic copy of the raw scores
+#pragma unroll 1
+                        for (int j = 0; j < 32; j++)
+                            if (c0 + j < a.k) a.dump[row * a.k + c0 + j] = v[j];
+                    }
 #pragma unroll
                     for (int j = 0; j < 32; j += 2) {
                         ev.push(__ldg(a.hs + c0 + j) - v[j], c0 + j);
@@ -473,6 +479,7 @@ cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
     a.lab = s.lab;
     a.cands = s.cands;
     a.error = s.error;
+    a.dump = s.dump;
     const int64_t tiles = (s.n + BM - 1) / BM;
     int64_t grid = num_sms();
     if (grid > tiles) grid = tiles;

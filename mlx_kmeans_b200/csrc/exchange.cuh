@@ -2,7 +2,7 @@
 // the work of one CTA (k_exchange_sum launches it alone; k_finish runs it first when the step's tail is fused).
 //
 // The rank copies its totals into its own exchange buffer, raises its flag in every peer's buffer (a release
-// store over NVLink), waits for every peer's flag (acquire loads of its own buffer, bounded), and sums all
+// store over NVLink), waits for every peer's flag (acquire loads of its own buffer, for at most a set time), and sums all
 // ranks' totals with plain peer loads.  The sum of integers does not depend on the order, so the result is the
 // same as NCCL's and the same on every rank.
 //
@@ -16,7 +16,13 @@
 
 namespace kmc {
 
-constexpr uint32_t kExSpin = 1u << 26;   // polls before a wait gives up (a few seconds)
+// A wait on a peer gives up after timeout_ns nanoseconds of the GPU's global timer (the limit comes from the
+// host: exchange_timeout_ns()).
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -31,7 +37,8 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
 // counters[1] gets kFlagExchange.  Ends with the summed totals visible to the CTA (a barrier).
 __device__ inline void exchange_cta(long long* __restrict__ totals, int64_t W,
                                     const unsigned long long* __restrict__ peers, int world, int rank,
-                                    unsigned long long step, long long* __restrict__ counters, int* fail) {
+                                    unsigned long long step, unsigned long long timeout_ns,
+                                    long long* __restrict__ counters, int* fail) {
     const int tid = threadIdx.x, nt = blockDim.x;
     if (tid == 0) *fail = 0;
     const size_t slot_off = (size_t)kExchangeHeader + (size_t)(step & 1) * (size_t)W * 8;
@@ -45,9 +52,10 @@ __device__ inline void exchange_cta(long long* __restrict__ totals, int64_t W,
         unsigned long long* flag = reinterpret_cast<unsigned long long*>(peers[tid]) + rank;
         st_release_sys(flag, tag);
         const unsigned long long* own = reinterpret_cast<const unsigned long long*>(mine) + tid;
+        const unsigned long long t0 = global_ns();
         uint32_t i = 0;
         while (ld_acquire_sys(own) < tag) {
-            if (++i == kExSpin) {
+            if ((++i & 63u) == 0 && global_ns() - t0 > timeout_ns) {
                 *fail = 1;
                 break;
             }

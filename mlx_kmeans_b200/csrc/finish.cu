@@ -142,6 +142,7 @@ struct FinishArgs {
     const unsigned long long* peers;   // the all-reduce over peer memory first (nullptr: none)
     int world, rank;
     unsigned long long step;
+    unsigned long long timeout_ns;     // how long the exchange waits for a peer
 };
 
 // center c, column j of the new centers (cnt = the cluster's count, > 0): sums / counts in float64, rounded
@@ -162,7 +163,8 @@ __global__ void __launch_bounds__(1024) k_finish(FinishArgs a) {
     __shared__ long long sh_n_empty, sh_inert, sh_nreloc;
     __shared__ int sh_big, sh_write, sh_xfail;
     // 0. (fused step tail) the totals summed over the ranks
-    if (a.peers) exchange_cta(a.totals, (int64_t)k * W, a.peers, a.world, a.rank, a.step, a.counters, &sh_xfail);
+    if (a.peers)
+        exchange_cta(a.totals, (int64_t)k * W, a.peers, a.world, a.rank, a.step, a.timeout_ns, a.counters, &sh_xfail);
     // 1. inertia (exact int64 sum) and empty count, before any relocation (core.py:2223)
     long long in = 0, ne = 0;
     for (int c = tid; c < k; c += nt) {
@@ -341,6 +343,7 @@ cudaError_t launch_finish(long long* totals, int k, int d, const uint32_t* cands
     a.world = world;
     a.rank = rank;
     a.step = step;
+    a.timeout_ns = peers ? exchange_timeout_ns() : 0;
     const int64_t total = (int64_t)k * d;
     a.grid_centers = total > kFinishOneCta;
     k_finish<<<1, 1024, 0, st>>>(a);

@@ -107,6 +107,7 @@ struct TcSplit {
     int32_t* lab;
     int4* cands;
     int* error;
+    float* dump;              // kmc_tc_dot: n x k raw scores x.c, or nullptr
 };
 int split_dp(int d);
 int split_kp(int k);
@@ -123,6 +124,7 @@ cudaError_t launch_accum_split(PassArgs a, const RowSplit& rs, const CenterSplit
 // Peer-memory all-reduce of the totals (exchange.cu).
 constexpr int kExchangeHeader = 512;      // 64 flags of 8 bytes before the two slots
 size_t exchange_bytes(int k, int d);
+unsigned long long exchange_timeout_ns();
 cudaError_t launch_exchange_sum(long long* totals, int k, int d, const unsigned long long* peers, int world, int rank,
                                 unsigned long long step, long long* counters, cudaStream_t st);
 

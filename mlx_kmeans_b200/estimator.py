@@ -140,10 +140,11 @@ class KMeans:
         if rows < self.n_clusters:
             raise ValueError('n_clusters cannot exceed the number of rows')
         best = None
-        for run in range(self.n_init):                  # restarts reuse the data already on the GPU
+        for run in range(self.n_init):                  # every start runs on the same device-resident Dataset
             seed = None if self.random_state is None else self.random_state + run
             C, inertia, iters = self._one_run(ds, rows, seed)
-            # A Lloyd step reports inertia before its center update: score the final centers (estimator.py:201-204)
+            # the last step's inertia belongs to the centers it started from; one more pass scores the returned ones
+            # (estimator.py:201-204)
             _, _, inertia, labels = ds.assign(C, return_labels=True)
             if self.verbose and self.n_init > 1:
                 print(f"start {run + 1}/{self.n_init}: inertia {inertia:.6e} after {iters} iterations")

@@ -1,9 +1,9 @@
 #!/usr/bin/env python3
 """Generate the golden fixtures in tests/golden/ from the reference's own Python oracle.
 
-Run where the reference checkout is mounted (its directory in REFERENCE_ROOT, or the default below):
+Run where the reference checkout is mounted, with its directory in REFERENCE_ROOT:
 
-    python tests/golden/make_golden.py
+    REFERENCE_ROOT=<reference checkout> python tests/golden/make_golden.py
 
 It imports the reference's float64 test oracle (tests/accuracy.py: `reference`, lines 31-51, and
 `reference_lloyd_step`, lines 108-129) and its CPU path (mlx_kmeans/core.py:197-215 `assign_numpy`),
@@ -17,7 +17,9 @@ import sys
 
 import numpy as np
 
-REF = os.environ.get("REFERENCE_ROOT", "/root/reference")
+REF = os.environ.get("REFERENCE_ROOT")
+if not REF:
+    sys.exit("set REFERENCE_ROOT to the reference checkout (kakollu/mlx-kmeans)")
 OUT = os.path.dirname(os.path.abspath(__file__))
 
 
