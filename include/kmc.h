@@ -15,9 +15,10 @@
  *   - The library allocates nothing on its own for these calls: the caller passes device workspaces
  *     (256-byte aligned) of the sizes the *_workspace_bytes functions give.
  *
- * Numeric contract (the reference's, see core.py:218-219 and tests/accuracy.py:31-51):
+ * Numeric contract (the reference's float64 test oracle, tests/accuracy.py:31-51):
  *   label = the center with the smallest float64 distance sum_j ((double)x_j - (double)c_j)^2 (NumPy's
- *   pairwise summation order), lowest index on exact ties; best = the float32 distance to that center,
+ *   pairwise summation order), lowest index on exact ties -- or, with KMC_PASS_LABEL32, the reference's
+ *   float32 exact-mode rule (core.py:218-219, 263-274); best = the float32 distance to that center,
  *   each square and add rounded on its own; totals are exact and independent of summation order.
  */
 #ifndef KMC_H
@@ -42,6 +43,12 @@ enum kmc_status {
 /* Flags of kmc_pass. */
 #define KMC_PASS_ACCUMULATE 1u   /* add into `totals` instead of overwriting them (data held in slices) */
 #define KMC_PASS_GENERIC 2u      /* force the any-shape kernel (tests compare the specialised kernels to it) */
+/* The float32 label rule of the reference's rows kernel (core.py:263-274, its exact-mode contract at
+ * core.py:218-219): label = the center with the smallest float32 direct sum s = s + (x_j - c_j)^2 over j in
+ * order, each subtraction, square and add rounded on its own (no fused multiply-add), strict < over centers in
+ * index order (lowest index on ties).  Without it the label is the float64-optimal center (the numeric contract
+ * below).  The two differ only where the float32 sums of two centers are within their rounding of each other. */
+#define KMC_PASS_LABEL32 4u
 
 /* Device statistics of one Lloyd step, as kmc_finish leaves them (layout fixed, 64 bytes). */
 typedef struct kmc_stats {

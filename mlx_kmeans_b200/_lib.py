@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(_HERE, "libkmc.so")
 KMC_OK, KMC_ERR_INVALID, KMC_ERR_CUDA, KMC_ERR_UNSUPPORTED = 0, 1, 2, 3
 KMC_PASS_ACCUMULATE = 1
 KMC_PASS_GENERIC = 2
+KMC_PASS_LABEL32 = 4
 KMC_MAX_DIMS = 4096
 STATS_BYTES = 64
 

@@ -84,7 +84,7 @@ class Dataset:
 
     TC_MIN_DIMS = 32                # from here up the assign runs on the tensor cores (kmc_pass_split)
 
-    def __init__(self, parts, group=None, device=None, tensor_cores=None):
+    def __init__(self, parts, group=None, device=None, tensor_cores=None, label_rule="float64"):
         if isinstance(parts, (torch.Tensor, np.ndarray)) or not isinstance(parts, (list, tuple)):
             parts = [parts]
         if not parts:
@@ -100,6 +100,7 @@ class Dataset:
         if d > _lib.KMC_MAX_DIMS:
             raise ValueError(f"{d} dims is above the supported maximum {_lib.KMC_MAX_DIMS}")
         self.d = d
+        self.label_rule = _check_rule(label_rule)
         self.group = group
         self.n_local = sum(p.shape[0] for p in self.parts)
         if group is not None:
@@ -265,14 +266,17 @@ class Dataset:
             dist.all_reduce(b["totals"], op=dist.ReduceOp.SUM, group=self.group)
 
     # -- one pass
-    def run_pass(self, C, labels=False, generic=False, bounded=False, reduce=True):
+    def run_pass(self, C, labels=False, generic=False, bounded=False, reduce=True, rule=None):
         """kmc_pass over every local slice, then (reduce) the all-reduce of the totals. C: (k, d) float32 CUDA.
-        bounded: use and refresh the per-row bounds (kmc_pass_bounded; no labels)."""
+        bounded: use and refresh the per-row bounds (kmc_pass_bounded; no labels). rule: the label rule ("float64"
+        or "float32"; None: the Dataset's)."""
         k = C.shape[0]
         b = self.buffers(k)
         lab, bst = self._label_buffers(b) if labels else (None, None)
         cm = self.colmax
         flags = _lib.KMC_PASS_GENERIC if generic else 0
+        if _check_rule(rule or self.label_rule) == "float32":
+            flags |= _lib.KMC_PASS_LABEL32
         st = _stream()
         bb = self.bounds(k) if bounded and not labels and not generic else None
         tc = self.tensor_cores and not generic
@@ -291,7 +295,7 @@ class Dataset:
                 _lib.call("kmc_pass", _ptr(p), p.shape[0], self.d, _ptr(C), k, _ptr(cm), self.n_total,
                           _ptr(b["totals"]), _ptr(lab[i]) if labels else None, _ptr(bst[i]) if labels else None,
                           flags, _ptr(b["ws"]), b["wsb"], st)
-            flags |= _lib.KMC_PASS_ACCUMULATE
+            flags = flags | _lib.KMC_PASS_ACCUMULATE
         if reduce:
             self.allreduce_totals(b, k)
         return b
@@ -302,14 +306,15 @@ class Dataset:
         return dict(inertia=float(host[:1].view(np.float64)[0]), n_empty=int(host[1]), n_relocated=int(host[2]),
                     needs_reloc=int(host[3]), flags=int(host[4]), rescored=int(host[5]), screened=int(host[6]))
 
-    def step(self, C, generic=False, bounded=True):
+    def step(self, C, generic=False, bounded=True, rule=None):
         """One Lloyd iteration on the device: C (k, d) CUDA -> (C_new CUDA tensor (a buffer reused by the
         next step with the same k; copy it to keep it), stats dict).  bounded: keep per-row bounds between
         steps so rows whose label cannot have changed skip the comparison with every center (the labels are
-        those of a full pass; the totals agree to the float32 rounding of the per-lane partial sums)."""
+        those of a full pass; the totals agree to the float32 rounding of the per-lane partial sums).  rule: the
+        label rule (None: the Dataset's)."""
         k = C.shape[0]
         x = self._exchange(k) if self.group is not None else False
-        b = self.run_pass(C, generic=generic, bounded=bounded, reduce=not x)
+        b = self.run_pass(C, generic=generic, bounded=bounded, reduce=not x, rule=rule)
         if x:
             # the all-reduce over peer memory and the finish in one launch
             _lib.call("kmc_exchange_finish", _ptr(b["totals"]), k, self.d, _ptr(x["dev"]), self.world, self.rank,
@@ -322,14 +327,14 @@ class Dataset:
         if s["flags"] & 2:
             raise RuntimeError("the all-reduce of the totals timed out waiting for a peer GPU")
         if s["needs_reloc"]:
-            s = self._relocate(C, b, s["n_empty"], generic)
+            s = self._relocate(C, b, s["n_empty"], generic, rule)
         return b["C_new"], s
 
-    def _relocate(self, C, b, n_empty, generic):
+    def _relocate(self, C, b, n_empty, generic, rule=None):
         """Empty clusters: recompute the pass with labels and best, gather the farthest rows of every slice
         and rank, and finish again with them (core.py:2224-2236)."""
         k = C.shape[0]
-        b = self.run_pass(C, labels=True, generic=generic)
+        b = self.run_pass(C, labels=True, generic=generic, rule=rule)
         E = int(n_empty)
         R = self.d + 4
         fwb = int(_lib.load().kmc_far_workspace_bytes(E))
@@ -352,10 +357,10 @@ class Dataset:
                   _ptr(b["stats"]), _ptr(b["ws"]), b["wsb"], _stream())
         return self.read_stats(b)
 
-    def assign(self, C, return_labels=False, generic=False):
+    def assign(self, C, return_labels=False, generic=False, rule=None):
         """One pass -> (sums float64 (k, d), counts int64 (k), inertia float[, labels int64 (n_local)])."""
         k = C.shape[0]
-        b = self.run_pass(C, labels=return_labels, generic=generic)
+        b = self.run_pass(C, labels=return_labels, generic=generic, rule=rule)
         sums = torch.empty((k, self.d), dtype=torch.float64, device=self.device)
         counts = torch.empty(k, dtype=torch.int64, device=self.device)
         inertia = torch.empty(1, dtype=torch.float64, device=self.device)
@@ -438,6 +443,18 @@ def _dataset(parts):
     return Dataset(list(parts))
 
 
+LABEL_RULES = ("float64", "float32")
+
+
+def _check_rule(rule):
+    """The label rules: "float64" (the float64-optimal center, NumPy-pairwise distance, lowest index on ties: the
+    reference's test oracle, tests/accuracy.py:31-51) or "float32" (the reference's exact-mode kernels' own rule,
+    core.py:218-219 and 263-274: the float32 direct sum, strict < in index order)."""
+    if rule not in LABEL_RULES:
+        raise ValueError(f"label_rule must be one of {LABEL_RULES}, got {rule!r}")
+    return rule
+
+
 def _check_method(method, accumulate, k, d):
     if method not in EXACT_METHODS + ("approx",):
         raise ValueError(f"unknown method {method!r}")
@@ -462,26 +479,28 @@ def _centers(C, ds):
 
 # ---------------------------------------------------------------- the reference's entry points
 
-def lloyd_step(parts, C, method="auto", accumulate="auto"):
+def lloyd_step(parts, C, method="auto", accumulate="auto", label_rule=None):
     """One exact Lloyd iteration on the GPU -> (new centers float32, inertia, number of empty clusters).
 
     core.py:2209-2242: the inertia belongs to the centers the step started from; empty clusters take the
     farthest rows (farthest first, lower row index on ties), a cluster still empty takes the largest
-    cluster's center. Everything but the statistics stays on the device."""
+    cluster's center. Everything but the statistics stays on the device. label_rule: "float64" or "float32"
+    (None: the Dataset's, "float64" by default)."""
     ds = _dataset(parts)
     Cd = _centers(C, ds)
     _check_method(method, accumulate, Cd.shape[0], ds.d)
-    C_new, s = ds.step(Cd, generic=(method == "generic"))
+    C_new, s = ds.step(Cd, generic=(method == "generic"), rule=label_rule and _check_rule(label_rule))
     inertia = float("nan") if s["flags"] & 1 else s["inertia"]
     return C_new.cpu().numpy(), inertia, s["n_empty"]
 
 
-def assign_mlx(parts, C, method="auto", return_labels=False, accumulate="auto"):
+def assign_mlx(parts, C, method="auto", return_labels=False, accumulate="auto", label_rule=None):
     """One pass -> (per-cluster sums float64, counts int64, inertia[, labels int64]) (core.py:2200-2206)."""
     ds = _dataset(parts)
     Cd = _centers(C, ds)
     _check_method(method, accumulate, Cd.shape[0], ds.d)
-    out = ds.assign(Cd, return_labels=return_labels, generic=(method == "generic"))
+    out = ds.assign(Cd, return_labels=return_labels, generic=(method == "generic"),
+                    rule=label_rule and _check_rule(label_rule))
     return out
 
 

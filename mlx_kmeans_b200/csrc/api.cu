@@ -223,7 +223,7 @@ int pass_impl(const char* who, const float* X, int64_t n, int d, const float* C,
     const bool clear = !(flags & KMC_PASS_ACCUMULATE);
     e = launch_prepare(C, k, d, colmax, n_total, ws.prep, ws.scale_x, ws.hc,
                        clear ? reinterpret_cast<long long*>(totals) : nullptr, clear ? ws.counters : nullptr,
-                       bounded ? b.meta : nullptr, bounded ? b.cprev : nullptr, st);
+                       bounded ? b.meta : nullptr, bounded ? b.cprev : nullptr, (flags & KMC_PASS_LABEL32) ? 1 : 0, st);
     if (e != cudaSuccess) return cuda_fail(e, who);
     if (n == 0) return KMC_OK;
     PassArgs a;
@@ -323,9 +323,10 @@ int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, cons
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e;
     const bool clear = !(flags & KMC_PASS_ACCUMULATE);
+    const int rule = (flags & KMC_PASS_LABEL32) ? 1 : 0;
     e = launch_prepare(C, k, d, colmax, n_total, ws.prep, ws.scale_x, ws.hc,
                        clear ? reinterpret_cast<long long*>(totals) : nullptr, clear ? ws.counters : nullptr, nullptr,
-                       nullptr, st);
+                       nullptr, rule, st);
     if (e != cudaSuccess) return cuda_fail(e, who);
     if (n == 0) return KMC_OK;
     const RowSplit rs = carve_rows(split, n, d);
@@ -348,6 +349,7 @@ int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, cons
     ts.cands = rs.cands;
     ts.error = cs.error;
     ts.dump = nullptr;
+    ts.rule = rule;
     e = launch_assign_tc(ts, st);
     if (e != cudaSuccess) return cuda_fail(e, who);
     PassArgs a;
@@ -403,6 +405,7 @@ int kmc_tc_dot(const float* C, int64_t n, int d, int k, void* split, size_t spli
     ts.cands = rs.cands;
     ts.error = cs.error;
     ts.dump = out;
+    ts.rule = 0;
     e = launch_assign_tc(ts, st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(error, cs.error, sizeof(int), cudaMemcpyDeviceToDevice, st);
     if (e != cudaSuccess) return cuda_fail(e, who);

@@ -193,6 +193,7 @@ struct TcArgs {
     int4* cands;             // n: a flagged row's candidate centers (-1: none, w = -2: more than two)
     int* error;              // set on a barrier timeout
     float* dump;             // (kmc_tc_dot) n x k: every accumulated x.c as read from TMEM, or nullptr
+    float wr;                // window term per (|x| + max|c|)^2: the rounding of the label rule's distance
 };
 
 template <int BN, bool AR>
@@ -345,7 +346,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // Window on the gap between the two best scores: each score is off by at most E |x| |c| (the dropped
         // split terms and the float32 accumulation) plus 2^-24 (|c|^2 + |x| |c|) (rounding of |c|^2/2 and of
         // the subtraction); two of them, with |c| <= cmax, and a 2^-10 margin for the float32 evaluation of the
-        // window itself.  The float64 rounding of D64, which defines the label, adds 2^-40 (|x| + cmax)^2.
+        // window itself.  The distance that defines the label adds wr (|x| + cmax)^2: 2^-40 for the float64
+        // rounding of D64, rule32_coef(d) more under the float32 label rule (its direct sum's error).
         const float E2 = (float)(2.0 * (3.1 / 65536.0 + 3.0 * a.dp / 16777216.0));
         constexpr int HALF = BN / 2;
         uint32_t abuf = 0, aphase = 0;
@@ -399,7 +401,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (row < a.n) {
                 const float r = xr + cmax;
                 const float win = (E2 * xr * cmax + cmax * (cmax + xr) * (1.0f / 8388608.0f)) * (1.0f + 1.0f / 1024.0f) +
-                                  r * r * (1.0f / 1099511627776.0f);
+                                  r * r * a.wr;
                 const bool flag = !(m1 - m0 > win) || l0 >= a.k;
                 a.lab[row] = (int32_t)((uint32_t)l0 | (flag ? 0x80000000u : 0u));
                 // candidates: the centers whose score is within the window of the smallest; when the third is
@@ -480,6 +482,7 @@ cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
     a.cands = s.cands;
     a.error = s.error;
     a.dump = s.dump;
+    a.wr = (float)(1.0 / 1099511627776.0 + (s.rule ? rule32_coef(s.dp) : 0.0));
     const int64_t tiles = (s.n + BM - 1) / BM;
     int64_t grid = num_sms();
     if (grid > tiles) grid = tiles;

@@ -31,7 +31,7 @@ struct Prep {
     int flags;              // kFlag* below
     int bvalid;             // bounded passes: the per-row bounds were written by an earlier pass
     float bcum_lo, bcum_up; // bounded passes: total center drift so far, rounded down / up
-    int pad;
+    int rule;               // label rule: 0 = float64 distance (NumPy pairwise), 1 = float32 direct sum
 };
 
 enum : int {
@@ -79,6 +79,22 @@ __device__ __forceinline__ float best32_term(float s, float x, float c) {
     float q = __fsub_rn(x, c);
     return __fadd_rn(s, __fmul_rn(q, q));
 }
+
+// The float32 direct sum of the reference's rows kernel (core.py:263-274): s = s + (x_j - c_j)^2 over j in
+// order, each operation rounded on its own -- the distance the float32 label rule takes the argmin of.
+__device__ __forceinline__ float best32(const float* x, const float* c, int d) {
+    float s = 0.0f;
+    for (int j = 0; j < d; j++) s = best32_term(s, x[j], c[j]);
+    return s;
+}
+
+// Extra width of a screen window under the float32 label rule.  The direct sum of d terms is B = D (1 + theta),
+// |theta| <= gamma_{d+2} (a subtraction, a square and at most d - 1 additions of nonnegative terms per term), so a
+// center c beats the exact nearest l under that rule only if D_c - D_l <= theta (D_c + D_l), i.e. its half
+// distance exceeds l's by at most theta / (1 - theta) D_l.  With D_l <= 2 (|x|^2 + max|c|^2) (the low-d and
+// CUDA-core screens' unit) or D_l <= (|x| + max|c|)^2 (the tensor-core window's), a coefficient of 2.5 (d + 3) u
+// covers 2 theta / (1 - theta) for every d <= 4096 (u = 2^-24).
+__host__ __device__ inline double rule32_coef(int d) { return 2.5 * (d + 3) / 16777216.0; }
 
 // NumPy's pairwise sum of the float64 terms t_j = ((double)x_j - (double)c_j)^2, j in [lo, lo + n).
 // Fewer than 8 terms: in order; up to 128: eight running partials + tail; longer: split at n/2 rounded

@@ -68,7 +68,7 @@ cudaError_t launch_colmax(const float* X, int64_t n, int d, unsigned int* colmax
 // per-pass constants; optionally clears the totals and counters, and (bmeta != nullptr) prepares a bounded pass
 cudaError_t launch_prepare(const float* C, int k, int d, const unsigned int* colmax, int64_t n_total, Prep* prep,
                            double* scale_x, float* hc, long long* zero_totals, long long* zero_counters,
-                           double* bmeta, float* bcprev, cudaStream_t st);
+                           double* bmeta, float* bcprev, int rule, cudaStream_t st);
 cudaError_t launch_pass_generic(PassArgs a, cudaStream_t st);
 // Specialised low-dimensional fused pass; returns cudaErrorNotSupported when (d, k) has no instance.
 cudaError_t launch_pass_lowd(PassArgs a, cudaStream_t st);
@@ -108,6 +108,7 @@ struct TcSplit {
     int4* cands;
     int* error;
     float* dump;              // kmc_tc_dot: n x k raw scores x.c, or nullptr
+    int rule;                 // label rule (Prep::rule): widens the window
 };
 int split_dp(int d);
 int split_kp(int k);

@@ -81,7 +81,7 @@ __global__ void k_prepare(const float* __restrict__ C, int k, int d, const unsig
                           int64_t n_total, Prep* __restrict__ prep, double* __restrict__ scale_x,
                           float* __restrict__ hc, long long* __restrict__ zero_totals, int zero_n,
                           long long* __restrict__ zero_counters, double* __restrict__ bmeta,
-                          float* __restrict__ bcprev) {
+                          float* __restrict__ bcprev, int rule) {
     __shared__ float s_max[32];
     __shared__ float s_cmax2[32];
     __shared__ int s_bad;
@@ -152,13 +152,13 @@ __global__ void k_prepare(const float* __restrict__ C, int k, int d, const unsig
         p.scale_i = ldexp(1.0, si);
         p.inv_scale_i = ldexp(1.0, -si);
         p.cmax2 = cm2 * (1.0f + 1.0f / 1048576.0f);
-        p.win_coef = (float)(4.0 * (d + 2) / 16777216.0 + (double)d / 281474976710656.0);
+        p.win_coef = (float)(4.0 * (d + 2) / 16777216.0 + (double)d / 281474976710656.0 + (rule ? rule32_coef(d) : 0.0));
         p.win_abs = (float)((d + 2) * 7.174648137343064e-43);               // (d+2) 2^-140
         p.flags = (s_bad || bound > 3.0e38) ? kFlagNonFinite : 0;
         p.bvalid = 0;
         p.bcum_lo = 0.0f;
         p.bcum_up = 0.0f;
-        p.pad = 0;
+        p.rule = rule;
         *prep = p;
     }
     if (bmeta) {
@@ -228,11 +228,12 @@ __global__ void __launch_bounds__(256) k_pass_generic(PassArgs a) {
         if (!live) continue;
         int l = l1;
         const float win = __fmaf_rn(prep.win_coef, x2 + prep.cmax2, prep.win_abs);
-        if (!(s2 - s1 > win)) {             // inside the window (or not finite): decide in float64
+        if (!(s2 - s1 > win)) {             // inside the window (or not finite): decide by the label rule
             double bd = INFINITY;
             int bl = 0;
             for (int c = 0; c < k; c++) {
-                double v = d64_pairwise(xr, a.C + (int64_t)c * d, d);
+                const double v = prep.rule ? (double)best32(xr, a.C + (int64_t)c * d, d)
+                                           : d64_pairwise(xr, a.C + (int64_t)c * d, d);
                 if (v < bd) { bd = v; bl = c; }
             }
             l = bl;
@@ -274,7 +275,7 @@ cudaError_t launch_colmax(const float* X, int64_t n, int d, unsigned int* colmax
 
 cudaError_t launch_prepare(const float* C, int k, int d, const unsigned int* colmax, int64_t n_total, Prep* prep,
                            double* scale_x, float* hc, long long* zero_totals, long long* zero_counters,
-                           double* bmeta, float* bcprev, cudaStream_t st) {
+                           double* bmeta, float* bcprev, int rule, cudaStream_t st) {
     const int64_t zn = (int64_t)k * (d + 2);
     if (zero_totals && zn > 16384) {           // large totals: a memset is faster than one CTA
         cudaError_t e = cudaMemsetAsync(zero_totals, 0, sizeof(long long) * (size_t)zn, st);
@@ -282,7 +283,7 @@ cudaError_t launch_prepare(const float* C, int k, int d, const unsigned int* col
         zero_totals = nullptr;
     }
     k_prepare<<<1, 1024, 0, st>>>(C, k, d, colmax, n_total, prep, scale_x, hc, zero_totals, (int)zn, zero_counters,
-                                  bmeta, bcprev);
+                                  bmeta, bcprev, rule);
     return cudaGetLastError();
 }
 

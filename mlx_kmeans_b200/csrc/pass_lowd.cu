@@ -284,18 +284,30 @@ struct RowVec {
     float v[D];
 };
 
-// Decide the warp's rows flagged in `fm` in float64, one center per lane, lowest index on exact ties; returns
-// the label of the calling lane's row (`l` when its row is not flagged).  Out of line: it runs for a few rows
-// per million and would otherwise take registers from the row loop.
+// The float32 direct sum of the reference's rows kernel on registers (core.py:263-274), as best32
 template <int D>
-__device__ __noinline__ int rescore_rows(unsigned fm, RowVec<D> x, const float* cs, int k, int lane, int l) {
+__device__ __forceinline__ float best32_regs(const float* x, const float* c) {
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < D; j++) s = best32_term(s, x[j], c[j]);
+    return s;
+}
+
+// Decide the warp's rows flagged in `fm` by the label rule (rule 0: the float64 distance, rule 1: the float32
+// direct sum), one center per lane, lowest index on exact ties; returns the label of the calling lane's row
+// (`l` when its row is not flagged).  Out of line: it runs for a few rows per million and would otherwise take
+// registers from the row loop.
+template <int D>
+__device__ __noinline__ int rescore_rows(unsigned fm, RowVec<D> x, const float* cs, int k, int lane, int l,
+                                         int rule) {
     while (fm) {
         const int src = __ffs(fm) - 1;
         fm &= fm - 1;
         float xs[D];
 #pragma unroll
         for (int j = 0; j < D; j++) xs[j] = __shfl_sync(0xffffffffu, x.v[j], src);
-        double v = lane < k ? d64_regs<D>(xs, cs + lane * D) : INFINITY;
+        double v = lane >= k ? INFINITY
+                   : rule ? (double)best32_regs<D>(xs, cs + lane * D) : d64_regs<D>(xs, cs + lane * D);
         int vi = lane;
 #pragma unroll
         for (int o = 16; o; o >>= 1) {
@@ -393,6 +405,8 @@ struct LowdRow {
     static constexpr unsigned MASK = (1u << IDXBITS) - 1u;
     float coef, slack, cmax2, wabs;
     float cum_lo, cum_up;               // drift of the centers since the bounds were started (bounds mode)
+    float hold_f;                       // factor of the bound test (holds), wider under the float32 rule
+    int rule;                           // label rule (Prep::rule)
     unsigned keep;                      // ~(index mask), a launch argument so it stays in a register
     const float* cs;                    // shared copy of the centers (zero padded to 32 rows)
     unsigned cs_s;                      // its shared-window address
@@ -469,7 +483,7 @@ struct LowdRow {
             RowVec<D> xv;
 #pragma unroll
             for (int j = 0; j < D; j++) xv.v[j] = x[j];
-            s.l = rescore_rows<D>(fm, xv, cs, k, lane, s.l);
+            s.l = rescore_rows<D>(fm, xv, cs, k, lane, s.l, rule);
         }
         return s;
     }
@@ -530,10 +544,14 @@ struct LowdRow {
     // the exact distance is below Y^2: b carries at most (D + 4) 2^-23 of relative error, and the computed
     // y = fl(Y) and fl(y y) exceed Y and Y^2 by at most 2^-24 and 3 2^-24 relative, fl(b F) falls short of
     // b F by at most 2^-24 -- all inside F's extra factor 1 + 2^-20.
-    static constexpr float kHoldF = (float)((1.0 + (D + 4) / 8388608.0) * (1.0 + 1.0 / 1048576.0) * (1.0 + 1.0 / 8388608.0));
+    // Under the float32 label rule the stored label must also be the only center the direct sum can pick: every
+    // other center's exact distance must exceed the label's by the direct sum's relative error on both sides,
+    // (1 + theta) / (1 - theta) with theta <= gamma_{D+2}, folded into the factor as 1 + rule32_coef(D).
+    static constexpr double kHoldD = (1.0 + (D + 4) / 8388608.0) * (1.0 + 1.0 / 1048576.0) * (1.0 + 1.0 / 8388608.0);
+    static constexpr float kHoldF = (float)kHoldD;
     __device__ __forceinline__ bool holds(unsigned w, float b) const {
         const float y = __fsub_rn(__uint_as_float(w & keep), cum_up);
-        return y > 0.0f && __fmul_rn(b, kHoldF) < __fmul_rn(y, y);
+        return y > 0.0f && __fmul_rn(b, hold_f) < __fmul_rn(y, y);
     }
 
     // screened row: screen, residual, totals (and optionally labels and best)
@@ -567,7 +585,11 @@ struct LowdRow {
         // D64 -- may be misordered.  The index bits move a key by less than 2^(IDXBITS-23) of itself; every
         // key above the second smallest is at least that key less that share, hence slack = 2^(IDXBITS-22)
         // on |m1| + |m2| (a factor two to spare).
-        coef = (float)(((4.0 * D + 2.0) / 16777216.0) * (1.0 + 1.0 / 1024.0) + (double)D / 281474976710656.0);
+        // (The float32 label rule widens the window by rule32_coef(D): see common.cuh.)
+        rule = prep.rule;
+        coef = (float)(((4.0 * D + 2.0) / 16777216.0) * (1.0 + 1.0 / 1024.0) + (double)D / 281474976710656.0 +
+                       (rule ? rule32_coef(D) : 0.0));
+        hold_f = rule ? __double2float_ru(kHoldD * (1.0 + rule32_coef(D))) : kHoldF;
         slack = 1.0f / (float)(1u << (22 - IDXBITS));
         keep = a.key_keep;
         cmax2 = prep.cmax2;

@@ -5,9 +5,11 @@
 //   k_split_centers  once per pass: the same split of the centers (rows padded to the MMA tile), |c|^2/2 and
 //                    max |c| (rounded up)
 //   k_flag_list      the rows assign_tc.cu flagged (label bit 31), listed (staged per CTA in shared memory)
-//   k_decide_cands   their float64 decision (NumPy-pairwise D64 of the two candidate centers, a thread per row
-//                    for d <= 128, a warp per row beyond), lowest index on ties; rows with more candidates:
-//   k_rescore_tc     one CTA per row: a float32 screen of every center, then D64 of each center in its window
+//   k_decide_cands   their decision by the label rule (NumPy-pairwise D64 of the two candidate centers, a thread
+//                    per row for d <= 128, a warp per row beyond; or the float32 direct sum), lowest index on
+//                    ties; rows with more candidates:
+//   k_rescore_tc     one CTA per row: a float32 screen of every center, then the label rule's distance of each
+//                    center in its window
 //   k_fix_labels     per row: the histogram of the labels; the optional labels / best outputs (best: the
 //                    reference's float32 distance, each operation rounded on its own, in column order)
 //   k_scan_labels, k_scatter_rows   the rows grouped by label (a counting sort; the labels in grouped order too)
@@ -162,11 +164,13 @@ __global__ void __launch_bounds__(kSplitThreads) k_decide_cands(const float* __r
                                                                const unsigned int* __restrict__ nlist,
                                                                const int4* __restrict__ cands,
                                                                const int* __restrict__ tc_error,
+                                                               const Prep* __restrict__ prep,
                                                                int32_t* __restrict__ lab) {
     __shared__ __align__(8) unsigned char scratch[kSplitWarps][kD64WarpScratch];
     if (*tc_error) return;
     const int64_t cnt = *nlist;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rule = prep->rule;
     const bool wide = d > 128;
     const int64_t per = wide ? (int64_t)gridDim.x * kSplitWarps : (int64_t)gridDim.x * kSplitThreads;
     const int64_t first = wide ? (int64_t)blockIdx.x * kSplitWarps + warp : (int64_t)blockIdx.x * kSplitThreads + threadIdx.x;
@@ -180,8 +184,10 @@ __global__ void __launch_bounds__(kSplitThreads) k_decide_cands(const float* __r
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             if (cs[i] < 0) continue;
-            const double v = wide ? d64_warp(x, C + (int64_t)cs[i] * d, d, scratch[warp])
-                                  : d64_pairwise(x, C + (int64_t)cs[i] * d, d);
+            // (the float32 label rule's direct sum is sequential: every lane of a wide row computes it alike)
+            const double v = rule ? (double)best32(x, C + (int64_t)cs[i] * d, d)
+                             : wide ? d64_warp(x, C + (int64_t)cs[i] * d, d, scratch[warp])
+                                    : d64_pairwise(x, C + (int64_t)cs[i] * d, d);
             if (v < bv || (v == bv && cs[i] < bi)) { bv = v; bi = cs[i]; }
         }
         if (!wide || lane == 0) lab[row] = bi;
@@ -281,13 +287,15 @@ __global__ void __launch_bounds__(kRescoreThreads) k_rescore_tc(const float* __r
             // a warp per candidate (the list's order does not matter: smallest D64, then lowest index)
             for (int e = warp; e < nc; e += kRescoreThreads / 32) {
                 const int c = cl[e];
-                const double v = d64_warp(xs, C + (int64_t)c * d, d, scratch[warp]);
+                const double v = prep.rule ? (double)best32(xs, C + (int64_t)c * d, d)
+                                           : d64_warp(xs, C + (int64_t)c * d, d, scratch[warp]);
                 if (v < bv || (v == bv && c < bi)) { bv = v; bi = c; }
             }
         } else {
             for (int c = tid; c < k; c += kRescoreThreads) {
                 if (sc[c] > lim) continue;
-                const double v = d64_pairwise(xs, C + (int64_t)c * d, d);
+                const double v = prep.rule ? (double)best32(xs, C + (int64_t)c * d, d)
+                                           : d64_pairwise(xs, C + (int64_t)c * d, d);
                 if (v < bv || (v == bv && c < bi)) { bv = v; bi = c; }
             }
         }
@@ -802,7 +810,7 @@ cudaError_t launch_accum_split(PassArgs a, const RowSplit& rs, const CenterSplit
     k_flag_list<<<(int)fb, kSplitThreads, 0, st>>>(rs.lab, a.n, rs.cands, cs.error, rs.perm, cs.nflag, rs.ovf,
                                                    cs.novf, a.counters);
     k_decide_cands<<<num_sms() * 4, kSplitThreads, 0, st>>>(a.X, a.d, a.C, rs.perm, cs.nflag, rs.cands, cs.error,
-                                                             rs.lab);
+                                                             a.prep, rs.lab);
     k_rescore_tc<<<num_sms() * 8, kRescoreThreads, rsm, st>>>(a.X, a.n, a.d, a.C, cs.ct, a.hc, a.k, a.prep, rs.ovf,
                                                               cs.novf, cs.error, rs.lab, a.counters);
     // each CTA flushes up to k counters: enough rows per CTA that the flush stays small

@@ -16,6 +16,10 @@ from . import core
 class KMeans:
     """Exact k-means on B200 GPUs: every label is the float64-nearest center, lowest index on ties.
 
+    label_rule="float64" (default) labels every row with its float64-nearest center; "float32" reproduces the
+    reference's exact-mode kernels bit for bit (their float32 direct sum, strict < in index order, core.py:263-274).
+    The two differ only on rows whose float32 sums to two centers are within their rounding of each other.
+
     exact=False is accepted for API parity and runs the exact path (the reference ignores it as well below
     its crossover dims; the approximate kernel is not part of this build yet). accumulate="atomic" also runs the
     deterministic accumulation: totals here are exact integers, so there is no faster non-deterministic mode to
@@ -23,7 +27,8 @@ class KMeans:
     """
 
     def __init__(self, n_clusters=8, n_init=1, max_iter=300, tol=1e-4, random_state=None, verbose=False,
-                 spherical=False, accumulate="auto", exact=True, algorithm="lloyd", epochs=3, batch_size=None):
+                 spherical=False, accumulate="auto", exact=True, algorithm="lloyd", epochs=3, batch_size=None,
+                 label_rule="float64"):
         self.n_clusters = n_clusters
         self.n_init = n_init
         self.max_iter = max_iter
@@ -36,6 +41,7 @@ class KMeans:
         self.algorithm = algorithm
         self.epochs = epochs
         self.batch_size = batch_size
+        self.label_rule = label_rule
 
     @property
     def _method(self):
@@ -103,7 +109,7 @@ class KMeans:
         it = 0
         generic = self._method == "generic"
         for it in range(self.max_iter):
-            C_new, s = ds.step(C, generic=generic)
+            C_new, s = ds.step(C, generic=generic, rule=self.label_rule)
             C = C_new.clone()
             inertia = s["inertia"]
             if s["flags"] & 1 or not np.isfinite(inertia):
@@ -135,6 +141,7 @@ class KMeans:
         self._check_algorithm()
         if self.accumulate not in core.ACCUMULATE_METHODS:
             raise ValueError(f"unknown accumulate {self.accumulate!r}")
+        core._check_rule(self.label_rule)
         ds = self._parts(X)
         rows = ds.n_total
         if rows < self.n_clusters:
@@ -145,7 +152,7 @@ class KMeans:
             C, inertia, iters = self._one_run(ds, rows, seed)
             # the last step's inertia belongs to the centers it started from; one more pass scores the returned ones
             # (estimator.py:201-204)
-            _, _, inertia, labels = ds.assign(C, return_labels=True)
+            _, _, inertia, labels = ds.assign(C, return_labels=True, rule=self.label_rule)
             if self.verbose and self.n_init > 1:
                 print(f"start {run + 1}/{self.n_init}: inertia {inertia:.6e} after {iters} iterations")
             if best is None or inertia < best[1]:
@@ -160,7 +167,7 @@ class KMeans:
             raise ValueError(f"X has {ds.d} features but this model was fitted with "
                              f"{self.cluster_centers_.shape[1]}")
         C = torch.from_numpy(np.ascontiguousarray(self.cluster_centers_, dtype=np.float32)).to(ds.device)
-        _, _, inertia, labels = ds.assign(C, return_labels=True)
+        _, _, inertia, labels = ds.assign(C, return_labels=True, rule=self.label_rule)
         if not np.isfinite(inertia):
             self._explain_nonfinite(ds)
         return labels

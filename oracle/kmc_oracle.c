@@ -13,6 +13,11 @@
  *     NumPy in tests/test_oracle.py.
  *   - kmo_assign: label = argmin of kmo_d64 over centers, lowest index on exact ties
  *     (tests/accuracy.py:48-49, core.py:218-219 "lowest index on ties").
+ *   - kmo_assign_rule(rule = 1): the reference's exact-mode label rule itself, its rows kernel
+ *     (core.py:263-274, contract at core.py:218-219): for each center in index order the float32 direct
+ *     sum s = s + (x_j - c_j)^2 (kmo_best32: each subtraction, square and add rounded on its own), and
+ *     the center is taken when s < best (strict: lowest index on ties).  Pinned against a NumPy
+ *     restatement of that loop (tests/golden/make_golden.py: rows_kernel_labels).
  *   - kmo_best32: the per-row float32 distance to the assigned center that the reference keeps as
  *     `best` (core.py:248-257: s += (x_j - c_j)^2 in order), here with the square and the add rounded
  *     separately (no fused multiply-add), so the CUDA kernels can reproduce it bit for bit.
@@ -91,39 +96,55 @@ typedef struct {
     int64_t *labels;
     double *d64;
     float *best32;
+    int rule;
 } assign_job;
 
 static void *assign_worker(void *p) {
     assign_job *j = (assign_job *)p;
     for (int64_t i = j->r0; i < j->r1; i++) {
         const float *x = j->X + i * (int64_t)j->d;
-        double bd = INFINITY;
         int64_t bl = 0;
-        for (int c = 0; c < j->k; c++) {
-            double v = kmo_d64(x, j->C + (int64_t)c * j->d, j->d);
-            if (v < bd) { bd = v; bl = c; }      /* strict <: lowest index on ties */
+        if (j->rule == 1) {
+            float bs = INFINITY;
+            for (int c = 0; c < j->k; c++) {
+                float s = kmo_best32(x, j->C + (int64_t)c * j->d, j->d);
+                if (s < bs) { bs = s; bl = c; }      /* strict <: lowest index on ties */
+            }
+        } else {
+            double bd = INFINITY;
+            for (int c = 0; c < j->k; c++) {
+                double v = kmo_d64(x, j->C + (int64_t)c * j->d, j->d);
+                if (v < bd) { bd = v; bl = c; }      /* strict <: lowest index on ties */
+            }
         }
         if (j->labels) j->labels[i] = bl;
-        if (j->d64) j->d64[i] = bd;
+        if (j->d64) j->d64[i] = kmo_d64(x, j->C + bl * (int64_t)j->d, j->d);
         if (j->best32) j->best32[i] = kmo_best32(x, j->C + bl * (int64_t)j->d, j->d);
     }
     return NULL;
 }
 
-void kmo_assign(const float *X, int64_t n, int d, const float *C, int k, int64_t *labels, double *d64,
-                float *best32, int nthreads) {
+/* rule 0: the float64 distance (tests/accuracy.py:31-51); rule 1: the float32 direct sum (core.py:263-274).
+ * d64 (optional) receives each row's float64 distance to its label, best32 (optional) its float32 one. */
+void kmo_assign_rule(const float *X, int64_t n, int d, const float *C, int k, int64_t *labels, double *d64,
+                     float *best32, int nthreads, int rule) {
     if (nthreads < 1) nthreads = 1;
     if (nthreads > 256) nthreads = 256;
     if (n < 4096) nthreads = 1;
     pthread_t th[256];
     assign_job jobs[256];
     for (int t = 0; t < nthreads; t++) {
-        jobs[t] = (assign_job){X, C, n * t / nthreads, n * (t + 1) / nthreads, d, k, labels, d64, best32};
+        jobs[t] = (assign_job){X, C, n * t / nthreads, n * (t + 1) / nthreads, d, k, labels, d64, best32, rule};
         if (nthreads > 1) pthread_create(&th[t], NULL, assign_worker, &jobs[t]);
         else assign_worker(&jobs[t]);
     }
     if (nthreads > 1)
         for (int t = 0; t < nthreads; t++) pthread_join(th[t], NULL);
+}
+
+void kmo_assign(const float *X, int64_t n, int d, const float *C, int k, int64_t *labels, double *d64,
+                float *best32, int nthreads) {
+    kmo_assign_rule(X, n, d, C, k, labels, d64, best32, nthreads, 0);
 }
 
 /* ------------------------------------------------------------------ Lloyd step */

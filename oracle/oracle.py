@@ -39,6 +39,9 @@ def lib():
         L.kmo_assign.restype = None
         L.kmo_assign.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int, _f32p, ctypes.c_int, _i64p, _f64p, _f32p,
                                  ctypes.c_int]
+        L.kmo_assign_rule.restype = None
+        L.kmo_assign_rule.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int, _f32p, ctypes.c_int, _i64p, _f64p,
+                                      _f32p, ctypes.c_int, ctypes.c_int]
         L.kmo_finish.restype = ctypes.c_int
         L.kmo_finish.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int, _f32p, ctypes.c_int, _i64p, _f32p, _f32p,
                                  ctypes.POINTER(ctypes.c_double), _i64p]
@@ -57,10 +60,14 @@ def _threads():
     return max(1, min(64, os.cpu_count() or 1))
 
 
-def assign(X, C, threads=None):
-    """Exact labels (float64 argmin, lowest index on ties; tests/accuracy.py:31-51), their float64 distance
-    and the float32 `best` distance (core.py:248-257, square and add rounded separately).
-    -> (labels int64, d64 float64, best32 float32)."""
+RULES = {"float64": 0, "float32": 1}
+
+
+def assign(X, C, threads=None, rule="float64"):
+    """Exact labels and each row's float64 distance and float32 `best` distance (core.py:248-257, square and add
+    rounded separately) to its label.  rule "float64": argmin of the float64 distance, lowest index on ties
+    (tests/accuracy.py:31-51); rule "float32": the reference's rows kernel (core.py:263-274), argmin of the float32
+    direct sum with strict < in index order.  -> (labels int64, d64 float64, best32 float32)."""
     X = np.ascontiguousarray(X, np.float32)
     C = np.ascontiguousarray(C, np.float32)
     n, d = X.shape
@@ -68,17 +75,17 @@ def assign(X, C, threads=None):
     labels = np.empty(n, np.int64)
     d64 = np.empty(n, np.float64)
     best = np.empty(n, np.float32)
-    lib().kmo_assign(X, n, d, C, k, labels, d64, best, threads or _threads())
+    lib().kmo_assign_rule(X, n, d, C, k, labels, d64, best, threads or _threads(), RULES[rule])
     return labels, d64, best
 
 
-def lloyd_step(X, C, labels=None, best=None):
-    """core.py:2209-2242 on the oracle's exact labels.
+def lloyd_step(X, C, labels=None, best=None, rule="float64"):
+    """core.py:2209-2242 on the oracle's exact labels (of the given label rule).
     -> (C_new float32, inertia float, n_empty int, relocations [(cluster, row)], labels, best32)."""
     X = np.ascontiguousarray(X, np.float32)
     C = np.ascontiguousarray(C, np.float32)
     if labels is None or best is None:
-        labels, _, best = assign(X, C)
+        labels, _, best = assign(X, C, rule=rule)
     labels = np.ascontiguousarray(labels, np.int64)
     best = np.ascontiguousarray(best, np.float32)
     n, d = X.shape

@@ -32,6 +32,25 @@ def _load_reference():
     return acc, core
 
 
+def rows_kernel_labels(X, C):
+    """NumPy restatement of the reference's exact-mode label rule, its rows kernel (mlx_kmeans/core.py:263-274,
+    a Metal kernel that cannot run here): for each center in index order s = s + t * t with t = x_j - c_j over
+    the columns in order, every operation a float32 operation rounded on its own (NumPy does not fuse the
+    multiply and add), and the center is taken when s < best. -> (labels int64, best float32)."""
+    n, d = X.shape
+    best = np.full(n, np.inf, np.float32)
+    lab = np.zeros(n, np.int64)
+    for c in range(len(C)):
+        s = np.zeros(n, np.float32)
+        for j in range(d):
+            t = X[:, j] - C[c, j]
+            s = s + t * t
+        lt = s < best
+        best = np.where(lt, s, best)
+        lab = np.where(lt, c, lab)
+    return lab, best
+
+
 def blobs(rng, n, d, true_k, spread, noise):
     centers = rng.uniform(-spread, spread, size=(true_k, d))
     return (centers[rng.integers(0, true_k, n)] + rng.normal(0, noise, (n, d))).astype(np.float32)
@@ -87,6 +106,13 @@ def cases(rng):
     X = blobs(rng, 2000, 4, 4, 10, 1)
     C = np.concatenate([X[rng.choice(len(X), 12, replace=False)], rng.uniform(900, 1000, (4, 4)).astype(np.float32)])
     out.append(("relocation_4empty_d4_k16", X, C, True))
+    # the two label rules apart: rows far from every center (float32 sums of ~2^20 lose the last bits that
+    # separate the centers) around pairs of centers a few float32 ulps apart
+    X = (blobs(rng, 3000, 16, 8, 1, 0.5) + 1000).astype(np.float32)
+    C = X[rng.choice(len(X), 8, replace=False)].copy()
+    C = np.concatenate([C, C + np.float32(2.0 ** -15) * rng.standard_normal(C.shape).astype(np.float32)])
+    C = (C - 1000).astype(np.float32)
+    out.append(("rules_apart_d16_k16", X, C, False))
     return out
 
 
@@ -99,14 +125,17 @@ def main():
         C = np.ascontiguousarray(C, np.float32)
         labels, best_d = acc.reference(X, C)
         sums_np, counts_np, inertia_np = core.assign_numpy([X], C)
+        labels32, best32 = rows_kernel_labels(X, C)
         rec = dict(X=X, C=C, labels=labels.astype(np.int64), best_d=best_d.astype(np.float64),
-                   np_sums=sums_np, np_counts=counts_np, np_inertia=np.float64(inertia_np))
+                   np_sums=sums_np, np_counts=counts_np, np_inertia=np.float64(inertia_np),
+                   labels32=labels32, best32=best32)
         if reloc:
             C_new, n_empty = acc.reference_lloyd_step(X, C, labels)
             rec.update(C_new=C_new.astype(np.float64), n_empty=np.int64(n_empty))
         np.savez_compressed(os.path.join(OUT, f"{name}.npz"), **rec)
         index.append(name)
-        print(f"{name:32s} n={len(X):6d} d={X.shape[1]:4d} k={len(C):4d}")
+        print(f"{name:32s} n={len(X):6d} d={X.shape[1]:4d} k={len(C):4d}  "
+              f"rows whose float32-rule label differs: {int((labels32 != labels).sum())}")
     with open(os.path.join(OUT, "INDEX.txt"), "w") as f:
         f.write("\n".join(index) + "\n")
 

@@ -52,6 +52,29 @@ def test_tensor_core_configs_match_oracle(cfg, n, k, cuda_device):
     assert abs(inertia - in_ref) <= 1e-6 * in_ref
 
 
+@pytest.mark.parametrize("cfg,n,k", [(3, 2_000_000, 16), (2, 200_000, 64), (4, 20_000, 1024), (5, 20_000, 4096)])
+def test_both_label_rules_at_config_shapes(cfg, n, k, cuda_device):
+    """Each label rule bit-exact to its oracle on a slice of the configuration; the rows where the rules
+    disagree are counted (printed: -s)."""
+    import torch
+    import mlx_kmeans_b200 as km
+    X = _slice(cfg, n, cuda_device)
+    Xh = X.cpu().numpy()
+    rng = np.random.default_rng(cfg + 10)
+    C = Xh[rng.choice(n, k, replace=False)].copy()
+    C += (0.01 * rng.standard_normal(C.shape) * np.abs(Xh).mean()).astype(np.float32)
+    ds = km.Dataset([X])
+    Ct = torch.from_numpy(C).to(cuda_device)
+    got = {}
+    for rule in ("float64", "float32"):
+        ref, _, _ = O.assign(Xh, C, rule=rule)
+        lab = ds.assign(Ct, return_labels=True, rule=rule)[3]
+        assert np.array_equal(lab, ref), f"{rule}: {int((lab != ref).sum())} labels differ"
+        got[rule] = lab
+    print(f"config {cfg} slice {n} x {Xh.shape[1]}, k={k}: rows labelled differently by the two rules: "
+          f"{int((got['float64'] != got['float32']).sum())}")
+
+
 def test_config1_recipe_step_by_step(cuda_device):
     """Configuration 1 as specified: make_data_numpy(100k, 8, k_true=8, seed 0), k-means++ on a 16k-row sample,
     20 exact Lloyd steps; each step's labels, centers, inertia and empties against the oracle's step."""

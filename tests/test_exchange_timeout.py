@@ -54,6 +54,7 @@ def test_sharded_step_raises_when_a_peer_never_arrives(cuda_device, monkeypatch)
     L, lib, own, peer, peers, X = _setup(cuda_device)
     import mlx_kmeans_b200 as km
     ds = km.Dataset([torch.from_numpy(X).to(cuda_device)])
+    ds.colmax                                            # (the column maxima of this one-GPU Dataset, computed now)
     # a sharded Dataset's exchange state, with the stand-in peer: the step takes the fused exchange + finish
     ds.group, ds.world, ds.rank = object(), 2, 0
     ds._xch[K] = dict(dev=peers, step=0)

@@ -121,3 +121,28 @@ def test_pp_init_spreads_over_clusters():
     seeds = rng.integers(2**63 - 1, size=7).astype(np.uint64)
     picks, _ = O.pp_init(S, 8, 0, seeds)
     assert len(set(lab[picks].tolist())) == 8
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_float32_rule_matches_the_rows_kernel_restatement(name):
+    """The oracle's float32 label rule against the NumPy restatement of the reference's rows kernel
+    (core.py:263-274) recorded in the fixtures: labels and the float32 distances bit-exact."""
+    g = load_golden(name)
+    labels, _, best = O.assign(g["X"], g["C"], rule="float32")
+    assert np.array_equal(labels, g["labels32"])
+    assert np.array_equal(best.view(np.uint32), g["best32"].view(np.uint32))
+
+
+def test_the_label_rules_disagree_only_inside_the_float32_rounding():
+    """Where the two rules pick different centers, the float32 direct sums of both centers are within the sum's
+    relative error bound gamma_{d+2} of each other (and the float64 distances differ by at most that too)."""
+    g = load_golden("rules_apart_d16_k16")
+    X, C = g["X"], g["C"]
+    l64, l32 = g["labels"], g["labels32"]
+    diff = np.nonzero(l64 != l32)[0]
+    assert len(diff) > 0
+    d = X.shape[1]
+    gam = (d + 2) * 2.0 ** -24 / (1 - (d + 2) * 2.0 ** -24)
+    for i in diff:
+        a, b = O.d64(X[i], C[l64[i]]), O.d64(X[i], C[l32[i]])
+        assert a <= b <= a * (1 + gam) / (1 - gam)

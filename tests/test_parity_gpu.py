@@ -33,7 +33,7 @@ def _ds(X, device, parts=1):
     return km.Dataset([Xt[a:b].contiguous() for a, b in zip(cuts[:-1], cuts[1:])])
 
 
-def _check_assign(X, C, out, labels_ref):
+def _check_assign(X, C, out, labels_ref, rule="float64"):
     sums, counts, inertia, labels = out
     assert np.array_equal(labels, labels_ref), f"{int((labels != labels_ref).sum())} labels differ"
     k, d = C.shape
@@ -44,9 +44,63 @@ def _check_assign(X, C, out, labels_ref):
     rms = float(np.sqrt((X.astype(np.float64) ** 2).mean())) or 1.0
     err = np.abs(sums - ref_sums) / (rms * np.maximum(ref_counts, 1)[:, None])
     assert err.max() <= 1e-7
-    _, _, best = O.assign(X, C)
+    _, _, best = O.assign(X, C, rule=rule)
     ref_inertia = float(best.astype(np.float64).sum())
     assert abs(inertia - ref_inertia) <= 1e-6 * max(ref_inertia, 1e-30)
+
+
+@pytest.mark.parametrize("name", CASES)
+@pytest.mark.parametrize("path", ["auto", "generic", "tensor_cores"])
+def test_float32_rule_matches_golden(name, path, cuda_device):
+    """label_rule="float32" (the reference's rows kernel, core.py:263-274) on every path: labels bit-exact to the
+    NumPy restatement recorded in the fixtures (and so to the oracle's float32 rule)."""
+    g = load_golden(name)
+    ds = _ds(g["X"], cuda_device)
+    if path == "tensor_cores":
+        ds.tensor_cores = True
+    C = _torch().from_numpy(g["C"]).to(cuda_device)
+    out = ds.assign(C, return_labels=True, generic=(path == "generic"), rule="float32")
+    _check_assign(g["X"], g["C"], out, g["labels32"], rule="float32")
+
+
+def _rules_apart_lowd(n, d, k, seed):
+    """Low-d rows far from their centers, around pairs of centers a few float32 ulps apart: the float32 direct
+    sum and the float64 distance pick different centers for a share of the rows."""
+    rng = np.random.default_rng(seed)
+    X = (rng.uniform(-1, 1, (k // 2, d))[rng.integers(0, k // 2, n)] + 0.3 * rng.standard_normal((n, d)) + 600)
+    X = X.astype(np.float32)
+    C = X[rng.choice(n, k // 2, replace=False)] - np.float32(600)
+    C = np.concatenate([C, C + np.float32(2.0 ** -14) * rng.standard_normal(C.shape).astype(np.float32)])
+    return X, C.astype(np.float32)
+
+
+@pytest.mark.parametrize("d,k", [(4, 16), (2, 32), (8, 8), (3, 6)])
+def test_float32_rule_low_d_fused_bounded_generic(d, k, cuda_device):
+    """The fused low-d kernel, the bounded pass (after a step whose bounds are then used) and the generic kernel
+    under the float32 rule against the oracle's, on data where the two rules disagree."""
+    import mlx_kmeans_b200 as km
+    torch = _torch()
+    X, C = _rules_apart_lowd(60_000, d, k, d * 100 + k)
+    l64, _, _ = O.assign(X, C)
+    l32, _, _ = O.assign(X, C, rule="float32")
+    assert (l64 != l32).sum() > 0
+    ds = _ds(X, cuda_device)
+    Ct = torch.from_numpy(C).to(cuda_device)
+    for generic in (False, True):
+        out = ds.assign(Ct, return_labels=True, generic=generic, rule="float32")
+        _check_assign(X, C, out, l32, rule="float32")
+    # bounded steps: the first writes the bounds, the second (same centers, zero drift) keeps labels by them
+    bd = _ds(X, cuda_device)
+    bd.label_rule = "float32"
+    for _ in range(2):
+        bd.step(Ct, bounded=True)
+    assert np.array_equal(_word_labels(bd, k), l32)
+    C_ref, in_ref, ne_ref, _, _, _ = O.lloyd_step(X, C, rule="float32")
+    C_new, inertia, n_empty = km.lloyd_step(bd, C, label_rule="float32")
+    rms = float(np.sqrt((X.astype(np.float64) ** 2).mean()))
+    assert n_empty == ne_ref
+    assert np.max(np.abs(C_new.astype(np.float64) - C_ref)) / rms <= 1e-6
+    assert abs(inertia - in_ref) <= 1e-6 * in_ref
 
 
 @pytest.mark.parametrize("name", CASES)
