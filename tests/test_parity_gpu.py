@@ -64,14 +64,15 @@ def test_float32_rule_matches_golden(name, path, cuda_device):
 
 
 def _rules_apart_lowd(n, d, k, seed):
-    """Low-d rows far from their centers, around pairs of centers a few float32 ulps apart: the float32 direct
-    sum and the float64 distance pick different centers for a share of the rows."""
+    """Low-d rows around pairs of centers a few float32 ulps apart: the two centers' distances differ by about
+    their float32 rounding, so the float32 direct sum and the float64 distance pick different centers for a
+    share of the rows."""
     rng = np.random.default_rng(seed)
-    X = (rng.uniform(-1, 1, (k // 2, d))[rng.integers(0, k // 2, n)] + 0.3 * rng.standard_normal((n, d)) + 600)
-    X = X.astype(np.float32)
-    C = X[rng.choice(n, k // 2, replace=False)] - np.float32(600)
-    C = np.concatenate([C, C + np.float32(2.0 ** -14) * rng.standard_normal(C.shape).astype(np.float32)])
-    return X, C.astype(np.float32)
+    base = rng.uniform(-4, 4, (k // 2, d)).astype(np.float32)
+    step = (rng.integers(1, 4, base.shape) * np.where(rng.random(base.shape) < 0.5, -1, 1)).astype(np.float32)
+    C = np.concatenate([base, base + step * np.spacing(base)]).astype(np.float32)
+    X = (base[rng.integers(0, k // 2, n)] + 0.5 * rng.standard_normal((n, d))).astype(np.float32)
+    return X, C
 
 
 @pytest.mark.parametrize("d,k", [(4, 16), (2, 32), (8, 8), (3, 6)])
