@@ -392,9 +392,10 @@ struct BoundSmem {
     static constexpr size_t packed = (size_t)Packed<D, K>::kWords * 8;
     static constexpr size_t acc = (size_t)K * (D + 2) * 8;
     static constexpr size_t queue = (size_t)kWarps * kQueue * 4;
-    static constexpr size_t total = sums + cnts + centers + packed + acc + queue;
-    static_assert(sums % 16 == 0 && cnts % 16 == 0 && centers % 16 == 0 && packed % 8 == 0 && acc % 8 == 0,
-                  "shared carve alignment");
+    static constexpr size_t qrows = (size_t)kWarps * kQueue * D * 4;   // the queued rows' values
+    static constexpr size_t total = sums + cnts + centers + packed + acc + queue + qrows;
+    static_assert(sums % 16 == 0 && cnts % 16 == 0 && centers % 16 == 0 && packed % 8 == 0 && acc % 8 == 0 &&
+                  queue % 16 == 0, "shared carve alignment");
 };
 
 // Per-thread state of the row loop.  Counts are packed four 8-bit fields to a word: a lane adds at most
@@ -834,7 +835,8 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
     float* cs = reinterpret_cast<float*>(smem + off);              off += L::centers;
     unsigned long long* pks = reinterpret_cast<unsigned long long*>(smem + off);   off += L::packed;
     long long* acc = reinterpret_cast<long long*>(smem + off);     off += L::acc;
-    int* queue_all = reinterpret_cast<int*>(smem + off);
+    int* queue_all = reinterpret_cast<int*>(smem + off);           off += L::queue;
+    float* qrows_all = reinterpret_cast<float*>(smem + off);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int k = a.k;
@@ -897,7 +899,10 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
     if constexpr (PK) lds_row2<D>(cr2, st.cs_s + (wq[0] & MASK) * (unsigned)(D * 4));
     else load_row<D>(cr, st.cs_s + (wq[0] & MASK) * (unsigned)(D * 4));
 
+    // failing rows queue per warp: the row's offset in the block and its values (taken from the registers it was
+    // streamed into, so a flush reads shared memory only)
     int* queue = queue_all + warp * kQueue;
+    const unsigned qrows_s = (unsigned)__cvta_generic_to_shared(qrows_all + (size_t)warp * kQueue * D);
     int qhead = 0, qcount = 0;
 
     for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
@@ -908,11 +913,13 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
 
         // screen `cnt` queued rows, one per lane
         auto flush = [&](int cnt) {
+            __syncwarp();                          // the queue entries other lanes stored are visible
             const bool v = lane < cnt;
-            const int qoff = v ? queue[(qhead + lane) & (kQueue - 1)] : 0;
+            const int slot = (qhead + lane) & (kQueue - 1);
+            const int qoff = v ? queue[slot] : 0;
             const int64_t row = blk0 + qoff;
             float x[D];
-            if (v) ldg_row<D>(x, a.X + row * D);
+            if (v) load_row<D>(x, qrows_s + (unsigned)(slot * D * 4));
             else {
 #pragma unroll
                 for (int j = 0; j < D; j++) x[j] = 0.0f;
@@ -927,6 +934,7 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
             st.screened += v ? 1 : 0;
             qhead = (qhead + cnt) & (kQueue - 1);
             qcount -= cnt;
+            __syncwarp();                          // every lane has read its entry before the slots are reused
         };
 
         const float* xblk = a.X + base * D;
@@ -990,7 +998,13 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
                     const unsigned fm = __ballot_sync(0xffffffffu, valid && !keep);
                     if (fm) {
                         const int pos = __popc(fm & ((1u << lane) - 1u));
-                        if ((fm >> lane) & 1u) queue[(qhead + qcount + pos) & (kQueue - 1)] = rofs;
+                        if ((fm >> lane) & 1u) {
+                            const int slot = (qhead + qcount + pos) & (kQueue - 1);
+                            queue[slot] = rofs;
+                            const unsigned qa = qrows_s + (unsigned)(slot * D * 4);
+                            if constexpr (PK) sts_row2<D>(qa, xq2[q]);
+                            else store_row<D>(qa, xq[q]);
+                        }
                         qcount += __popc(fm);
                         if (qcount >= 32) flush(32);
                     }
