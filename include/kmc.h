@@ -49,6 +49,11 @@ enum kmc_status {
  * index order (lowest index on ties).  Without it the label is the float64-optimal center (the numeric contract
  * below).  The two differ only where the float32 sums of two centers are within their rounding of each other. */
 #define KMC_PASS_LABEL32 4u
+/* exact=False (the reference's approximate assignment, core.py:859-1088 and 2036-2060), kmc_pass_split only:
+ * x.c from one bf16 MMA per product (x and c rounded to bf16, float32 accumulation) and the smallest score's
+ * center taken with no error window, so a row whose two best centers are within the bf16 rounding may get the
+ * second.  Counts, sums and inertia are still exact for the labels given (read from the float32 rows). */
+#define KMC_PASS_APPROX 8u
 
 /* Device statistics of one Lloyd step, as kmc_finish leaves them (layout fixed, 64 bytes). */
 typedef struct kmc_stats {
@@ -200,6 +205,33 @@ int kmc_far_rows(const float *X, int64_t n, int d, const int32_t *labels, const 
  * Replaces core.py:2223-2241. */
 int kmc_finish(int64_t *totals, int k, int d, const uint32_t *cands, int64_t cand_rows, int ranks, float *C_new,
                kmc_stats *stats, void *workspace, size_t ws_bytes, void *stream);
+
+/* ---------------------------------------------------------------- Lloyd loop on the device
+ * Replaces the loop of estimator.py:132-150 (`_one_run`: step, then stop once |prev - inertia| <= tol * prev)
+ * with no host round trip per step.  The loop's record (kmc_loop, device, 64 bytes) holds the stopping rule's
+ * state; kmc_loop_init sets it.  kmc_lloyd enqueues `steps` Lloyd steps (kmc_pass or kmc_pass_bounded when
+ * `bounds` is given, then kmc_finish) on one slice, reading the centers from C0 and C1 in turn (step i reads
+ * C_{i % 2} and writes C_{(i + 1) % 2}); after each step the finish applies the stopping rule, and once the loop
+ * has stopped the kernels of the steps still queued return at once.  One kmc_stats_read-style copy of the record
+ * at the end says how it stopped: converged, max_steps reached, non-finite (flags), or a step that emptied
+ * clusters (kmc_finish without candidates leaves its centers unwritten): the caller then relocates that step with
+ * kmc_far_rows + kmc_finish, continues the record with kmc_loop_init(steps_done + 1, that step's inertia) and
+ * calls kmc_lloyd again.  Single GPU, one slice; shapes on the tensor-core pass use the step-by-step calls.
+ * The final centers are in C_{steps % 2} of the record's `steps` counted from this call's start. */
+typedef struct kmc_loop {
+    double prev_inertia;   /* inertia of the last step run */
+    double tol;
+    int64_t steps;         /* steps completed */
+    int64_t max_steps;
+    int64_t state;         /* 0 running, 1 converged, 2 a step needs relocation, 3 non-finite, 4 max_steps ran */
+    int64_t have_prev;
+    int64_t reserved[2];
+} kmc_loop;
+int kmc_loop_init(kmc_loop *loop, double tol, int64_t max_steps, int64_t steps_done, double prev_inertia,
+                  int have_prev, void *stream);
+int kmc_lloyd(const float *X, int64_t n, int d, float *C0, float *C1, int k, const uint32_t *colmax, int64_t n_total,
+              int64_t *totals, unsigned flags, void *bounds, size_t bounds_size, kmc_stats *stats, kmc_loop *loop,
+              int steps, void *workspace, size_t ws_bytes, void *stream);
 
 /* Copy the device statistics to the host and wait for them (the one synchronising call). */
 int kmc_stats_read(const kmc_stats *stats_dev, kmc_stats *stats_host, void *stream);

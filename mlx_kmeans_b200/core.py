@@ -83,6 +83,7 @@ class Dataset:
     """
 
     TC_MIN_DIMS = 32                # from here up the assign runs on the tensor cores (kmc_pass_split)
+    APPROX_MIN_DIMS = 64            # exact=False from here up (core.py:1030-1034 / 2036-2041: below, exact is as fast)
 
     def __init__(self, parts, group=None, device=None, tensor_cores=None, label_rule="float64"):
         if isinstance(parts, (torch.Tensor, np.ndarray)) or not isinstance(parts, (list, tuple)):
@@ -266,10 +267,16 @@ class Dataset:
             dist.all_reduce(b["totals"], op=dist.ReduceOp.SUM, group=self.group)
 
     # -- one pass
-    def run_pass(self, C, labels=False, generic=False, bounded=False, reduce=True, rule=None):
+    def uses_approx(self, approx):
+        """Whether an exact=False pass takes the approximate kernel here (tensor-core shapes from
+        APPROX_MIN_DIMS dims up; elsewhere it runs exactly, as the reference does below its crossover)."""
+        return bool(approx) and self.tensor_cores and self.d >= self.APPROX_MIN_DIMS
+
+    def run_pass(self, C, labels=False, generic=False, bounded=False, reduce=True, rule=None, approx=False):
         """kmc_pass over every local slice, then (reduce) the all-reduce of the totals. C: (k, d) float32 CUDA.
         bounded: use and refresh the per-row bounds (kmc_pass_bounded; no labels). rule: the label rule ("float64"
-        or "float32"; None: the Dataset's)."""
+        or "float32"; None: the Dataset's). approx: exact=False (one bf16 product per score, no window) where
+        uses_approx allows it."""
         k = C.shape[0]
         b = self.buffers(k)
         lab, bst = self._label_buffers(b) if labels else (None, None)
@@ -277,6 +284,8 @@ class Dataset:
         flags = _lib.KMC_PASS_GENERIC if generic else 0
         if _check_rule(rule or self.label_rule) == "float32":
             flags |= _lib.KMC_PASS_LABEL32
+        if not generic and self.uses_approx(approx):
+            flags |= _lib.KMC_PASS_APPROX
         st = _stream()
         bb = self.bounds(k) if bounded and not labels and not generic else None
         tc = self.tensor_cores and not generic
@@ -306,15 +315,15 @@ class Dataset:
         return dict(inertia=float(host[:1].view(np.float64)[0]), n_empty=int(host[1]), n_relocated=int(host[2]),
                     needs_reloc=int(host[3]), flags=int(host[4]), rescored=int(host[5]), screened=int(host[6]))
 
-    def step(self, C, generic=False, bounded=True, rule=None):
+    def step(self, C, generic=False, bounded=True, rule=None, approx=False):
         """One Lloyd iteration on the device: C (k, d) CUDA -> (C_new CUDA tensor (a buffer reused by the
         next step with the same k; copy it to keep it), stats dict).  bounded: keep per-row bounds between
         steps so rows whose label cannot have changed skip the comparison with every center (the labels are
         those of a full pass; the totals agree to the float32 rounding of the per-lane partial sums).  rule: the
-        label rule (None: the Dataset's)."""
+        label rule (None: the Dataset's). approx: exact=False (see run_pass)."""
         k = C.shape[0]
         x = self._exchange(k) if self.group is not None else False
-        b = self.run_pass(C, generic=generic, bounded=bounded, reduce=not x, rule=rule)
+        b = self.run_pass(C, generic=generic, bounded=bounded, reduce=not x, rule=rule, approx=approx)
         if x:
             # the all-reduce over peer memory and the finish in one launch
             _lib.call("kmc_exchange_finish", _ptr(b["totals"]), k, self.d, _ptr(x["dev"]), self.world, self.rank,
@@ -327,14 +336,66 @@ class Dataset:
         if s["flags"] & 2:
             raise RuntimeError("the all-reduce of the totals timed out waiting for a peer GPU")
         if s["needs_reloc"]:
-            s = self._relocate(C, b, s["n_empty"], generic, rule)
+            s = self._relocate(C, b, s["n_empty"], generic, rule, approx)
         return b["C_new"], s
 
-    def _relocate(self, C, b, n_empty, generic, rule=None):
+    def device_loop_ok(self, generic=False):
+        """Whether a fit can run its Lloyd loop on the device (kmc_lloyd): one GPU, one slice, the CUDA-core
+        pass (the tensor-core pass runs step by step)."""
+        return self.group is None and len(self.parts) == 1 and (generic or not self.tensor_cores)
+
+    def lloyd_loop(self, C, max_iter, tol, generic=False, bounded=True, rule=None):
+        """Up to max_iter Lloyd steps from C (k, d) CUDA, stopping as the reference's estimator does
+        (estimator.py:132-150: once |prev - inertia| <= tol * prev), with the loop on the device (kmc_lloyd): the
+        host reads the loop's record once at the end, and once per step that empties clusters (that step is
+        relocated here, as Dataset.step does, and the loop resumes).  -> (centers (k, d) CUDA tensor, inertia of the
+        last step, steps run, flags of the last step)."""
+        L = _lib.load()
+        k = C.shape[0]
+        b = self.buffers(k)
+        if "loop" not in b:
+            b["loop"] = torch.zeros(64, dtype=torch.uint8, device=self.device)
+        loop = b["loop"]
+        p = self.parts[0]
+        cm = self.colmax
+        flags = _lib.KMC_PASS_GENERIC if generic else 0
+        if _check_rule(rule or self.label_rule) == "float32":
+            flags |= _lib.KMC_PASS_LABEL32
+        bb, bbytes = self.bounds(k)[0] if bounded and not generic else (None, 0)
+        bufs = [C.clone(), torch.empty_like(C)]
+        cur = 0                                        # the buffer holding the current centers
+        st = _stream()
+        done, prev, have = 0, 0.0, 0
+        while True:
+            _lib.call("kmc_loop_init", _ptr(loop), float(tol), int(max_iter), done, prev, have, st)
+            _lib.call("kmc_lloyd", _ptr(p), p.shape[0], self.d, _ptr(bufs[cur]), _ptr(bufs[1 - cur]), k, _ptr(cm),
+                      self.n_total, _ptr(b["totals"]), flags, _ptr(bb), bbytes, _ptr(b["stats"]), _ptr(loop),
+                      int(max_iter - done), _ptr(b["ws"]), b["wsb"], st)
+            rec = loop.cpu().numpy()                   # the one synchronising read of this segment
+            ran = int(rec[16:24].view(np.int64)[0]) - done
+            state = int(rec[32:40].view(np.int64)[0])
+            cur = (cur + ran) % 2
+            done += ran
+            prev = float(rec[0:8].view(np.float64)[0])
+            have = int(rec[40:48].view(np.int64)[0])
+            if state != 2:                             # converged, max_iter, or non-finite: the last step's stats
+                stats = self.read_stats(b)
+                return bufs[cur], stats["inertia"], done, stats["flags"]
+            # a step emptied clusters: relocate it on the host, then apply the stopping rule to it
+            s = self._relocate(bufs[cur], b, self.read_stats(b)["n_empty"], generic, rule)
+            done += 1
+            inertia = s["inertia"]
+            bufs[1 - cur].copy_(b["C_new"])
+            cur = 1 - cur
+            if s["flags"] & 1 or (have and abs(prev - inertia) <= tol * prev) or done >= max_iter:
+                return bufs[cur], inertia, done, s["flags"]
+            prev, have = inertia, 1
+
+    def _relocate(self, C, b, n_empty, generic, rule=None, approx=False):
         """Empty clusters: recompute the pass with labels and best, gather the farthest rows of every slice
         and rank, and finish again with them (core.py:2224-2236)."""
         k = C.shape[0]
-        b = self.run_pass(C, labels=True, generic=generic, rule=rule)
+        b = self.run_pass(C, labels=True, generic=generic, rule=rule, approx=approx)
         E = int(n_empty)
         R = self.d + 4
         fwb = int(_lib.load().kmc_far_workspace_bytes(E))
@@ -357,10 +418,10 @@ class Dataset:
                   _ptr(b["stats"]), _ptr(b["ws"]), b["wsb"], _stream())
         return self.read_stats(b)
 
-    def assign(self, C, return_labels=False, generic=False, rule=None):
+    def assign(self, C, return_labels=False, generic=False, rule=None, approx=False):
         """One pass -> (sums float64 (k, d), counts int64 (k), inertia float[, labels int64 (n_local)])."""
         k = C.shape[0]
-        b = self.run_pass(C, labels=return_labels, generic=generic, rule=rule)
+        b = self.run_pass(C, labels=return_labels, generic=generic, rule=rule, approx=approx)
         sums = torch.empty((k, self.d), dtype=torch.float64, device=self.device)
         counts = torch.empty(k, dtype=torch.int64, device=self.device)
         inertia = torch.empty(1, dtype=torch.float64, device=self.device)
@@ -489,7 +550,8 @@ def lloyd_step(parts, C, method="auto", accumulate="auto", label_rule=None):
     ds = _dataset(parts)
     Cd = _centers(C, ds)
     _check_method(method, accumulate, Cd.shape[0], ds.d)
-    C_new, s = ds.step(Cd, generic=(method == "generic"), rule=label_rule and _check_rule(label_rule))
+    C_new, s = ds.step(Cd, generic=(method == "generic"), rule=label_rule and _check_rule(label_rule),
+                       approx=(method == "approx"))
     inertia = float("nan") if s["flags"] & 1 else s["inertia"]
     return C_new.cpu().numpy(), inertia, s["n_empty"]
 
@@ -500,7 +562,7 @@ def assign_mlx(parts, C, method="auto", return_labels=False, accumulate="auto", 
     Cd = _centers(C, ds)
     _check_method(method, accumulate, Cd.shape[0], ds.d)
     out = ds.assign(Cd, return_labels=return_labels, generic=(method == "generic"),
-                    rule=label_rule and _check_rule(label_rule))
+                    rule=label_rule and _check_rule(label_rule), approx=(method == "approx"))
     return out
 
 

@@ -85,6 +85,7 @@ BoundsState carve_bounds(void* base, int64_t n, int d, int k) {
     BoundsState b;
     char* p = static_cast<char*>(base);
     b.meta = reinterpret_cast<double*>(p);
+    b.hsep = reinterpret_cast<float*>(p + 128);
     b.cprev = reinterpret_cast<float*>(p + 256);
     b.rows = reinterpret_cast<uint32_t*>(p + 256 + a256(sizeof(float) * (size_t)k * d));
     (void)n;
@@ -207,7 +208,7 @@ namespace {
 // kmc_pass and kmc_pass_bounded: bounds == nullptr for a plain pass
 int pass_impl(const char* who, const float* X, int64_t n, int d, const float* C, int k, const uint32_t* colmax,
               int64_t n_total, int64_t* totals, int32_t* labels, float* best, unsigned flags, void* workspace,
-              size_t ws_bytes, void* bounds, void* stream) {
+              size_t ws_bytes, void* bounds, void* stream, void* loop = nullptr) {
     if (int s = check_shape(n, d, k)) return s;
     if (!C || !colmax || !totals || !workspace || (n > 0 && !X))
         return fail(KMC_ERR_INVALID, "%s: null pointer", who);
@@ -223,7 +224,8 @@ int pass_impl(const char* who, const float* X, int64_t n, int d, const float* C,
     const bool clear = !(flags & KMC_PASS_ACCUMULATE);
     e = launch_prepare(C, k, d, colmax, n_total, ws.prep, ws.scale_x, ws.hc,
                        clear ? reinterpret_cast<long long*>(totals) : nullptr, clear ? ws.counters : nullptr,
-                       bounded ? b.meta : nullptr, bounded ? b.cprev : nullptr, (flags & KMC_PASS_LABEL32) ? 1 : 0, st);
+                       bounded ? b.meta : nullptr, bounded ? b.cprev : nullptr, bounded ? b.hsep : nullptr,
+                       (flags & KMC_PASS_LABEL32) ? 1 : 0, st, loop);
     if (e != cudaSuccess) return cuda_fail(e, who);
     if (n == 0) return KMC_OK;
     PassArgs a;
@@ -244,8 +246,10 @@ int pass_impl(const char* who, const float* X, int64_t n, int d, const float* C,
     a.ctile = 0;
     a.key_keep = 0;
     a.brows = nullptr;
+    a.hsep = nullptr;
     if (bounded) {
         a.brows = b.rows;
+        a.hsep = b.hsep;
         a.labels = nullptr;
         a.best = nullptr;
     }
@@ -287,6 +291,49 @@ int kmc_pass_bounded(const float* X, int64_t n, int d, const float* C, int k, co
                      ws_bytes, bounds, stream);
 }
 
+static_assert(sizeof(kmc_loop) == sizeof(LoopState), "kmc_loop layout");
+
+int kmc_loop_init(kmc_loop* loop, double tol, int64_t max_steps, int64_t steps_done, double prev_inertia,
+                  int have_prev, void* stream) {
+    if (!loop) return fail(KMC_ERR_INVALID, "kmc_loop_init: null pointer");
+    if (!(tol >= 0.0) || max_steps < 0 || steps_done < 0)
+        return fail(KMC_ERR_INVALID, "kmc_loop_init: tol %g, max_steps %lld, steps_done %lld", tol,
+                    (long long)max_steps, (long long)steps_done);
+    cudaError_t e = launch_loop_init(loop, tol, max_steps, steps_done, prev_inertia, have_prev,
+                                     static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "kmc_loop_init");
+    return KMC_OK;
+}
+
+int kmc_lloyd(const float* X, int64_t n, int d, float* C0, float* C1, int k, const uint32_t* colmax, int64_t n_total,
+              int64_t* totals, unsigned flags, void* bounds, size_t bounds_size, kmc_stats* stats, kmc_loop* loop,
+              int steps, void* workspace, size_t ws_bytes, void* stream) {
+    const char* who = "kmc_lloyd";
+    if (int s = check_shape(n, d, k)) return s;
+    if (!C0 || !C1 || !colmax || !totals || !stats || !loop || !workspace || (n > 0 && !X))
+        return fail(KMC_ERR_INVALID, "%s: null pointer", who);
+    if (steps < 0) return fail(KMC_ERR_INVALID, "%s: steps %d", who, steps);
+    if (flags & (KMC_PASS_ACCUMULATE | KMC_PASS_APPROX))
+        return fail(KMC_ERR_INVALID, "%s: flags 0x%x (one slice per call; the approximate pass is kmc_pass_split's)",
+                    who, flags);
+    if (bounds && bounds_size < bounds_bytes(n, d, k))
+        return fail(KMC_ERR_INVALID, "%s: bounds of %zu bytes, need %zu", who, bounds_size, bounds_bytes(n, d, k));
+    Workspace ws = carve(workspace, d, k);
+    if (ws_bytes < ws.bytes) return fail(KMC_ERR_INVALID, "%s: workspace of %zu bytes, need %zu", who, ws_bytes, ws.bytes);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    for (int i = 0; i < steps; i++) {
+        float* Cin = (i & 1) ? C1 : C0;
+        float* Cout = (i & 1) ? C0 : C1;
+        if (int s = pass_impl(who, X, n, d, Cin, k, colmax, n_total, totals, nullptr, nullptr, flags, workspace,
+                              ws_bytes, bounds, stream, loop))
+            return s;
+        cudaError_t e = launch_finish(reinterpret_cast<long long*>(totals), k, d, nullptr, 0, 1, Cout, stats, ws, st,
+                                      nullptr, 1, 0, 0, loop);
+        if (e != cudaSuccess) return cuda_fail(e, who);
+    }
+    return KMC_OK;
+}
+
 size_t kmc_split_bytes(int64_t n, int d) { return split_rows_bytes(n, d); }
 
 size_t kmc_csplit_bytes(int d, int k) { return split_centers_bytes(d, k); }
@@ -326,7 +373,7 @@ int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, cons
     const int rule = (flags & KMC_PASS_LABEL32) ? 1 : 0;
     e = launch_prepare(C, k, d, colmax, n_total, ws.prep, ws.scale_x, ws.hc,
                        clear ? reinterpret_cast<long long*>(totals) : nullptr, clear ? ws.counters : nullptr, nullptr,
-                       nullptr, rule, st);
+                       nullptr, nullptr, rule, st);
     if (e != cudaSuccess) return cuda_fail(e, who);
     if (n == 0) return KMC_OK;
     const RowSplit rs = carve_rows(split, n, d);
@@ -350,6 +397,7 @@ int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, cons
     ts.error = cs.error;
     ts.dump = nullptr;
     ts.rule = rule;
+    ts.approx = (flags & KMC_PASS_APPROX) ? 1 : 0;
     e = launch_assign_tc(ts, st);
     if (e != cudaSuccess) return cuda_fail(e, who);
     PassArgs a;
@@ -370,6 +418,7 @@ int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, cons
     a.ctile = 0;
     a.key_keep = 0;
     a.brows = nullptr;
+    a.hsep = nullptr;
     e = launch_accum_split(a, rs, cs, st);
     if (e != cudaSuccess) return cuda_fail(e, who);
     return KMC_OK;
@@ -406,6 +455,7 @@ int kmc_tc_dot(const float* C, int64_t n, int d, int k, void* split, size_t spli
     ts.error = cs.error;
     ts.dump = out;
     ts.rule = 0;
+    ts.approx = 0;
     e = launch_assign_tc(ts, st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(error, cs.error, sizeof(int), cudaMemcpyDeviceToDevice, st);
     if (e != cudaSuccess) return cuda_fail(e, who);

@@ -27,6 +27,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "kmc_internal.h"
 
@@ -44,12 +46,14 @@ constexpr uint32_t kSpinLimit = 1u << 22;
 // Shared memory.  AR (rows resident, dp <= 128): the row tile's xh / xl chunks stay for all center tiles and the
 // stages carry only ch / cl; otherwise every stage carries a chunk of each.
 constexpr int kResidentChunks = 2;       // dp <= 128
-template <int BN, bool AR>
+// APPROX (exact=False): the hi parts only, one MMA per product.
+template <int BN, bool AR, bool APPROX>
 struct TcSmem {
     static constexpr int A = BM * BK * 2;             // one 128 x 64 bf16 operand chunk (16 KB)
     static constexpr int B = BN * BK * 2;             // one BN x 64 bf16 chunk
-    static constexpr int AREG = AR ? kResidentChunks * 2 * A : 0;
-    static constexpr int STAGE = AR ? 2 * B : 2 * A + 2 * B;   // hi and lo of each operand it carries
+    static constexpr int PARTS = APPROX ? 1 : 2;      // hi and lo, or hi alone
+    static constexpr int AREG = AR ? kResidentChunks * PARTS * A : 0;
+    static constexpr int STAGE = AR ? PARTS * B : PARTS * (A + B);   // the parts of each operand it carries
     static constexpr int BAR = 256;                   // barriers, TMEM address, abort flag
     static constexpr int EPI = 2 * 4 * 32 * 5 * 4;    // the column halves' trackers: [tile parity][quarter][lane]
     static constexpr int total = AREG + kTcStages * STAGE + BAR + EPI + 1024;   // + slack to align to 1 KB
@@ -196,11 +200,34 @@ struct TcArgs {
     float wr;                // window term per (|x| + max|c|)^2: the rounding of the label rule's distance
 };
 
-template <int BN, bool AR>
+// The smallest score and its center (exact=False: no window, so the rest of the order is not needed); the same
+// interface as Top3 with m1 = m2 = +inf.
+struct Top1 {
+    float m0, m1, m2;
+    int l0, l1;
+    __device__ __forceinline__ void init() {
+        m0 = m1 = m2 = INFINITY;
+        l0 = l1 = 0;
+    }
+    __device__ __forceinline__ void push(float s, int c) {      // increasing c: strict less keeps the lower index
+        const bool a0 = s < m0;
+        l0 = a0 ? c : l0;
+        m0 = a0 ? s : m0;
+    }
+    __device__ __forceinline__ void merge(float n0, int k0, float, int, float) {
+        if (n0 < m0 || (n0 == m0 && k0 < l0)) {
+            m0 = n0;
+            l0 = k0;
+        }
+    }
+};
+
+template <int BN, bool AR, bool APPROX>
 __global__ void __launch_bounds__(kTcThreads, 1)
     k_assign_tc(const __grid_constant__ CUtensorMap mxh, const __grid_constant__ CUtensorMap mxl,
                 const __grid_constant__ CUtensorMap mch, const __grid_constant__ CUtensorMap mcl, TcArgs a) {
-    using S = TcSmem<BN, AR>;
+    using S = TcSmem<BN, AR, APPROX>;
+    constexpr int PARTS = S::PARTS;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // (resident rows,) stages at the first 1024-byte boundary, then the barrier block
     const uint32_t raw = smem_u32(smem_raw);
@@ -261,10 +288,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     // the row tile, once: after the previous tile's last MMA has read the resident chunks
                     ok = mbar_wait(aempty, tph ^ 1u, abort_flag);
                     if (!ok) break;
-                    mbar_expect_tx(afull, (uint32_t)(kchunks * 2 * S::A));
+                    mbar_expect_tx(afull, (uint32_t)(kchunks * PARTS * S::A));
                     for (int kc = 0; kc < kchunks; kc++) {
-                        tma_load_2d(base + kc * 2 * S::A, &mxh, kc * BK, (int)(t * BM), afull);
-                        tma_load_2d(base + kc * 2 * S::A + S::A, &mxl, kc * BK, (int)(t * BM), afull);
+                        tma_load_2d(base + kc * PARTS * S::A, &mxh, kc * BK, (int)(t * BM), afull);
+                        if constexpr (!APPROX)
+                            tma_load_2d(base + kc * 2 * S::A + S::A, &mxl, kc * BK, (int)(t * BM), afull);
                     }
                     tph ^= 1u;
                 }
@@ -276,12 +304,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         mbar_expect_tx(full(stage), S::STAGE);
                         if constexpr (AR) {
                             tma_load_2d(st, &mch, kc * BK, nt * BN, full(stage));
-                            tma_load_2d(st + S::B, &mcl, kc * BK, nt * BN, full(stage));
+                            if constexpr (!APPROX) tma_load_2d(st + S::B, &mcl, kc * BK, nt * BN, full(stage));
                         } else {
                             tma_load_2d(st, &mxh, kc * BK, (int)(t * BM), full(stage));
-                            tma_load_2d(st + S::A, &mxl, kc * BK, (int)(t * BM), full(stage));
-                            tma_load_2d(st + 2 * S::A, &mch, kc * BK, nt * BN, full(stage));
-                            tma_load_2d(st + 2 * S::A + S::B, &mcl, kc * BK, nt * BN, full(stage));
+                            if constexpr (APPROX) {
+                                tma_load_2d(st + S::A, &mch, kc * BK, nt * BN, full(stage));
+                            } else {
+                                tma_load_2d(st + S::A, &mxl, kc * BK, (int)(t * BM), full(stage));
+                                tma_load_2d(st + 2 * S::A, &mch, kc * BK, nt * BN, full(stage));
+                                tma_load_2d(st + 2 * S::A + S::B, &mcl, kc * BK, nt * BN, full(stage));
+                            }
                         }
                         if (++stage == kTcStages) { stage = 0; phase ^= 1u; }
                     }
@@ -310,16 +342,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         if (!ok) break;
                         tc_fence_after();
                         const uint32_t st = sbase + stage * S::STAGE;
-                        const uint32_t sa = AR ? base + kc * 2 * S::A : st;
-                        const uint32_t sb = AR ? st : st + 2 * S::A;
+                        const uint32_t sa = AR ? base + kc * PARTS * S::A : st;
+                        const uint32_t sb = AR ? st : st + PARTS * S::A;
                         const uint64_t ah = sw128_desc(sa), al = sw128_desc(sa + S::A);
                         const uint64_t bh = sw128_desc(sb), bl = sw128_desc(sb + S::B);
 #pragma unroll
                         for (int kk = 0; kk < BK / 16; kk++) {
                             const uint64_t off = (uint64_t)((kk * 32) >> 4);   // 16 bf16 = 32 B along K
                             mma_bf16(d_tmem, ah + off, bh + off, idesc, (kc | kk) != 0);
-                            mma_bf16(d_tmem, ah + off, bl + off, idesc, 1u);
-                            mma_bf16(d_tmem, al + off, bh + off, idesc, 1u);
+                            if constexpr (!APPROX) {
+                                mma_bf16(d_tmem, ah + off, bl + off, idesc, 1u);
+                                mma_bf16(d_tmem, al + off, bh + off, idesc, 1u);
+                            }
                         }
                         mma_commit(empty(stage));          // the stage is free once these MMAs are done
                         if (++stage == kTcStages) { stage = 0; phase ^= 1u; }
@@ -356,7 +390,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, it++) {
             const int64_t row = t * BM + 32 * q + lane;
             const float xr = (h == 0 && row < a.n) ? __ldg(a.xn + row) : 0.0f;   // in flight meanwhile
-            Top3 ev, od;                                  // even and odd columns: two independent chains
+            using Trk = std::conditional_t<APPROX, Top1, Top3>;
+            Trk ev, od;                                   // even and odd columns: two independent chains
             ev.init();
             od.init();
             for (int nt = 0; nt < ntiles && ok; nt++) {
@@ -402,7 +437,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const float r = xr + cmax;
                 const float win = (E2 * xr * cmax + cmax * (cmax + xr) * (1.0f / 8388608.0f)) * (1.0f + 1.0f / 1024.0f) +
                                   r * r * a.wr;
-                const bool flag = !(m1 - m0 > win) || l0 >= a.k;
+                // exact=False: no window (only a row whose best is a padding center -- non-finite scores -- goes to
+                // the float64 decision)
+                const bool flag = APPROX ? l0 >= a.k : (!(m1 - m0 > win) || l0 >= a.k);
                 a.lab[row] = (int32_t)((uint32_t)l0 | (flag ? 0x80000000u : 0u));
                 // candidates: the centers whose score is within the window of the smallest; when the third is
                 // too (or a score is not finite), there may be more than two: -2 sends the row to the full decision
@@ -455,7 +492,7 @@ bool make_map(CUtensorMap* m, const void* base, int64_t rows, int dp, int box_ro
     return r == CUDA_SUCCESS;
 }
 
-template <int BN, bool AR>
+template <int BN, bool AR, bool APPROX>
 cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
     CUtensorMap mxh, mxl, mch, mcl;
     if (!make_map(&mxh, s.xh, s.n, s.dp, BM) || !make_map(&mxl, s.xl, s.n, s.dp, BM) ||
@@ -464,9 +501,10 @@ cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
     static unsigned long long configured = 0;
     int dev = 0;
     cudaGetDevice(&dev);
-    const size_t smem = TcSmem<BN, AR>::total;
+    const size_t smem = TcSmem<BN, AR, APPROX>::total;
     if (!(configured >> (dev & 63) & 1ull)) {
-        cudaError_t e = cudaFuncSetAttribute(k_assign_tc<BN, AR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(k_assign_tc<BN, AR, APPROX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
         if (e != cudaSuccess) return e;
         configured |= 1ull << (dev & 63);
     }
@@ -487,8 +525,14 @@ cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
     int64_t grid = num_sms();
     if (grid > tiles) grid = tiles;
     if (grid < 1) grid = 1;
-    k_assign_tc<BN, AR><<<(int)grid, kTcThreads, smem, st>>>(mxh, mxl, mch, mcl, a);
+    k_assign_tc<BN, AR, APPROX><<<(int)grid, kTcThreads, smem, st>>>(mxh, mxl, mch, mcl, a);
     return cudaGetLastError();
+}
+
+template <int BN>
+cudaError_t run_tc_ar(const TcSplit& s, bool ar, cudaStream_t st) {
+    if (s.approx) return ar ? run_tc<BN, true, true>(s, st) : run_tc<BN, false, true>(s, st);
+    return ar ? run_tc<BN, true, false>(s, st) : run_tc<BN, false, false>(s, st);
 }
 
 }  // namespace
@@ -499,9 +543,9 @@ cudaError_t launch_assign_tc(const TcSplit& s, cudaStream_t st) {
     // the row tile stays resident when it fits (dp <= 128) and is used for more than one center tile
     const bool ar = s.dp <= kResidentChunks * BK && s.kp / tc_block_n(s.k) > 1;
     switch (tc_block_n(s.k)) {
-        case 64: return ar ? run_tc<64, true>(s, st) : run_tc<64, false>(s, st);
-        case 128: return ar ? run_tc<128, true>(s, st) : run_tc<128, false>(s, st);
-        default: return ar ? run_tc<256, true>(s, st) : run_tc<256, false>(s, st);
+        case 64: return run_tc_ar<64>(s, ar, st);
+        case 128: return run_tc_ar<128>(s, ar, st);
+        default: return run_tc_ar<256>(s, ar, st);
     }
 }
 

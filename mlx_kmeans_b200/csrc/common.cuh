@@ -32,6 +32,27 @@ struct Prep {
     int bvalid;             // bounded passes: the per-row bounds were written by an earlier pass
     float bcum_lo, bcum_up; // bounded passes: total center drift so far, rounded down / up
     int rule;               // label rule: 0 = float64 distance (NumPy pairwise), 1 = float32 direct sum
+    int skip;               // a device Lloyd loop has stopped: the pass and the finish of this step do nothing
+};
+
+// State of a Lloyd loop run on the device (kmc_lloyd; the public kmc_loop, 64 bytes).  k_prepare reads `state` to
+// skip the steps after the loop stopped; k_finish applies the reference's stopping rule after every step
+// (estimator.py:132-150: stop once |prev - inertia| <= tol * prev) and updates the record.
+struct LoopState {
+    double prev_inertia;    // inertia of the last step run (the tol test compares the next one with it)
+    double tol;
+    long long steps;        // steps completed (this loop record)
+    long long max_steps;
+    long long state;        // kLoop* below
+    long long have_prev;    // prev_inertia is set
+    long long reserved[2];
+};
+enum : long long {
+    kLoopRunning = 0,
+    kLoopConverged = 1,     // the tol test held after the last step
+    kLoopRelocate = 2,      // the last step emptied clusters: its centers were not written (the host relocates)
+    kLoopNonFinite = 3,     // non-finite data, centers or distance
+    kLoopMaxSteps = 4,      // max_steps steps ran
 };
 
 enum : int {

@@ -143,7 +143,35 @@ struct FinishArgs {
     int world, rank;
     unsigned long long step;
     unsigned long long timeout_ns;     // how long the exchange waits for a peer
+    LoopState* loop;                   // a device Lloyd loop's record (kmc_lloyd), or nullptr
 };
+
+// After a step of a device Lloyd loop (thread 0 of k_finish): the reference's stopping rule (estimator.py:132-150).
+__device__ void loop_after_step(LoopState* L, const Stats& s) {
+    if (s.flags & kFlagNonFinite || !(s.inertia <= 1.0e308)) {
+        L->state = kLoopNonFinite;
+        return;
+    }
+    if (s.needs_reloc) {                     // the host relocates, finishes this step and resumes the loop
+        L->state = kLoopRelocate;
+        return;
+    }
+    L->steps += 1;
+    if (L->have_prev && fabs(L->prev_inertia - s.inertia) <= L->tol * L->prev_inertia) L->state = kLoopConverged;
+    else if (L->steps >= L->max_steps) L->state = kLoopMaxSteps;
+    L->prev_inertia = s.inertia;
+    L->have_prev = 1;
+}
+
+__global__ void k_loop_init(LoopState* L, double tol, long long max_steps, long long steps, double prev, int have_prev) {
+    L->prev_inertia = prev;
+    L->tol = tol;
+    L->steps = steps;
+    L->max_steps = max_steps;
+    L->state = steps >= max_steps ? kLoopMaxSteps : kLoopRunning;
+    L->have_prev = have_prev;
+    L->reserved[0] = L->reserved[1] = 0;
+}
 
 // center c, column j of the new centers (cnt = the cluster's count, > 0): sums / counts in float64, rounded
 // once to float32; a cluster relocated into from a single row is that row
@@ -162,6 +190,10 @@ __global__ void __launch_bounds__(1024) k_finish(FinishArgs a) {
     __shared__ int s_bigi[32];
     __shared__ long long sh_n_empty, sh_inert, sh_nreloc;
     __shared__ int sh_big, sh_write, sh_xfail;
+    if (a.loop && a.loop->state != kLoopRunning) {    // the device loop stopped: nothing to do (read before any
+        if (tid == 0 && a.grid_centers) a.counters[4] = 0;   // thread writes the record, after the barriers below)
+        return;
+    }
     // 0. (fused step tail) the totals summed over the ranks
     if (a.peers)
         exchange_cta(a.totals, (int64_t)k * W, a.peers, a.world, a.rank, a.step, a.timeout_ns, a.counters, &sh_xfail);
@@ -248,6 +280,7 @@ __global__ void __launch_bounds__(1024) k_finish(FinishArgs a) {
             s.screened = a.counters[2];
             s.pad = 0;
             *a.stats = s;
+            if (a.loop) loop_after_step(a.loop, s);
         }
         return;
     }
@@ -302,6 +335,7 @@ __global__ void __launch_bounds__(1024) k_finish(FinishArgs a) {
         s.screened = a.counters[2];
         s.pad = 0;
         *a.stats = s;
+        if (a.loop) loop_after_step(a.loop, s);
     }
 }
 
@@ -324,8 +358,10 @@ __global__ void __launch_bounds__(256) k_finish_centers(FinishArgs a) {
 
 cudaError_t launch_finish(long long* totals, int k, int d, const uint32_t* cands, int64_t cand_rows, int ranks,
                           float* C_new, void* stats, const Workspace& ws, cudaStream_t st,
-                          const unsigned long long* peers, int world, int rank, unsigned long long step) {
+                          const unsigned long long* peers, int world, int rank, unsigned long long step,
+                          void* loop) {
     FinishArgs a;
+    a.loop = static_cast<LoopState*>(loop);
     a.totals = totals;
     a.k = k;
     a.d = d;
@@ -373,6 +409,12 @@ __global__ void k_unpack(const long long* __restrict__ totals, int k, int d, con
         const bool bad = (prep->flags | counters[1]) & kFlagNonFinite;
         *inertia = bad ? __longlong_as_double(0x7ff8000000000000ll) : (double)t * prep->inv_scale_i;
     }
+}
+
+cudaError_t launch_loop_init(void* loop, double tol, long long max_steps, long long steps, double prev_inertia,
+                             int have_prev, cudaStream_t st) {
+    k_loop_init<<<1, 1, 0, st>>>(static_cast<LoopState*>(loop), tol, max_steps, steps, prev_inertia, have_prev);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_unpack(const long long* totals, int k, int d, const double* scale_x, const Prep* prep,

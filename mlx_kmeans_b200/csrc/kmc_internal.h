@@ -27,12 +27,15 @@ struct PassArgs {
     int ctile;                // generic kernel: centers per shared tile
     unsigned key_keep;        // fused low-d kernel: ~(center index bits) of a key
     uint32_t* brows;          // bounded pass: one bound word per row (nullptr: plain pass)
+    const float* hsep;        // bounded pass: per center, (half its distance to the nearest other center)^2
     int64_t n_total;          // rows of the whole dataset (all slices and GPUs): sets the fixed-point grids
 };
 
-// Bounds state of one slice (caller memory): [meta: double drift, int64 valid][centers of the last pass].
+// Bounds state of one slice (caller memory): [meta: double drift, double valid; at byte 128: hsep, k <= 32 floats]
+// [centers of the last pass][one word per row].
 struct BoundsState {
     double* meta;
+    float* hsep;              // k: (s_c / 2)^2 rounded down, s_c = distance from center c to its nearest other one
     float* cprev;             // k x d
     uint32_t* rows;           // n
 };
@@ -68,7 +71,8 @@ cudaError_t launch_colmax(const float* X, int64_t n, int d, unsigned int* colmax
 // per-pass constants; optionally clears the totals and counters, and (bmeta != nullptr) prepares a bounded pass
 cudaError_t launch_prepare(const float* C, int k, int d, const unsigned int* colmax, int64_t n_total, Prep* prep,
                            double* scale_x, float* hc, long long* zero_totals, long long* zero_counters,
-                           double* bmeta, float* bcprev, int rule, cudaStream_t st);
+                           double* bmeta, float* bcprev, float* bhsep, int rule, cudaStream_t st,
+                           const void* loop = nullptr);
 cudaError_t launch_pass_generic(PassArgs a, cudaStream_t st);
 // Specialised low-dimensional fused pass; returns cudaErrorNotSupported when (d, k) has no instance.
 cudaError_t launch_pass_lowd(PassArgs a, cudaStream_t st);
@@ -109,6 +113,7 @@ struct TcSplit {
     int* error;
     float* dump;              // kmc_tc_dot: n x k raw scores x.c, or nullptr
     int rule;                 // label rule (Prep::rule): widens the window
+    int approx;               // exact=False: one bf16 MMA per product (hi parts), no window
 };
 int split_dp(int d);
 int split_kp(int k);
@@ -134,7 +139,9 @@ cudaError_t launch_far_rows(const float* X, int64_t n, int d, const int32_t* lab
 cudaError_t launch_finish(long long* totals, int k, int d, const uint32_t* cands, int64_t cand_rows, int ranks,
                           float* C_new, void* stats, const Workspace& ws, cudaStream_t st,
                           const unsigned long long* peers = nullptr, int world = 1, int rank = 0,
-                          unsigned long long step = 0);
+                          unsigned long long step = 0, void* loop = nullptr);
+cudaError_t launch_loop_init(void* loop, double tol, long long max_steps, long long steps, double prev_inertia,
+                             int have_prev, cudaStream_t st);
 cudaError_t launch_unpack(const long long* totals, int k, int d, const double* scale_x, const Prep* prep,
                           const long long* counters, double* sums, int64_t* counts, double* inertia, cudaStream_t st);
 

@@ -36,8 +36,26 @@ __global__ void k_colmax(const float* __restrict__ X, int64_t total, int d, int6
 // bounds lose max_c drift per pass (Hamerly: the distance to any other center shrinks by at most its move).
 // The running total goes to the pass as float32 bounds on both sides; the current centers become c_prev.  When
 // the bounds are not valid yet the pass writes them all, so they are valid afterwards with zero drift.
+//
+// It also writes each center's half separation (Hamerly's s(c)/2 test): hsep[c] = (s_c / 2)^2 rounded down, s_c the
+// distance from c to its nearest other center (float64, rounded down; +inf when k = 1).  A row at distance u from its
+// stored label's center l with u < s_l / 2 is closer to l than to any other center c, since |x - c| >= s_l - u > u
+// (the triangle inequality) -- whatever the centers did since its bound was stored.
 __device__ void bounds_prepare_cta(const float* __restrict__ C, int k, int d, double* __restrict__ meta,
-                                   float* __restrict__ cprev, Prep* __restrict__ prep) {
+                                   float* __restrict__ cprev, float* __restrict__ hsep, Prep* __restrict__ prep) {
+    for (int c = threadIdx.x; c < k; c += blockDim.x) {
+        double s2 = INFINITY;
+        for (int o = 0; o < k; o++) {
+            if (o == c) continue;
+            double t = 0.0;
+            for (int j = 0; j < d; j++) {
+                const double q = (double)C[(int64_t)c * d + j] - (double)C[(int64_t)o * d + j];   // exact
+                t = __fma_rd(q, q, t);
+            }
+            s2 = fmin(s2, t);
+        }
+        hsep[c] = __double2float_rd(0.25 * s2);
+    }
     __shared__ double s_dmax[32];
     const bool valid = meta[1] != 0.0;
     double mx = 0.0;
@@ -81,10 +99,15 @@ __global__ void k_prepare(const float* __restrict__ C, int k, int d, const unsig
                           int64_t n_total, Prep* __restrict__ prep, double* __restrict__ scale_x,
                           float* __restrict__ hc, long long* __restrict__ zero_totals, int zero_n,
                           long long* __restrict__ zero_counters, double* __restrict__ bmeta,
-                          float* __restrict__ bcprev, int rule) {
+                          float* __restrict__ bcprev, float* __restrict__ bhsep, int rule,
+                          const LoopState* __restrict__ loop) {
     __shared__ float s_max[32];
     __shared__ float s_cmax2[32];
     __shared__ int s_bad;
+    if (loop && loop->state != kLoopRunning) {        // the device loop stopped: this step does nothing
+        if (threadIdx.x == 0) prep->skip = 1;
+        return;
+    }
     if (threadIdx.x == 0) s_bad = 0;
     if (zero_totals)
         for (int e = threadIdx.x; e < zero_n; e += blockDim.x) zero_totals[e] = 0;
@@ -159,11 +182,12 @@ __global__ void k_prepare(const float* __restrict__ C, int k, int d, const unsig
         p.bcum_lo = 0.0f;
         p.bcum_up = 0.0f;
         p.rule = rule;
+        p.skip = 0;
         *prep = p;
     }
     if (bmeta) {
         __syncthreads();
-        bounds_prepare_cta(C, k, d, bmeta, bcprev, prep);
+        bounds_prepare_cta(C, k, d, bmeta, bcprev, bhsep, prep);
     }
 }
 
@@ -182,6 +206,7 @@ __global__ void __launch_bounds__(256) k_pass_generic(PassArgs a) {
     float* htile = ctile + (size_t)a.ctile * d;
     for (int s = threadIdx.x; s < nslots; s += blockDim.x) sacc[s] = 0;
     const Prep prep = *a.prep;
+    if (prep.skip) return;
     const double scale_i = prep.scale_i;
     int rescored = 0, bad = 0;
 
@@ -275,15 +300,16 @@ cudaError_t launch_colmax(const float* X, int64_t n, int d, unsigned int* colmax
 
 cudaError_t launch_prepare(const float* C, int k, int d, const unsigned int* colmax, int64_t n_total, Prep* prep,
                            double* scale_x, float* hc, long long* zero_totals, long long* zero_counters,
-                           double* bmeta, float* bcprev, int rule, cudaStream_t st) {
+                           double* bmeta, float* bcprev, float* bhsep, int rule, cudaStream_t st,
+                           const void* loop) {
     const int64_t zn = (int64_t)k * (d + 2);
-    if (zero_totals && zn > 16384) {           // large totals: a memset is faster than one CTA
+    if (zero_totals && zn > 16384 && !loop) {  // large totals: a memset is faster than one CTA
         cudaError_t e = cudaMemsetAsync(zero_totals, 0, sizeof(long long) * (size_t)zn, st);
         if (e != cudaSuccess) return e;
         zero_totals = nullptr;
     }
     k_prepare<<<1, 1024, 0, st>>>(C, k, d, colmax, n_total, prep, scale_x, hc, zero_totals, (int)zn, zero_counters,
-                                  bmeta, bcprev, rule);
+                                  bmeta, bcprev, bhsep, rule, static_cast<const LoopState*>(loop));
     return cudaGetLastError();
 }
 

@@ -732,6 +732,7 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(PlainSmem<D, K>::total) 
     float* cs = reinterpret_cast<float*>(smem + L::ring + L::sums + L::cnts);
     long long* acc = reinterpret_cast<long long*>(smem + L::ring + L::sums + L::cnts + L::centers);
 
+    if (a.prep->skip) return;                          // a device Lloyd loop has stopped
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int k = a.k;
     const int64_t n = a.n;
@@ -807,7 +808,10 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(PlainSmem<D, K>::total) 
     st.finish(acc, a, tid);
 }
 
-// The bounded pass.  Each thread streams its rows and their bound words straight into registers, P rows ahead
+// The bounded pass.  A row keeps its stored label without a screen when either test proves it the nearest center:
+// Hamerly's bound (its distance to the label's center below the stored lower bound less the drift since) or his
+// half-separation test (that distance below half the label center's distance to its nearest other center,
+// hsep, which needs no history).  Each thread streams its rows and their bound words straight into registers, P rows ahead
 // (global loads that skip L1: every byte is read once), so neither passes through shared memory; the center
 // of the next row's stored label is read one row ahead.  A row whose bound holds adds its residual to its
 // lane's slot of the stored label.  Rows whose bound fails queue per warp (offsets within the block) and are
@@ -838,11 +842,14 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
     int* queue_all = reinterpret_cast<int*>(smem + off);           off += L::queue;
     float* qrows_all = reinterpret_cast<float*>(smem + off);
 
+    if (a.prep->skip) return;                          // a device Lloyd loop has stopped
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int k = a.k;
     const int64_t n = a.n;
+    __shared__ float sh_hsep[32];                        // Hamerly's s(c)/2 test, squared (0 past k: never holds)
 
     for (int e = tid; e < 32 * D; e += kThreads) cs[e] = (e / D) < k ? a.C[e] : 0.0f;
+    for (int e = tid; e < 32; e += kThreads) sh_hsep[e] = e < k ? a.hsep[e] : 0.0f;
     for (int e = tid; e < Packed<D, K>::kWords; e += kThreads) pks[e] = Packed<D, K>::word(a.C, a.hc, k, e);
     for (int e = tid; e < K * (D + 2); e += kThreads) acc[e] = 0;
     for (int e = tid; e < kWarps * L::kSums; e += kThreads) sums_all[e] = 0.0f;
@@ -959,6 +966,7 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
                     const int l = (int)(w & MASK);
                     // this lane's slot of the stored label first: its latency overlaps the arithmetic
                     const unsigned sa = st.slot_addr(l);
+                    const float hl = sh_hsep[l];
                     bool keep;
                     float b;
                     if constexpr (PK) {
@@ -973,7 +981,8 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
                             b = i == 0 ? lo_of(q2) : __fadd_rn(b, lo_of(q2));
                             b = __fadd_rn(b, hi_of(q2));
                         }
-                        keep = bounded && valid && st.holds(w, b);
+                        // both tests evaluated (no branch per row)
+                        keep = bounded & valid & (st.holds(w, b) | (__fmul_rn(b, st.hold_f) < hl));
                         lds_row2<D>(cr2, st.cs_s + (wq[(s + 1) % P] & MASK) * (unsigned)(D * 4));   // row r + 1's
                         if (keep) {
 #pragma unroll
@@ -984,7 +993,8 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
                         float sl[D], t[D];
                         load_row<D>(sl, sa);
                         b = st.residual(xq[q], cr, t);
-                        keep = bounded && valid && st.holds(w, b);
+                        // both tests evaluated (no branch per row)
+                        keep = bounded & valid & (st.holds(w, b) | (__fmul_rn(b, st.hold_f) < hl));
                         load_row<D>(cr, st.cs_s + (wq[(s + 1) % P] & MASK) * (unsigned)(D * 4));   // row r + 1's
                         if (keep) {
                             add_into<D>(sl, t);

@@ -5,7 +5,8 @@
 Same constructor, attributes and errors as the reference (estimator.py:52-65, 180-230): n_clusters, n_init,
 max_iter, tol (relative inertia change), random_state, verbose, spherical, accumulate, exact, plus the
 reference's e-means options, which this build does not offer (algorithm must be "lloyd"). The Lloyd loop keeps
-its centers on the device; each step reads back one 64-byte statistics record for the tol test.
+its centers on the device and, on one GPU with the CUDA-core pass, runs whole on the device (kmc_lloyd: the tol test
+in the finish kernel, one host read at the end); elsewhere each step reads back one 64-byte statistics record.
 """
 import numpy as np
 import torch
@@ -20,8 +21,10 @@ class KMeans:
     reference's exact-mode kernels bit for bit (their float32 direct sum, strict < in index order, core.py:263-274).
     The two differ only on rows whose float32 sums to two centers are within their rounding of each other.
 
-    exact=False is accepted for API parity and runs the exact path (the reference ignores it as well below
-    its crossover dims; the approximate kernel is not part of this build yet). accumulate="atomic" also runs the
+    exact=False takes the approximate kernel from 64 dims up on the tensor-core path (x.c from one bf16 product,
+    the smallest score's center without an error window: the reference's approximate assignment, core.py:859-1088);
+    below that it runs exactly, as the reference does below its crossover. Counts, sums and inertia are exact for
+    the labels it gives. accumulate="atomic" also runs the
     deterministic accumulation: totals here are exact integers, so there is no faster non-deterministic mode to
     opt into.
     """
@@ -104,12 +107,21 @@ class KMeans:
         ds.reset_bounds()                  # a restart: the previous run's per-row bounds say nothing useful
         if self.spherical:
             C = self._normalise(C)
+        generic = self._method == "generic"
+        approx = self._method == "approx"
+        if not self.spherical and not self.verbose and ds.device_loop_ok(generic) and \
+                not ds.uses_approx(approx):
+            # the whole loop on the device: one host read at the end (estimator.py:132-150's stopping rule)
+            C, inertia, iters, flags = ds.lloyd_loop(C, self.max_iter, self.tol, generic=generic,
+                                                     rule=self.label_rule)
+            if flags & 1 or not np.isfinite(inertia):
+                self._explain_nonfinite(ds)
+            return C.clone(), inertia, iters
         prev = None
         inertia = float("nan")
         it = 0
-        generic = self._method == "generic"
         for it in range(self.max_iter):
-            C_new, s = ds.step(C, generic=generic, rule=self.label_rule)
+            C_new, s = ds.step(C, generic=generic, rule=self.label_rule, approx=approx)
             C = C_new.clone()
             inertia = s["inertia"]
             if s["flags"] & 1 or not np.isfinite(inertia):
@@ -152,7 +164,8 @@ class KMeans:
             C, inertia, iters = self._one_run(ds, rows, seed)
             # the last step's inertia belongs to the centers it started from; one more pass scores the returned ones
             # (estimator.py:201-204)
-            _, _, inertia, labels = ds.assign(C, return_labels=True, rule=self.label_rule)
+            _, _, inertia, labels = ds.assign(C, return_labels=True, rule=self.label_rule,
+                                              approx=self._method == "approx")
             if self.verbose and self.n_init > 1:
                 print(f"start {run + 1}/{self.n_init}: inertia {inertia:.6e} after {iters} iterations")
             if best is None or inertia < best[1]:
@@ -167,7 +180,8 @@ class KMeans:
             raise ValueError(f"X has {ds.d} features but this model was fitted with "
                              f"{self.cluster_centers_.shape[1]}")
         C = torch.from_numpy(np.ascontiguousarray(self.cluster_centers_, dtype=np.float32)).to(ds.device)
-        _, _, inertia, labels = ds.assign(C, return_labels=True, rule=self.label_rule)
+        _, _, inertia, labels = ds.assign(C, return_labels=True, rule=self.label_rule,
+                                          approx=self._method == "approx")
         if not np.isfinite(inertia):
             self._explain_nonfinite(ds)
         return labels
