@@ -3,8 +3,8 @@
     KMeans(n_clusters=64).fit(X).cluster_centers_
 
 Same constructor, attributes and errors as the reference (estimator.py:52-65, 180-230): n_clusters, n_init,
-max_iter, tol (relative inertia change), random_state, verbose, spherical, accumulate, exact, plus the
-reference's e-means options, which this build does not offer (algorithm must be "lloyd"). The Lloyd loop keeps
+max_iter, tol (relative inertia change), random_state, verbose, spherical, accumulate, exact, and the e-means
+options (algorithm="emeans", epochs, batch_size: mlx_kmeans_b200.emeans), plus label_rule. The Lloyd loop keeps
 its centers on the device and, on one GPU with the CUDA-core pass, runs whole on the device (kmc_lloyd: the tol test
 in the finish kernel, one host read at the end); elsewhere each step reads back one 64-byte statistics record.
 """
@@ -136,12 +136,35 @@ class KMeans:
             prev = inertia
         return C, inertia, it + 1
 
+    # e-means keeps its own exact accumulation; the reference's accumulator names map onto it
+    _EMEANS_ACCUMULATE = {"auto": "auto", "lanes": "lanes", "blocks": "blocks", "sorted": "segments"}
+
     def _check_algorithm(self):
+        """algorithm="lloyd" (default) or "emeans" with its options (estimator.py:155-170)."""
         algorithm = getattr(self, "algorithm", "lloyd")
         if algorithm not in ("lloyd", "emeans"):
             raise ValueError(f"algorithm must be 'lloyd' or 'emeans', got {algorithm!r}")
-        if algorithm == "emeans":
-            raise ValueError("algorithm='emeans' is not part of this build (the Lloyd path is)")
+        if algorithm != "emeans":
+            return
+        if isinstance(self.epochs, bool) or not isinstance(self.epochs, (int, np.integer)) or self.epochs < 1:
+            raise ValueError("epochs must be a positive integer")
+        if self.batch_size is not None and (isinstance(self.batch_size, bool) or
+                                            not isinstance(self.batch_size, (int, np.integer)) or self.batch_size < 1):
+            raise ValueError("batch_size must be None or a positive integer")
+        if self.spherical:
+            raise ValueError("spherical=True is not offered with algorithm='emeans'")
+        if self.accumulate not in self._EMEANS_ACCUMULATE:
+            raise ValueError(f"accumulate={self.accumulate!r} is not offered with algorithm='emeans' "
+                             f"(use one of {sorted(self._EMEANS_ACCUMULATE)})")
+
+    def _one_run_emeans(self, ds, rows, seed):
+        from . import emeans
+        if self.batch_size is not None and self.batch_size > rows:
+            raise ValueError(f"batch_size ({self.batch_size}) cannot exceed the number of rows ({rows})")
+        C, record = emeans.emeans_fit(ds, self.n_clusters, epochs=self.epochs, seed=seed, batch_size=self.batch_size,
+                                      assign="exact" if self.exact else "approx",
+                                      accumulate=self._EMEANS_ACCUMULATE[self.accumulate], verbose=self.verbose)
+        return torch.from_numpy(C).to(ds.device), record
 
     def fit(self, X, y=None):
         for name in ['n_clusters', 'n_init', 'max_iter']:
@@ -158,19 +181,30 @@ class KMeans:
         rows = ds.n_total
         if rows < self.n_clusters:
             raise ValueError('n_clusters cannot exceed the number of rows')
+        emeans = getattr(self, "algorithm", "lloyd") == "emeans"
         best = None
         for run in range(self.n_init):                  # every start runs on the same device-resident Dataset
             seed = None if self.random_state is None else self.random_state + run
-            C, inertia, iters = self._one_run(ds, rows, seed)
+            record = None
+            if emeans:
+                C, record = self._one_run_emeans(ds, rows, seed)
+                iters = self.epochs
+            else:
+                C, inertia, iters = self._one_run(ds, rows, seed)
             # the last step's inertia belongs to the centers it started from; one more pass scores the returned ones
             # (estimator.py:201-204)
             _, _, inertia, labels = ds.assign(C, return_labels=True, rule=self.label_rule,
                                               approx=self._method == "approx")
+            if emeans and not np.isfinite(inertia):
+                self._explain_nonfinite(ds)
             if self.verbose and self.n_init > 1:
-                print(f"start {run + 1}/{self.n_init}: inertia {inertia:.6e} after {iters} iterations")
+                print(f"start {run + 1}/{self.n_init}: inertia {inertia:.6e} after {iters} "
+                      f"{'epochs' if emeans else 'iterations'}")
             if best is None or inertia < best[1]:
-                best = (C.cpu().numpy(), inertia, iters, labels)
-        self.cluster_centers_, self.inertia_, self.n_iter_, self.labels_ = best
+                best = (C.cpu().numpy(), inertia, iters, labels, record)
+        self.cluster_centers_, self.inertia_, self.n_iter_, self.labels_ = best[:4]
+        if emeans:
+            self.emeans_record_ = best[4]
         return self
 
     def predict(self, X):
