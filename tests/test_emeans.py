@@ -10,7 +10,7 @@ trajectory within 1e-5 and the last-epoch means within 1e-6 of the RMS coordinat
 arithmetic allows):
   - every batch's labels are the float64-nearest of the float32 centres the batch was assigned against (bit-exact
     to the oracle), and every revival decision is the shared draw on the N the fit read;
-  - the oracle driven by the fit's labels and decisions follows the fit's centres to 1e-9 and ends at the same
+  - the oracle driven by the fit's labels and decisions follows the fit's centres to 1e-7 and ends at the same
     centres to 1e-6 of the RMS coordinate;
   - same seed, same bits; KMeans(algorithm="emeans") end to end.
 """
@@ -110,7 +110,9 @@ def test_fit_against_the_driven_oracle(name, cuda_device):
     Co, ro = emeans64(X, rec["k"], rec["epochs"], rec["seed"], rec["B"], rec["a0"], rec["init_centres"],
                       labels=[tr["labels"] for tr in trace], revivals=checks)
     drift = max(float(np.abs(tr["C"] - to["C"]).max()) for tr, to in zip(trace, ro["trace"]))
-    assert drift <= 1e-9 * rms, drift
+    # the batch sums are exact integers of each value, or (the fused low-d kernel) of per-lane float32 partials of
+    # the residuals: the parity suite's sums bar, 1e-7 of the RMS coordinate (the reference's own: 1e-5)
+    assert drift <= 1e-7 * rms, drift
     assert np.abs(C.astype(np.float64) - Co).max() <= 1e-6 * rms
     assert rec["revived"] == ro["revived"]
     assert np.array_equal(rec["last_epoch_counts"], ro["last_epoch_counts"])
