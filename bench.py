@@ -49,6 +49,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--generic", action="store_true", help="force the any-shape kernel (diagnostic)")
     p.add_argument("--no-bounds", action="store_true", help="compare every row with every center each pass")
+    p.add_argument("--approx", action="store_true",
+                   help="exact=False: the approximate tensor-core pass (one bf16 product per score; d >= 64)")
     return p.parse_args()
 
 
@@ -122,11 +124,18 @@ class Clocks:
 
 
 def cpu_baseline(cfg, budget_s=12.0, rows=4_000_000):
-    """The reference's CPU Lloyd pass (oracle/assign_numpy_port.py, core.py:197-215) on a leading sample."""
+    """The reference's CPU Lloyd pass (oracle/assign_numpy_port.py, core.py:197-215) on a leading sample: at most
+    `rows` rows, fewer where a pass of them would take more than a quarter of the budget (a probe pass on 20k rows
+    sets the rate)."""
     from oracle.assign_numpy_port import cpu_lloyd_pass
     from mlx_kmeans_b200.data import CONFIGS, host_sample
     c = CONFIGS[cfg]
-    n = min(rows, c["rows"])
+    probe = host_sample(cfg, min(20_000, c["rows"]), seed_offset=1)
+    cpu_lloyd_pass([probe], probe[:c["k"]].copy())
+    t = time.perf_counter()
+    cpu_lloyd_pass([probe], probe[:c["k"]].copy())
+    rate = len(probe) / (time.perf_counter() - t)
+    n = int(max(10_000, min(rows, c["rows"], rate * budget_s / 4)))
     X = host_sample(cfg, n)
     rng = np.random.default_rng(0)
     C = X[rng.choice(n, c["k"], replace=False)].copy()
@@ -239,7 +248,7 @@ def main():
 
     # warm-up: full Lloyd steps (relocation handled)
     for _ in range(max(args.warmup, 3)):
-        C_new, s = ds.step(C, generic=args.generic, bounded=not args.no_bounds)
+        C_new, s = ds.step(C, generic=args.generic, bounded=not args.no_bounds, approx=args.approx)
         C = C_new.clone()
 
     L = _lib.load()
@@ -257,6 +266,9 @@ def main():
     if tc:
         (spl, splb), (csp, cspb) = ds.split()[0], ds.csplit(k)
     flags = _lib.KMC_PASS_GENERIC if args.generic else 0
+    approx = args.approx and tc and ds.uses_approx(True)
+    if approx:
+        flags |= _lib.KMC_PASS_APPROX
     xch = ds._exchange(k) if world > 1 else False
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -330,7 +342,8 @@ def main():
                 a0 = torch.cuda.Event(enable_timing=True)
                 a0.record(st)
             Xd.copy_(Xh, non_blocking=True)
-            Ch, inertia, n_empty = km.lloyd_step(core.Dataset([Xd], group=group), Ch)
+            Ch, inertia, n_empty = km.lloyd_step(core.Dataset([Xd], group=group), Ch,
+                                                 method="approx" if args.approx else "auto")
         a1 = torch.cuda.Event(enable_timing=True)
         a1.record(st)
         torch.cuda.synchronize()
@@ -352,6 +365,7 @@ def main():
     # so its own ceiling is a third of that peak
     tpeak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
     tensor_bound = tc and flops_per_launch / (tpeak * 1e12) > bytes_per_launch / (pk["hbm_gbs"] * 1e9)
+    mmas = 1 if approx else 3             # bf16 MMAs per product: the pass's own ceiling is peak / mmas
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
@@ -373,7 +387,8 @@ def main():
                    "rows_rescored_in_float64_per_pass": rescored,
                    "per_row_bounds": bounded,
                    "fraction_of_rows_compared_with_every_center": screened if bounded else 1.0,
-                   "kernel": "generic" if args.generic else ("tensor cores (kmc_pass_split)" if tc else "auto")},
+                   "kernel": "generic" if args.generic else (("tensor cores (kmc_pass_split" +
+                                                               (", exact=False)" if approx else ")")) if tc else "auto")},
         "roofline": ({"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                       "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
                       "kernel_ms": pass_ms, "algorithmic_bytes_per_launch": bytes_per_launch,
@@ -381,7 +396,8 @@ def main():
                      if not tensor_bound else
                      {"bound": "tensor", "achieved": flops_per_launch / (pass_ms * 1e-3) / 1e12, "peak": tpeak,
                       "unit": "TFLOP/s", "frac": flops_per_launch / (pass_ms * 1e-3) / 1e12 / tpeak,
-                      "frac_of_split_ceiling": 3 * flops_per_launch / (pass_ms * 1e-3) / 1e12 / tpeak,
+                      "frac_of_split_ceiling": mmas * flops_per_launch / (pass_ms * 1e-3) / 1e12 / tpeak,
+                      "bf16_mmas_per_product": mmas,
                       "traffic": traffic, "kernel_ms": pass_ms, "algorithmic_flops_per_launch": flops_per_launch,
                       "peak_source": (f"{src} bf16_tflops_sustained (MEASURED_PEAKS.json)" if src == "measured"
                                       else "fallback")}),
