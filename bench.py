@@ -263,10 +263,15 @@ def main():
     tc = ds.tensor_cores and not args.generic       # d >= 32: the tensor-core pass (kmc_pass_split)
     bounded = not args.no_bounds and not args.generic and not tc
     bb, bbytes = ds.bounds(k)[0] if bounded else (None, 0)
+    approx = args.approx and tc and ds.uses_approx(True)
+    elk = None
     if tc:
         (spl, splb), (csp, cspb) = ds.split()[0], ds.csplit(k)
+        # per-center bounds (kmc_pass_elkan) built by the warm-up steps, used by every timed step
+        e = ds._elkan.get(k)
+        if not args.no_bounds and not approx and e is not None and e["valid"]:
+            elk = e["bufs"][0]
     flags = _lib.KMC_PASS_GENERIC if args.generic else 0
-    approx = args.approx and tc and ds.uses_approx(True)
     if approx:
         flags |= _lib.KMC_PASS_APPROX
     xch = ds._exchange(k) if world > 1 else False
@@ -285,7 +290,12 @@ def main():
     for i in range(K):
         Cin, Cout = Cs[i % 2], Cs[(i + 1) % 2]
         ev[i][0].record(st)
-        if tc:
+        if elk is not None:
+            _lib.check(L.kmc_pass_elkan(X.data_ptr(), X.shape[0], d, Cin.data_ptr(), k, cm.data_ptr(), n_total,
+                                        b["totals"].data_ptr(), None, None, flags, spl.data_ptr(), splb,
+                                        csp.data_ptr(), cspb, elk[0].data_ptr(), elk[1], b["ws"].data_ptr(),
+                                        b["wsb"], sp))
+        elif tc:
             _lib.check(L.kmc_pass_split(X.data_ptr(), X.shape[0], d, Cin.data_ptr(), k, cm.data_ptr(), n_total,
                                         b["totals"].data_ptr(), None, None, flags, spl.data_ptr(), splb,
                                         csp.data_ptr(), cspb, b["ws"].data_ptr(), b["wsb"], sp))
@@ -386,7 +396,9 @@ def main():
                    "relocation_steps_in_timed_region": reloc_steps,
                    "rows_rescored_in_float64_per_pass": rescored,
                    "per_row_bounds": bounded,
+                   "per_center_bounds": elk is not None,
                    "fraction_of_rows_compared_with_every_center": screened if bounded else 1.0,
+                   "fraction_of_row_center_pairs_visited": (screened / k) if elk is not None else None,
                    "kernel": "generic" if args.generic else (("tensor cores (kmc_pass_split" +
                                                                (", exact=False)" if approx else ")")) if tc else "auto")},
         "roofline": ({"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
@@ -406,7 +418,8 @@ def main():
         # float64 decision and the per-cluster reduction), k_finish (it runs the all-reduce over peer memory first
         # on several GPUs; with NCCL instead, NCCL's own kernel, not counted) and, above 32768 center values,
         # k_finish_centers
-        "gpu_launches": ((11 + (1 if k * d > 32768 else 0)) if tc else 3) * K,
+        # (with per-center bounds: k_elkan_drift and k_elkan in place of k_assign_tc)
+        "gpu_launches": ((11 + (1 if elk is not None else 0) + (1 if k * d > 32768 else 0)) if tc else 3) * K,
         "host_enqueue_ms_per_step": host_ms,
         "e2e": e2e,
     }

@@ -54,6 +54,8 @@ enum kmc_status {
  * center taken with no error window, so a row whose two best centers are within the bf16 rounding may get the
  * second.  Counts, sums and inertia are still exact for the labels given (read from the float32 rows). */
 #define KMC_PASS_APPROX 8u
+/* kmc_pass_elkan: (re)build the per-center bounds with a full tensor-core pass instead of using them. */
+#define KMC_PASS_ELKAN_BUILD 16u
 
 /* Device statistics of one Lloyd step, as kmc_finish leaves them (layout fixed, 64 bytes). */
 typedef struct kmc_stats {
@@ -139,6 +141,24 @@ int kmc_pass_split(const float *X, int64_t n, int d, const float *C, int k, cons
                    int64_t n_total, int64_t *totals, int32_t *labels, float *best, unsigned flags, void *split,
                    size_t split_bytes, void *csplit, size_t csplit_bytes, void *workspace, size_t ws_bytes,
                    void *stream);
+
+/* Per-center lower bounds between passes for the tensor-core shapes (Elkan): the reference's bounded high-d path
+ * (core.py:1690-2015, engaged at core.py:2063-2084).  A caller buffer of kmc_elkan_bytes(n, d, k) bytes per slice
+ * holds the centers the bounds refer to, their drift, and one float16 lower bound per (row, center), rounded toward
+ * zero.  kmc_pass_elkan is kmc_pass_split (same arguments plus the bounds; the same labels, best and totals, bit for
+ * bit) that, with KMC_PASS_ELKAN_BUILD, runs the full tensor-core pass and writes every bound, and without it runs
+ * the bounded pass: each row's distance to its previous label is recomputed, every bound is lowered by its center's
+ * drift since, and only the centers whose lowered bound does not exceed that distance (plus the decision window)
+ * are visited; near ties go to the same float64 (or float32-rule) decision.  The labels of the previous pass on the
+ * slice (kept in the split) are the starting guesses -- any labels are correct starting guesses, only the work
+ * depends on them.  The number of visited (row, center) pairs is added to the statistics' `screened`; a caller
+ * rebuilds (or drops) the bounds when it grows.  The first call on a split must build (any pass on the split leaves
+ * the grouped row order the bounded pass walks).  k must be a multiple of 8; not with KMC_PASS_APPROX. */
+size_t kmc_elkan_bytes(int64_t n, int d, int k);
+int kmc_pass_elkan(const float *X, int64_t n, int d, const float *C, int k, const uint32_t *colmax, int64_t n_total,
+                   int64_t *totals, int32_t *labels, float *best, unsigned flags, void *split, size_t split_bytes,
+                   void *csplit, size_t csplit_bytes, void *elkan, size_t elkan_bytes, void *workspace,
+                   size_t ws_bytes, void *stream);
 
 /* The tensor-core pass's raw scores, for auditing its error window (no counterpart in the reference): out
  * (device, n x k float32) = x.c for every row of the split (kmc_split_rows) and every center, exactly as the

@@ -16,6 +16,7 @@ KMC_PASS_ACCUMULATE = 1
 KMC_PASS_GENERIC = 2
 KMC_PASS_LABEL32 = 4
 KMC_PASS_APPROX = 8
+KMC_PASS_ELKAN_BUILD = 16
 KMC_MAX_DIMS = 4096
 STATS_BYTES = 64
 
@@ -51,6 +52,9 @@ SIGNATURES = {
     "kmc_csplit_bytes": (_sz, [_int, _int]),
     "kmc_pass_split": (_int, [_vp, _i64, _int, _vp, _int, _vp, _i64, _vp, _vp, _vp, _u, _vp, _sz, _vp, _sz, _vp, _sz,
                               _vp]),
+    "kmc_elkan_bytes": (_sz, [_i64, _int, _int]),
+    "kmc_pass_elkan": (_int, [_vp, _i64, _int, _vp, _int, _vp, _i64, _vp, _vp, _vp, _u, _vp, _sz, _vp, _sz, _vp, _sz,
+                              _vp, _sz, _vp]),
     "kmc_tc_dot": (_int, [_vp, _i64, _int, _int, _vp, _sz, _vp, _sz, _vp, _vp, _vp]),
     "kmc_loop_init": (_int, [_vp, ctypes.c_double, _i64, _i64, ctypes.c_double, _int, _vp]),
     "kmc_lloyd": (_int, [_vp, _i64, _int, _vp, _vp, _int, _vp, _i64, _vp, _u, _vp, _sz, _vp, _vp, _int, _vp, _sz,

@@ -84,6 +84,14 @@ class Dataset:
 
     TC_MIN_DIMS = 32                # from here up the assign runs on the tensor cores (kmc_pass_split)
     APPROX_MIN_DIMS = 64            # exact=False from here up (core.py:1030-1034 / 2036-2041: below, exact is as fast)
+    # per-center bounds (kmc_pass_elkan) on request (Dataset.elkan = True): while n k halves fit, and dropped by a
+    # pass that visits more than 5% of the (row, center) pairs (the reference's BOUNDS_MAX_BYTES / BOUNDS_MAX_VISITED,
+    # core.py:513-516).  Not by default: the bounded pass computes each visited distance on CUDA cores from the
+    # center's float32 vector, which at configuration 4 costs more than the dense tensor-core pass until far fewer
+    # than 1% of the pairs are visited (measured: 93% visited at step 5 of a fit, 2.7% at step 20, 16.9 ms against
+    # 4.1 ms for the dense pass there)
+    ELKAN_MAX_BYTES = 16 << 30
+    ELKAN_MAX_VISITED = 0.05
 
     def __init__(self, parts, group=None, device=None, tensor_cores=None, label_rule="float64"):
         if isinstance(parts, (torch.Tensor, np.ndarray)) or not isinstance(parts, (list, tuple)):
@@ -116,6 +124,8 @@ class Dataset:
         self._split = None
         self._csplit = {}
         self._xch = {}                  # per k: peer-memory exchange of the totals (multi-GPU), or False: NCCL
+        self._elkan = {}                # per k: per-center bounds of the tensor-core pass and their policy state
+        self.elkan = False              # True: per-center bounds between bounded tensor-core passes
 
     # -- per-dataset state
     @property
@@ -199,6 +209,38 @@ class Dataset:
         for bb in self._bounds.values():
             for t, _ in bb:
                 _lib.call("kmc_bounds_reset", _ptr(t), _stream())
+        for e in self._elkan.values():
+            e["valid"], e["cool"], e["wait"] = False, 0, 0
+
+    # -- per-center bounds of the tensor-core shapes (kmc_pass_elkan), one buffer per slice and k
+    def elkan_ok(self, k):
+        return (self.elkan is True and self.tensor_cores and k % 8 == 0 and
+                self.n_local * k * 2 <= self.ELKAN_MAX_BYTES)
+
+    def elkan_state(self, k):
+        e = self._elkan.get(k)
+        if e is None:
+            L = _lib.load()
+            bufs = []
+            for p in self.parts:
+                nb = int(L.kmc_elkan_bytes(p.shape[0], self.d, k))
+                bufs.append((torch.empty(nb, dtype=torch.uint8, device=self.device), nb))
+            e = dict(bufs=bufs, valid=False, cool=0, wait=0, used=False)
+            self._elkan[k] = e
+        return e
+
+    def elkan_after(self, k, stats):
+        """After a step: drop bounds that visited too many pairs, and wait longer each time that happens (1, 3,
+        7 passes) before building them again -- on data where they cannot pay they cost a build now and then."""
+        e = self._elkan.get(k)
+        if e is None or not e["used"]:
+            return
+        if stats["screened"] > self.ELKAN_MAX_VISITED * self.n_local * k:
+            e["valid"] = False
+            e["cool"] = min(2 * e["cool"] + 1, 7)
+            e["wait"] = e["cool"]
+        else:
+            e["cool"] = 0
 
     # -- the all-reduce of the totals over the ranks
     def _exchange(self, k):
@@ -287,13 +329,27 @@ class Dataset:
         if not generic and self.uses_approx(approx):
             flags |= _lib.KMC_PASS_APPROX
         st = _stream()
-        bb = self.bounds(k) if bounded and not labels and not generic else None
+        want_bounds = bounded and not labels and not generic
         tc = self.tensor_cores and not generic
+        bb = self.bounds(k) if want_bounds and not tc else None
+        eb = None
         if tc:
-            bb = None
             sp, cs = self.split(), self.csplit(k)
+            if want_bounds and self.elkan_ok(k) and not (flags & _lib.KMC_PASS_APPROX):
+                eb = self.elkan_state(k)
+                eb["used"] = False
+                if not eb["valid"] and eb["wait"] > 0:
+                    eb["wait"] -= 1
+                    eb = None
+            bb = None
         for i, p in enumerate(self.parts):
-            if tc:
+            if tc and eb is not None:
+                ebuf, ebytes = eb["bufs"][i]
+                _lib.call("kmc_pass_elkan", _ptr(p), p.shape[0], self.d, _ptr(C), k, _ptr(cm), self.n_total,
+                          _ptr(b["totals"]), _ptr(lab[i]) if labels else None, _ptr(bst[i]) if labels else None,
+                          flags | (0 if eb["valid"] else _lib.KMC_PASS_ELKAN_BUILD), _ptr(sp[i][0]), sp[i][1],
+                          _ptr(cs[0]), cs[1], _ptr(ebuf), ebytes, _ptr(b["ws"]), b["wsb"], st)
+            elif tc:
                 _lib.call("kmc_pass_split", _ptr(p), p.shape[0], self.d, _ptr(C), k, _ptr(cm), self.n_total,
                           _ptr(b["totals"]), _ptr(lab[i]) if labels else None, _ptr(bst[i]) if labels else None,
                           flags, _ptr(sp[i][0]), sp[i][1], _ptr(cs[0]), cs[1], _ptr(b["ws"]), b["wsb"], st)
@@ -305,6 +361,9 @@ class Dataset:
                           _ptr(b["totals"]), _ptr(lab[i]) if labels else None, _ptr(bst[i]) if labels else None,
                           flags, _ptr(b["ws"]), b["wsb"], st)
             flags = flags | _lib.KMC_PASS_ACCUMULATE
+        if eb is not None:
+            eb["used"] = eb["valid"]              # this pass used the bounds (a build pass visits nothing)
+            eb["valid"] = True
         if reduce:
             self.allreduce_totals(b, k)
         return b
@@ -335,6 +394,7 @@ class Dataset:
         s = self.read_stats(b)
         if s["flags"] & 2:
             raise RuntimeError("the all-reduce of the totals timed out waiting for a peer GPU")
+        self.elkan_after(k, s)
         if s["needs_reloc"]:
             s = self._relocate(C, b, s["n_empty"], generic, rule, approx)
         return b["C_new"], s

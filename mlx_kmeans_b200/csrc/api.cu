@@ -349,11 +349,14 @@ int kmc_split_rows(const float* X, int64_t n, int d, void* split, size_t split_b
     return KMC_OK;
 }
 
-int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, const uint32_t* colmax,
-                   int64_t n_total, int64_t* totals, int32_t* labels, float* best, unsigned flags, void* split,
-                   size_t split_bytes, void* csplit, size_t csplit_bytes, void* workspace, size_t ws_bytes,
-                   void* stream) {
-    const char* who = "kmc_pass_split";
+}  // extern "C"
+
+// kmc_pass_split and kmc_pass_elkan: elkan == nullptr for a plain tensor-core pass; else the per-center bounds,
+// built by the tensor-core pass (flags & KMC_PASS_ELKAN_BUILD) or used by the bounded pass.
+static int tc_pass_impl(const char* who, const float* X, int64_t n, int d, const float* C, int k,
+                        const uint32_t* colmax, int64_t n_total, int64_t* totals, int32_t* labels, float* best,
+                        unsigned flags, void* split, size_t split_bytes, void* csplit, size_t csplit_bytes,
+                        void* elkan, void* workspace, size_t ws_bytes, void* stream) {
     if (int s = check_shape(n, d, k)) return s;
     if (!C || !colmax || !totals || !workspace || !split || !csplit || (n > 0 && !X))
         return fail(KMC_ERR_INVALID, "%s: null pointer", who);
@@ -398,7 +401,24 @@ int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, cons
     ts.dump = nullptr;
     ts.rule = rule;
     ts.approx = (flags & KMC_PASS_APPROX) ? 1 : 0;
-    e = launch_assign_tc(ts, st);
+    ts.lb = nullptr;
+    ts.xsq_lo = rs.xsq_lo;
+    if (elkan) {
+        const ElkanState es = carve_elkan(elkan, n, d, k);
+        if (flags & KMC_PASS_ELKAN_BUILD) {            // a full pass that also writes every bound
+            ts.lb = es.lb;
+            e = launch_assign_tc(ts, st);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(es.cprev, C, sizeof(float) * (size_t)k * d, cudaMemcpyDeviceToDevice, st);
+        } else {                                       // the bounded pass: drift, then the rows
+            e = launch_elkan_drift(C, es, k, d, st);
+            // rows in the grouped order the previous pass's scatter left in rs.perm (every pass on the split ends with it)
+            if (e == cudaSuccess)
+                e = launch_elkan(X, n, d, C, k, es, rs.lab, rs.cands, rs.perm, ws.prep, ws.counters, st);
+        }
+    } else {
+        e = launch_assign_tc(ts, st);
+    }
     if (e != cudaSuccess) return cuda_fail(e, who);
     PassArgs a;
     a.X = X;
@@ -422,6 +442,34 @@ int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, cons
     e = launch_accum_split(a, rs, cs, st);
     if (e != cudaSuccess) return cuda_fail(e, who);
     return KMC_OK;
+}
+
+extern "C" {
+
+int kmc_pass_split(const float* X, int64_t n, int d, const float* C, int k, const uint32_t* colmax,
+                   int64_t n_total, int64_t* totals, int32_t* labels, float* best, unsigned flags, void* split,
+                   size_t split_bytes, void* csplit, size_t csplit_bytes, void* workspace, size_t ws_bytes,
+                   void* stream) {
+    return tc_pass_impl("kmc_pass_split", X, n, d, C, k, colmax, n_total, totals, labels, best,
+                        flags & ~(unsigned)KMC_PASS_ELKAN_BUILD, split, split_bytes, csplit, csplit_bytes, nullptr,
+                        workspace, ws_bytes, stream);
+}
+
+size_t kmc_elkan_bytes(int64_t n, int d, int k) { return elkan_bytes(n, d, k); }
+
+int kmc_pass_elkan(const float* X, int64_t n, int d, const float* C, int k, const uint32_t* colmax, int64_t n_total,
+                   int64_t* totals, int32_t* labels, float* best, unsigned flags, void* split, size_t split_bytes,
+                   void* csplit, size_t csplit_bytes, void* elkan, size_t elkan_bytes_, void* workspace,
+                   size_t ws_bytes, void* stream) {
+    const char* who = "kmc_pass_elkan";
+    if (int s = check_shape(n, d, k)) return s;
+    if (!elkan) return fail(KMC_ERR_INVALID, "%s: null bounds", who);
+    if (k % 8) return fail(KMC_ERR_UNSUPPORTED, "%s: k = %d, the bounds need k to be a multiple of 8", who, k);
+    if (flags & KMC_PASS_APPROX) return fail(KMC_ERR_INVALID, "%s: the bounds are for the exact pass", who);
+    if (elkan_bytes_ < elkan_bytes(n, d, k))
+        return fail(KMC_ERR_INVALID, "%s: bounds of %zu bytes, need %zu", who, elkan_bytes_, elkan_bytes(n, d, k));
+    return tc_pass_impl(who, X, n, d, C, k, colmax, n_total, totals, labels, best, flags, split, split_bytes, csplit,
+                        csplit_bytes, elkan, workspace, ws_bytes, stream);
 }
 
 int kmc_tc_dot(const float* C, int64_t n, int d, int k, void* split, size_t split_bytes, void* csplit,
@@ -456,6 +504,8 @@ int kmc_tc_dot(const float* C, int64_t n, int d, int k, void* split, size_t spli
     ts.dump = out;
     ts.rule = 0;
     ts.approx = 0;
+    ts.lb = nullptr;
+    ts.xsq_lo = rs.xsq_lo;
     e = launch_assign_tc(ts, st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(error, cs.error, sizeof(int), cudaMemcpyDeviceToDevice, st);
     if (e != cudaSuccess) return cuda_fail(e, who);

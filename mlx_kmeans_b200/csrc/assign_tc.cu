@@ -27,6 +27,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cuda_fp16.h>
+
 #include <type_traits>
 
 #include "common.cuh"
@@ -198,6 +200,8 @@ struct TcArgs {
     int* error;              // set on a barrier timeout
     float* dump;             // (kmc_tc_dot) n x k: every accumulated x.c as read from TMEM, or nullptr
     float wr;                // window term per (|x| + max|c|)^2: the rounding of the label rule's distance
+    __half* lb;              // (Elkan bounds, built here) n x k: a lower bound on every row-center distance, or nullptr
+    const float* xsq_lo;     // n: |x|^2 rounded down (with lb)
 };
 
 // The smallest score and its center (exact=False: no window, so the rest of the order is not needed); the same
@@ -389,7 +393,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         int it = 0;                                       // tiles done: the hand-over slot alternates with it
         for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, it++) {
             const int64_t row = t * BM + 32 * q + lane;
-            const float xr = (h == 0 && row < a.n) ? __ldg(a.xn + row) : 0.0f;   // in flight meanwhile
+            const float xr = ((h == 0 || a.lb) && row < a.n) ? __ldg(a.xn + row) : 0.0f;   // in flight meanwhile
+            // Elkan bounds of this row (a.lb): |x - c|^2 = |x|^2 + 2 (|c|^2/2 - x.c) >= xsq_lo + 2 (score - err), err
+            // the score's error bound of the window below (E |x| max|c| + 2^-24 max|c|^2, with a margin), every
+            // step rounded down, then the square root rounded down and stored as half rounded toward zero
+            float lb_x = 0.0f, lb_err = 0.0f;
+            if (a.lb && row < a.n) {
+                const float cm = *a.cmax;
+                lb_x = __ldg(a.xsq_lo + row);
+                lb_err = __fmul_ru(__fadd_ru(__fmul_ru(__fmul_ru((float)(3.1 / 65536.0 + 3.0 * a.dp / 16777216.0), xr), cm),
+                                             __fmul_ru(__fmul_ru(cm, cm), 1.0f / 16777216.0f)),
+                                   1.0f + 1.0f / 1024.0f);
+            }
             using Trk = std::conditional_t<APPROX, Top1, Top3>;
             Trk ev, od;                                   // even and odd columns: two independent chains
             ev.init();
@@ -403,6 +418,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     float v[32];
                     tmem_ld32(lane_base + abuf * BN + cc, v);
                     const int c0 = nt * BN + cc;
+                    if (a.lb != nullptr && row < a.n) {            // the Elkan bounds of these 32 centers
+                        __half hv[32];
+#pragma unroll
+                        for (int j = 0; j < 32; j++) {
+                            const float sc = __fsub_rd(__fsub_rd(__ldg(a.hs + c0 + j), v[j]), lb_err);
+                            const float d2 = __fmaf_rd(2.0f, sc, lb_x);
+                            hv[j] = __float2half_rz(d2 > 0.0f ? __fsqrt_rd(d2) : 0.0f);
+                        }
+                        __half* dst = a.lb + row * a.k + c0;
+                        if (c0 + 32 <= a.k) {                      // k % 8 == 0: 16-byte aligned pieces
+#pragma unroll
+                            for (int g = 0; g < 4; g++)
+                                reinterpret_cast<uint4*>(dst)[g] = reinterpret_cast<const uint4*>(hv)[g];
+                        } else {
+                            for (int j = 0; j < 32 && c0 + j < a.k; j++) dst[j] = hv[j];
+                        }
+                    }
                     if (a.dump != nullptr && row < a.n) {          // diagnostic copy of the raw scores
 #pragma unroll 1
                         for (int j = 0; j < 32; j++)
@@ -521,6 +553,8 @@ cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
     a.error = s.error;
     a.dump = s.dump;
     a.wr = (float)(1.0 / 1099511627776.0 + (s.rule ? rule32_coef(s.dp) : 0.0));
+    a.lb = static_cast<__half*>(s.lb);
+    a.xsq_lo = s.xsq_lo;
     const int64_t tiles = (s.n + BM - 1) / BM;
     int64_t grid = num_sms();
     if (grid > tiles) grid = tiles;

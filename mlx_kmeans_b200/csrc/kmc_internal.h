@@ -87,6 +87,7 @@ struct RowSplit {
     uint32_t* perm;           // n: rows grouped by label (before that: the rows the tensor-core kernel flagged)
     int4* cands;              // n: each flagged row's candidate centers (x, y; w = -2: more than two)
     uint32_t* ovf;            // n: flagged rows with more than two candidates
+    float* xsq_lo;            // n: |x|^2 rounded down (the Elkan bounds' lower bound on distances)
 };
 // ... and per-pass center operands
 struct CenterSplit {
@@ -114,6 +115,8 @@ struct TcSplit {
     float* dump;              // kmc_tc_dot: n x k raw scores x.c, or nullptr
     int rule;                 // label rule (Prep::rule): widens the window
     int approx;               // exact=False: one bf16 MMA per product (hi parts), no window
+    void* lb;                 // Elkan bounds to build (n x k half), or nullptr
+    const float* xsq_lo;      // n: |x|^2 rounded down (with lb)
 };
 int split_dp(int d);
 int split_kp(int k);
@@ -126,6 +129,19 @@ cudaError_t launch_split_rows(const float* X, int64_t n, int d, const RowSplit& 
 cudaError_t launch_split_centers(const float* C, int k, int d, const CenterSplit& s, cudaStream_t st);
 cudaError_t launch_assign_tc(const TcSplit& s, cudaStream_t st);
 cudaError_t launch_accum_split(PassArgs a, const RowSplit& rs, const CenterSplit& cs, cudaStream_t st);
+
+// Per-center lower bounds between passes for the tensor-core shapes (elkan.cu): caller memory
+// [centers the bounds refer to: k x d float][drift: k float][bounds: n x k half].
+struct ElkanState {
+    float* cprev;
+    float* drift;
+    void* lb;
+};
+size_t elkan_bytes(int64_t n, int d, int k);
+ElkanState carve_elkan(void* base, int64_t n, int d, int k);
+cudaError_t launch_elkan_drift(const float* C, const ElkanState& e, int k, int d, cudaStream_t st);
+cudaError_t launch_elkan(const float* X, int64_t n, int d, const float* C, int k, const ElkanState& e, int32_t* lab,
+                         int4* cands, const uint32_t* order, const Prep* prep, long long* counters, cudaStream_t st);
 
 // Peer-memory all-reduce of the totals (exchange.cu).
 constexpr int kExchangeHeader = 512;      // 64 flags of 8 bytes before the two slots

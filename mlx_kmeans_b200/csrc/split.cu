@@ -41,12 +41,12 @@ __device__ __forceinline__ void split_bf16(float v, __nv_bfloat16& h, __nv_bfloa
 __global__ void __launch_bounds__(kSplitThreads) k_split_rows(const float* __restrict__ X, int64_t n, int d, int dp,
                                                              __nv_bfloat16* __restrict__ xh,
                                                              __nv_bfloat16* __restrict__ xl,
-                                                             float* __restrict__ xn) {
+                                                             float* __restrict__ xn, float* __restrict__ xsq_lo) {
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t)gridDim.x * (kSplitThreads / 32);
     for (int64_t r = (int64_t)blockIdx.x * (kSplitThreads / 32) + (threadIdx.x >> 5); r < n; r += warps) {
         const float* x = X + r * d;
-        double s = 0.0;
+        double s = 0.0, sd = 0.0;                         // |x|^2 rounded up and rounded down
         for (int j = lane; j < dp; j += 32) {
             const float v = j < d ? x[j] : 0.0f;
             __nv_bfloat16 h, l;
@@ -54,10 +54,17 @@ __global__ void __launch_bounds__(kSplitThreads) k_split_rows(const float* __res
             xh[r * dp + j] = h;
             xl[r * dp + j] = l;
             s = __fma_ru((double)v, (double)v, s);
+            sd = __fma_rd((double)v, (double)v, sd);
         }
 #pragma unroll
-        for (int o = 16; o; o >>= 1) s = __dadd_ru(s, __shfl_xor_sync(0xffffffffu, s, o));
-        if (lane == 0) xn[r] = __double2float_ru(__dsqrt_ru(s));
+        for (int o = 16; o; o >>= 1) {
+            s = __dadd_ru(s, __shfl_xor_sync(0xffffffffu, s, o));
+            sd = __dadd_rd(sd, __shfl_xor_sync(0xffffffffu, sd, o));
+        }
+        if (lane == 0) {
+            xn[r] = __double2float_ru(__dsqrt_ru(s));
+            xsq_lo[r] = __double2float_rd(sd);
+        }
     }
 }
 
@@ -715,7 +722,7 @@ int split_kp(int k) { return (k + tc_block_n(k) - 1) / tc_block_n(k) * tc_block_
 
 size_t split_rows_bytes(int64_t n, int d) {
     const int64_t nn = n > 0 ? n : 1, dp = split_dp(d);
-    return (size_t)(2 * a256(nn * dp * 2) + 4 * a256(nn * 4) + a256(nn * 16));
+    return (size_t)(2 * a256(nn * dp * 2) + 5 * a256(nn * 4) + a256(nn * 16));
 }
 
 size_t split_centers_bytes(int d, int k) {
@@ -734,6 +741,7 @@ RowSplit carve_rows(void* base, int64_t n, int d) {
     s.perm = reinterpret_cast<uint32_t*>(p + 2 * a256(nn * dp * 2) + 2 * a256(nn * 4));
     s.ovf = reinterpret_cast<uint32_t*>(p + 2 * a256(nn * dp * 2) + 3 * a256(nn * 4));
     s.cands = reinterpret_cast<int4*>(p + 2 * a256(nn * dp * 2) + 4 * a256(nn * 4));
+    s.xsq_lo = reinterpret_cast<float*>(p + 2 * a256(nn * dp * 2) + 4 * a256(nn * 4) + a256(nn * 16));
     return s;
 }
 
@@ -780,7 +788,7 @@ cudaError_t launch_split_rows(const float* X, int64_t n, int d, const RowSplit& 
     const int64_t cap = (int64_t)num_sms() * 16;
     if (blocks > cap) blocks = cap;
     k_split_rows<<<(int)blocks, kSplitThreads, 0, st>>>(X, n, d, split_dp(d), static_cast<__nv_bfloat16*>(s.xh),
-                                                         static_cast<__nv_bfloat16*>(s.xl), s.xn);
+                                                         static_cast<__nv_bfloat16*>(s.xl), s.xn, s.xsq_lo);
     return cudaGetLastError();
 }
 
