@@ -20,9 +20,10 @@
 //            tcgen05.commit frees the stage and, after the last chunk, hands the accumulator to the epilogue.
 //   warps 2-9  epilogue: two warps per TMEM lane quarter, one per half of the accumulator's columns; a thread
 //            owns one row (TMEM lane), reads its scores 32 columns at a time (tcgen05.ld) and keeps the two
-//            best scores with their centers (lowest index first on ties) and the third best score, in two
-//            interleaved branch-free trackers; at the end of the row tile the pair merges its halves through
-//            shared memory and writes label | flag << 31 and, for a flagged row, its candidates.
+//            best scores with their centers (lowest index first on ties) and the third best score (or a
+//            lower bound on it), score by score in two interleaved chains (Top3) or, with many centers, a
+//            chunk at a time (TopC); at the end of the row tile the pair merges its halves through shared
+//            memory and writes label | flag << 31 and, for a flagged row, its candidates.
 // Every wait on an mbarrier is bounded; on a timeout the CTA records an error, stops its loops and frees TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -204,6 +205,116 @@ struct TcArgs {
     const float* xsq_lo;     // n: |x|^2 rounded down (with lb)
 };
 
+// 1 if x != 0 (or infinite), 0 if x == 0: x * 2^127 is at least 2^-22 for any nonzero float, and the second
+// product saturates to 1 (the FMA pipe's .sat clamp; a NaN gives 0, which only a row flagged for the full
+// decision can hold).
+__device__ __forceinline__ float nonzero01(float x) {
+    float r;
+    asm("mul.rn.sat.f32 %0, %1, 0f7F000000;" : "=f"(r) : "f"(__fmul_rn(x, 0x1p127f)));
+    return r;
+}
+
+// Position of the first s[j] equal to m among 32 scores, as a float (32 if none), in FMA-pipe arithmetic only:
+// with ne_j = [s_j != m], the number of leading unequal scores is ne_0 (1 + ne_1 (1 + ne_2 (...))), one fused
+// multiply-add per score, over four segments of 8 joined by [segment all unequal] = sat(h - 7).  ABS compares
+// |s_j - m| (scores below m present); without it every s_j >= m.
+template <bool ABS>
+__device__ __forceinline__ float first_equal(const float (&s)[32], float m) {
+    float h[4];
+#pragma unroll
+    for (int g = 0; g < 4; g++) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int j = 7; j >= 0; j--) {
+            const float d = s[8 * g + j] - m;
+            const float ne = nonzero01(ABS ? fabsf(d) : d);
+            acc = fmaf(ne, acc, ne);
+        }
+        h[g] = acc;
+    }
+    float p = fmaf(__saturatef(h[2] - 7.0f), h[3], h[2]);
+    p = fmaf(__saturatef(h[1] - 7.0f), p, h[1]);
+    return fmaf(__saturatef(h[0] - 7.0f), p, h[0]);
+}
+
+// The two smallest scores with their centers and a lower bound on the third smallest, fed a 32-column chunk at
+// a time.  A tournament gives the chunk's two smallest values (pairs by min / max, then min(max(a0, b0),
+// min(a1, b1)) for the second; equal values are kept), 92 compare operations for 32 scores; the chunk's
+// smallest is located (first occurrence) only when it enters the top two, by first_equal on the FMA pipe, and
+// its second only when both enter.  Ties keep the lower index: earlier chunks hold lower indices, a chunk value
+// equal to a kept one does not displace it, and within a chunk the first occurrence comes first.  The third
+// smallest of the union is min(m2, max(m1, mc), t) with t the chunk's third; t >= sc is not computed and sc
+// stands for it, so m2 is exact unless the chunk holds the row's three smallest, and never above the true third
+// (a row inside the window then goes to the full decision rather than the two-candidate one).  Scores must be
+// finite for the positions to be exact; a row with a non-finite score has a non-finite window and goes to the
+// full decision, and positions are clamped to the chunk so a label stays in range.
+struct TopC {
+    float m0, m1, m2;
+    int l0, l1;
+    __device__ __forceinline__ void init() {
+        m0 = m1 = m2 = INFINITY;
+        l0 = l1 = 0;
+    }
+    __device__ __forceinline__ void chunk(const float (&s)[32], int cb) {
+        float a[16], b[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            a[i] = fminf(s[2 * i], s[2 * i + 1]);
+            b[i] = fmaxf(s[2 * i], s[2 * i + 1]);
+        }
+#pragma unroll
+        for (int w = 8; w >= 1; w >>= 1) {
+#pragma unroll
+            for (int i = 0; i < w; i++) {
+                const float lo = fminf(a[i], a[i + w]);
+                b[i] = fminf(fmaxf(a[i], a[i + w]), fminf(b[i], b[i + w]));
+                a[i] = lo;
+            }
+        }
+        const float mc = a[0], sc = b[0];
+        m2 = fminf(fminf(m2, sc), fmaxf(m1, mc));
+        if (mc < m1) {                                   // the chunk's smallest enters the top two
+            const int pm = (int)fminf(first_equal<false>(s, mc), 31.0f);
+            if (mc < m0) {
+                if (m0 <= sc) {                          // second: the previous smallest
+                    m1 = m0;
+                    l1 = l0;
+                } else {                                 // second: the chunk's second smallest
+                    int ps;
+                    if (sc != mc) {
+                        ps = (int)fminf(first_equal<true>(s, sc), 31.0f);
+                    } else {                             // a tie inside the chunk: its second occurrence
+                        ps = 32;
+#pragma unroll
+                        for (int j = 31; j >= 0; j--) ps = (j > pm && s[j] == mc) ? j : ps;
+                        ps = min(ps, 31);
+                    }
+                    m1 = sc;
+                    l1 = cb + ps;
+                }
+                m0 = mc;
+                l0 = cb + pm;
+            } else {                                     // m0 <= mc < m1
+                m1 = mc;
+                l1 = cb + pm;
+            }
+        }
+    }
+    __device__ __forceinline__ void push_ordered(float s, int c) {
+        const bool a0 = s < m0 || (s == m0 && c < l0), a1 = s < m1 || (s == m1 && c < l1), a2 = s < m2;
+        m2 = a1 ? m1 : (a2 ? s : m2);
+        m1 = a0 ? m0 : (a1 ? s : m1);
+        l1 = a0 ? l0 : (a1 ? c : l1);
+        m0 = a0 ? s : m0;
+        l0 = a0 ? c : l0;
+    }
+    __device__ __forceinline__ void merge(float n0, int k0, float n1, int k1, float n2) {
+        push_ordered(n0, k0);
+        push_ordered(n1, k1);
+        if (n2 < m2) m2 = n2;
+    }
+};
+
 // The smallest score and its center (exact=False: no window, so the rest of the order is not needed); the same
 // interface as Top3 with m1 = m2 = +inf.
 struct Top1 {
@@ -226,7 +337,7 @@ struct Top1 {
     }
 };
 
-template <int BN, bool AR, bool APPROX>
+template <int BN, bool AR, bool APPROX, bool CHUNK>
 __global__ void __launch_bounds__(kTcThreads, 1)
     k_assign_tc(const __grid_constant__ CUtensorMap mxh, const __grid_constant__ CUtensorMap mxl,
                 const __grid_constant__ CUtensorMap mch, const __grid_constant__ CUtensorMap mcl, TcArgs a) {
@@ -405,8 +516,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                              __fmul_ru(__fmul_ru(cm, cm), 1.0f / 16777216.0f)),
                                    1.0f + 1.0f / 1024.0f);
             }
-            using Trk = std::conditional_t<APPROX, Top1, Top3>;
-            Trk ev, od;                                   // even and odd columns: two independent chains
+            using Trk = std::conditional_t<APPROX, Top1, std::conditional_t<CHUNK, TopC, Top3>>;
+            Trk ev, od;                                   // per score: even and odd columns in two chains
             ev.init();
             od.init();
             for (int nt = 0; nt < ntiles && ok; nt++) {
@@ -432,18 +543,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             for (int g = 0; g < 4; g++)
                                 reinterpret_cast<uint4*>(dst)[g] = reinterpret_cast<const uint4*>(hv)[g];
                         } else {
-                            for (int j = 0; j < 32 && c0 + j < a.k; j++) dst[j] = hv[j];
+#pragma unroll
+                            for (int j = 0; j < 32; j++)
+                                if (c0 + j < a.k) dst[j] = hv[j];
                         }
                     }
                     if (a.dump != nullptr && row < a.n) {          // diagnostic copy of the raw scores
-#pragma unroll 1
+#pragma unroll
                         for (int j = 0; j < 32; j++)
                             if (c0 + j < a.k) a.dump[row * a.k + c0 + j] = v[j];
                     }
+                    // scores |c|^2/2 - x.c (hs 16-byte aligned: its base is, and c0 is a multiple of 32)
 #pragma unroll
-                    for (int j = 0; j < 32; j += 2) {
-                        ev.push(__ldg(a.hs + c0 + j) - v[j], c0 + j);
-                        od.push(__ldg(a.hs + c0 + j + 1) - v[j + 1], c0 + j + 1);
+                    for (int g = 0; g < 8; g++) {
+                        const float4 hq = __ldg(reinterpret_cast<const float4*>(a.hs + c0) + g);
+                        v[4 * g] = hq.x - v[4 * g];
+                        v[4 * g + 1] = hq.y - v[4 * g + 1];
+                        v[4 * g + 2] = hq.z - v[4 * g + 2];
+                        v[4 * g + 3] = hq.w - v[4 * g + 3];
+                    }
+                    if constexpr (!CHUNK) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 2) {
+                            ev.push(v[j], c0 + j);
+                            od.push(v[j + 1], c0 + j + 1);
+                        }
+                    } else {
+                        ev.chunk(v, c0);
                     }
                 }
                 tc_fence_before();
@@ -451,7 +577,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 abuf ^= 1u;
                 if (abuf == 0) aphase ^= 1u;
             }
-            ev.merge(od.m0, od.l0, od.m1, od.l1, od.m2);
+            if constexpr (!CHUNK) ev.merge(od.m0, od.l0, od.m1, od.l1, od.m2);
             float* slot = epi + ((((it & 1) * 4 + q) * 32 + lane) * 5);
             if (h == 1) {
                 slot[0] = ev.m0;
@@ -524,7 +650,7 @@ bool make_map(CUtensorMap* m, const void* base, int64_t rows, int dp, int box_ro
     return r == CUDA_SUCCESS;
 }
 
-template <int BN, bool AR, bool APPROX>
+template <int BN, bool AR, bool APPROX, bool CHUNK = false>
 cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
     CUtensorMap mxh, mxl, mch, mcl;
     if (!make_map(&mxh, s.xh, s.n, s.dp, BM) || !make_map(&mxl, s.xl, s.n, s.dp, BM) ||
@@ -535,7 +661,7 @@ cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
     cudaGetDevice(&dev);
     const size_t smem = TcSmem<BN, AR, APPROX>::total;
     if (!(configured >> (dev & 63) & 1ull)) {
-        cudaError_t e = cudaFuncSetAttribute(k_assign_tc<BN, AR, APPROX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(k_assign_tc<BN, AR, APPROX, CHUNK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
         if (e != cudaSuccess) return e;
         configured |= 1ull << (dev & 63);
@@ -559,13 +685,23 @@ cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
     int64_t grid = num_sms();
     if (grid > tiles) grid = tiles;
     if (grid < 1) grid = 1;
-    k_assign_tc<BN, AR, APPROX><<<(int)grid, kTcThreads, smem, st>>>(mxh, mxl, mch, mcl, a);
+    k_assign_tc<BN, AR, APPROX, CHUNK><<<(int)grid, kTcThreads, smem, st>>>(mxh, mxl, mch, mcl, a);
     return cudaGetLastError();
 }
+
+// The per-chunk tracker (TopC) pays off with many chunks per row, used from 32 chunks of 32 columns per epilogue
+// thread (2048 centers): against the per-score one it measured 25% faster at 50M x 128, k = 4096, level at
+// 1M x 768, k = 1024, and 40% slower at 10M x 32, k = 64 (one chunk per thread, where the tournament and its
+// lookups outweigh 32 pushes).
+constexpr int kChunkTrackerMinK = 2048;
 
 template <int BN>
 cudaError_t run_tc_ar(const TcSplit& s, bool ar, cudaStream_t st) {
     if (s.approx) return ar ? run_tc<BN, true, true>(s, st) : run_tc<BN, false, true>(s, st);
+    if constexpr (BN == 256) {
+        if (s.kp >= kChunkTrackerMinK)
+            return ar ? run_tc<BN, true, false, true>(s, st) : run_tc<BN, false, false, true>(s, st);
+    }
     return ar ? run_tc<BN, true, false>(s, st) : run_tc<BN, false, false>(s, st);
 }
 

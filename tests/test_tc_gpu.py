@@ -70,7 +70,7 @@ def _embeddings(n, d, k_true, seed):
 
 
 @pytest.mark.parametrize("n,d,k", [(20_000, 768, 300), (3_001, 100, 600), (50_000, 128, 512), (4_000, 64, 64),
-                                   (30_000, 32, 64), (5_000, 20, 40)])
+                                   (30_000, 32, 64), (5_000, 20, 40), (8_000, 64, 2100), (5_000, 72, 4096)])
 def test_tc_matches_cuda_core_pass(n, d, k, cuda_device):
     """Ragged row tiles, padded columns, several (padded) center tiles: labels and totals identical to the
     CUDA-core pass, labels identical to the float64 oracle."""
@@ -129,19 +129,25 @@ def test_tc_lloyd_step_and_slices(cuda_device):
     assert np.array_equal(outs[0], outs[1])
 
 
-def test_tc_many_equal_centers(cuda_device):
-    """Six copies of one center: rows near it have six exact ties, more candidates than the tensor-core kernel
-    keeps (two), so they take the full float64 decision; the label is the lowest index, as in the oracle."""
+@pytest.mark.parametrize("k,copies", [(40, [3, 9, 10, 17, 30, 31]), (2500, [3, 9, 10, 700, 2047, 2400]),
+                                      (2500, [5, 6]), (2500, [5, 1500]), (4096, [4095, 31, 32, 2048])])
+def test_tc_many_equal_centers(k, copies, cuda_device):
+    """Copies of one center: rows near it have exact ties.  Two copies are two candidates (decided in float64
+    between them, or in full when the per-chunk tracker of many centers finds both in one 32-column chunk), more
+    than two take the full float64 decision; the label is the lowest index, as in the oracle.  With 2048 centers
+    and more the kernel keeps its top two a chunk at a time (copies in one chunk, in neighbouring chunks, in the
+    last and first chunks of the row)."""
     import torch
     rng = np.random.default_rng(5)
     X = rng.standard_normal((5_000, 64)).astype(np.float32)
-    C = rng.standard_normal((40, 64)).astype(np.float32)
-    C[[3, 9, 10, 17, 30, 31]] = 0.05 * rng.standard_normal(64).astype(np.float32)
+    C = rng.standard_normal((k, 64)).astype(np.float32) * (1.0 + 0.01 * (k > 100))
+    C[copies] = 0.05 * rng.standard_normal(64).astype(np.float32)
     ds = _ds(X, cuda_device)
     out = ds.assign(torch.from_numpy(C).to(cuda_device), return_labels=True)
     ref, _, _ = O.assign(X, C)
     assert np.array_equal(out[3], ref)
-    assert (ref == 3).sum() > 0 and not np.isin(ref, [9, 10, 17, 30, 31]).any()
+    low = min(copies)
+    assert (ref == low).sum() > 0 and not np.isin(ref, [c for c in copies if c != low]).any()
 
 
 @pytest.mark.parametrize("d", [3, 7, 8, 31, 32, 100, 128, 129, 136, 200, 255, 513, 768, 1000, 4096])
