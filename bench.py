@@ -280,11 +280,13 @@ def main():
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     clocks = Clocks(vis.split(",")[local] if vis else str(local))
 
+    clocks.start()
+    time.sleep(0.2)
+    # the barrier right before the first timed launch: a rank that starts late would otherwise keep the others
+    # waiting in the first step's exchange, and that start-up skew would count as step time
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks.start()
-    time.sleep(0.2)
     t0.record(st)
     h0 = time.perf_counter()
     for i in range(K):

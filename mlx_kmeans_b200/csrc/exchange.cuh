@@ -7,9 +7,13 @@
 // same as NCCL's and the same on every rank.
 //
 // Exchange buffer of a rank (kmc_exchange_alloc; the peers map it through CUDA IPC):
-//   [flags: 64 x uint64; flag r = the last step rank r has published]  [slot 0: W int64]  [slot 1: W int64]
-// Step s publishes into slot s & 1.  A rank writes slot s & 1 again at step s + 2 only after it has seen every
-// peer's flag for step s + 1, which each peer raises after it finished reading step s: two slots suffice.
+//   [flags: 64 rows x 64 uint64; flag (b, r) = the last step rank r has published through row b]
+//   [slot 0: W int64]  [slot 1: W int64]
+// Step s publishes into slot s & 1.  One CTA exchanges a range of the totals through one flag row: row 0 and
+// every value for narrow totals, CTA b of the wide exchange (k_exchange_wide) row b and the b-th range.  A rank
+// writes slot s & 1 again at step s + 2 only after it has seen, in some row, every peer's flag for step s + 1;
+// a peer raises a flag for step s + 1 in a kernel that starts after its step-s kernel (every CTA of it) finished
+// reading, so two slots suffice whichever rows the steps used.
 #pragma once
 #include "common.cuh"
 #include "kmc_internal.h"
@@ -33,9 +37,10 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
     return v;
 }
 
-// The whole CTA calls this; `fail` is a shared int.  On a timeout the totals keep the rank's own values and
-// counters[1] gets kFlagExchange.  Ends with the summed totals visible to the CTA (a barrier).
-__device__ inline void exchange_cta(long long* __restrict__ totals, int64_t W,
+// The whole CTA calls this for the values [e0, e1) of the W totals, through flag row `row`; `fail` is a shared
+// int.  On a timeout those totals keep the rank's own values and counters[1] gets kFlagExchange.  Ends with the
+// summed totals visible to the CTA (a barrier).
+__device__ inline void exchange_cta(long long* __restrict__ totals, int64_t W, int64_t e0, int64_t e1, int row,
                                     const unsigned long long* __restrict__ peers, int world, int rank,
                                     unsigned long long step, unsigned long long timeout_ns,
                                     long long* __restrict__ counters, int* fail) {
@@ -44,14 +49,14 @@ __device__ inline void exchange_cta(long long* __restrict__ totals, int64_t W,
     const size_t slot_off = (size_t)kExchangeHeader + (size_t)(step & 1) * (size_t)W * 8;
     char* mine = reinterpret_cast<char*>(peers[rank]);
     long long* my_slot = reinterpret_cast<long long*>(mine + slot_off);
-    for (int64_t e = tid; e < W; e += nt) my_slot[e] = totals[e];
+    for (int64_t e = e0 + tid; e < e1; e += nt) my_slot[e] = totals[e];
     __threadfence_system();
     __syncthreads();
     const unsigned long long tag = step + 1;
     if (tid < world && tid != rank) {
-        unsigned long long* flag = reinterpret_cast<unsigned long long*>(peers[tid]) + rank;
+        unsigned long long* flag = reinterpret_cast<unsigned long long*>(peers[tid]) + row * 64 + rank;
         st_release_sys(flag, tag);
-        const unsigned long long* own = reinterpret_cast<const unsigned long long*>(mine) + tid;
+        const unsigned long long* own = reinterpret_cast<const unsigned long long*>(mine) + row * 64 + tid;
         const unsigned long long t0 = global_ns();
         uint32_t i = 0;
         while (ld_acquire_sys(own) < tag) {
@@ -67,13 +72,18 @@ __device__ inline void exchange_cta(long long* __restrict__ totals, int64_t W,
         __syncthreads();
         return;
     }
-    for (int64_t e = tid; e < W; e += nt) {
-        long long s = 0;
+    // four values per thread per round: 4 x world independent loads in flight over NVLink
+    for (int64_t e = e0 + tid; e < e1; e += 4 * (int64_t)nt) {
+        long long s[4] = {0, 0, 0, 0};
         for (int r = 0; r < world; r++) {
             const long long* slot = reinterpret_cast<const long long*>(reinterpret_cast<const char*>(peers[r]) + slot_off);
-            s += slot[e];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (e + (int64_t)u * nt < e1) s[u] += slot[e + (int64_t)u * nt];
         }
-        totals[e] = s;
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+            if (e + (int64_t)u * nt < e1) totals[e + (int64_t)u * nt] = s[u];
     }
     __syncthreads();
 }

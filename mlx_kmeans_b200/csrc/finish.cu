@@ -196,7 +196,8 @@ __global__ void __launch_bounds__(1024) k_finish(FinishArgs a) {
     }
     // 0. (fused step tail) the totals summed over the ranks
     if (a.peers)
-        exchange_cta(a.totals, (int64_t)k * W, a.peers, a.world, a.rank, a.step, a.timeout_ns, a.counters, &sh_xfail);
+        exchange_cta(a.totals, (int64_t)k * W, 0, (int64_t)k * W, 0, a.peers, a.world, a.rank, a.step, a.timeout_ns,
+                     a.counters, &sh_xfail);
     // 1. inertia (exact int64 sum) and empty count, before any relocation (core.py:2223)
     long long in = 0, ne = 0;
     for (int c = tid; c < k; c += nt) {
@@ -360,6 +361,11 @@ cudaError_t launch_finish(long long* totals, int k, int d, const uint32_t* cands
                           float* C_new, void* stats, const Workspace& ws, cudaStream_t st,
                           const unsigned long long* peers, int world, int rank, unsigned long long step,
                           void* loop) {
+    if (peers && exchange_wide(k, d)) {         // wide totals: the multi-CTA exchange as a launch of its own
+        cudaError_t e = launch_exchange_sum(totals, k, d, peers, world, rank, step, ws.counters, st);
+        if (e != cudaSuccess) return e;
+        peers = nullptr;
+    }
     FinishArgs a;
     a.loop = static_cast<LoopState*>(loop);
     a.totals = totals;

@@ -144,11 +144,14 @@ cudaError_t launch_elkan(const float* X, int64_t n, int d, const float* C, int k
                          int4* cands, const uint32_t* order, const Prep* prep, long long* counters, cudaStream_t st);
 
 // Peer-memory all-reduce of the totals (exchange.cu).
-constexpr int kExchangeHeader = 512;      // 64 flags of 8 bytes before the two slots
+constexpr int kExchangeRows = 64;         // flag rows: the exchange of wide totals runs one CTA per row
+constexpr int kExchangeHeader = kExchangeRows * 64 * 8;   // 64 rows x 64 ranks' flags of 8 bytes before the slots
+constexpr int64_t kExchangeWideMin = 16384;  // totals of at least this many int64 values take the multi-CTA exchange
 size_t exchange_bytes(int k, int d);
 unsigned long long exchange_timeout_ns();
 cudaError_t launch_exchange_sum(long long* totals, int k, int d, const unsigned long long* peers, int world, int rank,
                                 unsigned long long step, long long* counters, cudaStream_t st);
+bool exchange_wide(int k, int d);
 
 cudaError_t launch_far_rows(const float* X, int64_t n, int d, const int32_t* labels, const float* best, int64_t row0,
                             int64_t cand_rows, uint32_t* cands, const FarWorkspace& ws, cudaStream_t st);

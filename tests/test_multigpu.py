@@ -1,5 +1,7 @@
-"""Sharded Lloyd steps over 2 GPUs (NCCL) against one GPU: the centers, inertia and counts after several steps
-must be bit-identical (exact int64 totals, shards on the block grid). Skipped with fewer than 2 GPUs."""
+"""Sharded Lloyd steps over 2 GPUs (totals summed through peer memory) against one GPU: the centers, inertia and
+counts after several steps must be bit-identical (exact int64 totals, shards on the block grid), on the low-d
+bounded pass (config 3), the CUDA-core pass (config 1) and the tensor-core pass with wide totals (config 5's
+shape on 1.5M rows). Skipped with fewer than 2 GPUs."""
 import os
 import socket
 
@@ -72,7 +74,7 @@ def _spawn(world, cfg):
     return res
 
 
-@pytest.mark.parametrize("cfg", [3, 1])
+@pytest.mark.parametrize("cfg", [3, 1, 5])        # 5: wide totals (k = 4096, d = 128), the multi-CTA exchange
 def test_two_gpus_match_one_gpu_bit_for_bit(cfg):
     import torch
     if torch.cuda.device_count() < 2:
