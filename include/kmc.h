@@ -188,7 +188,9 @@ int kmc_exchange_sum(int64_t *totals, int k, int d, const uint64_t *peers, int w
 
 /* kmc_exchange_sum then kmc_finish without relocation candidates, in one launch (the step's tail when rows are
  * sharded over GPUs): the same exchange protocol and step count (`step` as for kmc_exchange_sum; a timeout sets
- * stats flag 2 and leaves this rank's own totals), then the divide, empties and statistics of kmc_finish. */
+ * stats flag 2 and leaves this rank's own totals), then the divide, empties and statistics of kmc_finish.  Wide
+ * totals (k (d + 2) >= 16384 values) are exchanged by a multi-CTA launch of their own first, as kmc_exchange_sum
+ * does for them. */
 int kmc_exchange_finish(int64_t *totals, int k, int d, const uint64_t *peers, int world, int rank, uint64_t step,
                         float *C_new, kmc_stats *stats, void *workspace, size_t ws_bytes, void *stream);
 
