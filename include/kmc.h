@@ -75,9 +75,10 @@ int kmc_version(void);
 const char *kmc_last_error(void);
 /* Number of streaming multiprocessors of the current device (grid sizing of the caller's own work). */
 int kmc_num_sms(void);
-/* Row granularity of the pass kernels' fixed blocks: when every shard / slice starts at a global row that
- * is a multiple of this, the totals are bit-identical however the rows are split over slices and GPUs. */
-int64_t kmc_row_block(void);
+/* Row granularity of the pass kernels' fixed blocks for a dataset of n_total rows in all (slices and GPUs):
+ * when every shard / slice starts at a global row that is a multiple of this, the totals are bit-identical
+ * however the rows are split over slices and GPUs.  8192 below 64M rows, 20480 from there. */
+int64_t kmc_row_block(int64_t n_total);
 
 /* ---------------------------------------------------------------- workspace */
 

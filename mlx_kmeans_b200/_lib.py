@@ -32,7 +32,7 @@ SIGNATURES = {
     "kmc_version": (_int, []),
     "kmc_last_error": (ctypes.c_char_p, []),
     "kmc_num_sms": (_int, []),
-    "kmc_row_block": (_i64, []),
+    "kmc_row_block": (_i64, [_i64]),
     "kmc_workspace_bytes": (_sz, [_int, _int]),
     "kmc_far_workspace_bytes": (_sz, [_i64]),
     "kmc_colmax": (_int, [_vp, _i64, _int, _vp, _u, _vp]),

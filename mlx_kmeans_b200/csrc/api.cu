@@ -182,7 +182,7 @@ const char* kmc_last_error(void) { return g_err.c_str(); }
 
 int kmc_num_sms(void) { return num_sms(); }
 
-int64_t kmc_row_block(void) { return lowd_block_rows(); }
+int64_t kmc_row_block(int64_t n_total) { return lowd_block_rows(n_total); }
 
 size_t kmc_workspace_bytes(int d, int k) { return carve(nullptr, d, k).bytes; }
 

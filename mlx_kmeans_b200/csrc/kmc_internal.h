@@ -29,6 +29,7 @@ struct PassArgs {
     uint32_t* brows;          // bounded pass: one bound word per row (nullptr: plain pass)
     const float* hsep;        // bounded pass: per center, (half its distance to the nearest other center)^2
     int64_t n_total;          // rows of the whole dataset (all slices and GPUs): sets the fixed-point grids
+    int rpl;                  // fused low-d kernels: rows per lane between folds (from n_total: the block size)
 };
 
 // Bounds state of one slice (caller memory): [meta: double drift, double valid; at byte 128: hsep, k <= 32 floats]
@@ -76,7 +77,7 @@ cudaError_t launch_prepare(const float* C, int k, int d, const unsigned int* col
 cudaError_t launch_pass_generic(PassArgs a, cudaStream_t st);
 // Specialised low-dimensional fused pass; returns cudaErrorNotSupported when (d, k) has no instance.
 cudaError_t launch_pass_lowd(PassArgs a, cudaStream_t st);
-int64_t lowd_block_rows();
+int64_t lowd_block_rows(int64_t n_total);
 
 // Tensor-core pass (d >= 32): per-slice operands, computed once per dataset ...
 struct RowSplit {

@@ -14,11 +14,11 @@
 //            lane, NumPy-pairwise D64, lowest index on ties -- so a label is never decided by rounding.
 //   totals   residual t = x - c_label (the float32 `best` is built from it, square and add rounded on their
 //            own); lane-private float32 sums per (cluster, column) and 8-bit counts in shared memory; every
-//            block of kRowsPerLane rows per lane the warp folds the 32 lanes in a fixed order (fold_block),
+//            block of rpl rows per lane the warp folds the 32 lanes in a fixed order (fold_block),
 //            adds count * c back (sum x = sum t + n c), rounds once to the fixed-point grid and adds the
 //            integers into the CTA's int64 totals.  Inertia: float64 per lane, folded per block likewise.
-// A block is a fixed range of kBlockRows local rows, so results are bit-reproducible; with shard starts that
-// are multiples of kBlockRows they are also identical for any split of the rows over GPUs.
+// A block is a fixed range of 128 rpl local rows, so results are bit-reproducible; with shard starts that are
+// multiples of the block (kmc_row_block(n_total)) they are also identical for any split of the rows over GPUs.
 //
 // Two kernels:
 //   k_pass_lowd     every row is screened (optionally writing labels and `best`).
@@ -48,13 +48,18 @@ constexpr int kStages = 8;             // ring slots per thread of the screening
 #endif
 // rows per thread in flight in the bounded kernel, held in registers: about 128 bytes of rows
 constexpr int bounded_ahead(int d) { return KMC_BOUNDED_AHEAD ? KMC_BOUNDED_AHEAD : d <= 4 ? 8 : 4; }
-#ifndef KMC_ROWS_PER_LANE
-#define KMC_ROWS_PER_LANE 64
-#endif
-constexpr int kRowsPerLane = KMC_ROWS_PER_LANE;   // rows per lane between folds (a multiple of 16, < 256)
-constexpr int kBlockRows = kThreads * kRowsPerLane;   // 8192 rows per block
+// Rows per lane between folds (PassArgs::rpl), set by the dataset's global row count so that every split of the
+// rows over slices and GPUs uses the same blocks: 64 (8192-row blocks) up to kLargeRows rows, 160 (20480-row
+// blocks) from there -- the per-block fold of the lane sums and each round's start are paid 2.5x less often
+// (96M x 4, k = 16: 0.520 -> 0.492 ms per pass), and a 12M-row shard of eight GPUs is 586 blocks, one round of
+// the 592 CTA slots, where 8192-row blocks needed three rounds for 2.47 blocks per slot (0.092 -> 0.082 ms).
+// Small datasets keep the smaller blocks so that more CTAs share the rows.
+constexpr int kRowsSmall = 64, kRowsLarge = 160;
+constexpr int64_t kLargeRows = 64000000;
+constexpr int rows_per_lane(int64_t n_total) { return n_total >= kLargeRows ? kRowsLarge : kRowsSmall; }
 constexpr int kQueue = 64;             // queued rows per warp in the bounded kernel (power of two, >= 64)
-static_assert(kRowsPerLane % kStages == 0 && kRowsPerLane % 8 == 0 && kRowsPerLane < 256, "block layout");
+static_assert(kRowsSmall % kStages == 0 && kRowsSmall % 8 == 0 && kRowsLarge % kStages == 0 &&
+              kRowsLarge % 8 == 0 && kRowsLarge < 256, "block layout: 8-bit counts per lane between folds");
 
 __device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
     return ((unsigned long long)__float_as_uint(hi) << 32) | __float_as_uint(lo);
@@ -399,7 +404,7 @@ struct BoundSmem {
 };
 
 // Per-thread state of the row loop.  Counts are packed four 8-bit fields to a word: a lane adds at most
-// kRowsPerLane < 256 rows to one cluster between folds.
+// rpl < 256 rows to one cluster between folds.
 template <int D, int K>
 struct LowdRow {
     static constexpr unsigned IDXBITS = idx_bits(K);
@@ -614,14 +619,14 @@ struct LowdRow {
 
     // End of a block: fold the lanes' slots into the CTA's int64 totals (fixed order => deterministic) and
     // the block's inertia into acc[1].  Counts first: the even and the odd 8-bit fields of each word are summed
-    // over the warp as 16-bit fields (at most 32 * kRowsPerLane < 2^16 each), and lane j < 4 parks the count of
+    // over the warp as 16-bit fields (at most 32 * rpl < 2^16 each), and lane j < 4 parks the count of
     // cluster 4 w + j in its own word.  Then the columns: the 32 lanes' partial sums of a column in a fixed
     // order (even D: columns j, j + 1 of a cluster as one packed float32 pair, a five-level tree; odd D: one
     // column in float64), then sum x = sum t + count * c in float64, rounded once to the fixed-point grid.  (The
-    // lanes' partials are sequential float32 sums of kRowsPerLane residuals already; five more levels of float32
+    // lanes' partials are sequential float32 sums of rpl residuals already; five more levels of float32
     // addition keep the error of the same order.)
     __device__ __forceinline__ void fold_block(long long* acc, const double* scale_x, double scale_i) {
-        static_assert(32 * kRowsPerLane < 65536, "16-bit count fields");
+        static_assert(32 * kRowsLarge < 65536, "16-bit count fields");
         __syncwarp();
 #pragma unroll
         for (int w = 0; w < (K + 3) / 4; w++) {
@@ -749,17 +754,20 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(PlainSmem<D, K>::total) 
     LowdRow<D, K> st;
     st.init(a, prep, cs, sums_all, cnts_all, L::kSums, L::kCnts, warp, lane);
 
-    // Row of thread tid at step r of block b: b * kBlockRows + r * kThreads + tid.  Ring slot r % kStages
+    // Row of thread tid at step r of block b: b * BR + r * kThreads + tid (BR = kThreads * rpl rows per block).
+    // Ring slot r % kStages
     // holds step r; the prefetch of step r + kStages - 1 is issued at step r into the slot read at step
     // r - 1, so this thread's reads of that slot have completed.  The prefetch walks a pointer (and, near
     // the end of the rows, a row index) kStages - 1 steps ahead of the reads, jumping to the CTA's next
     // block when it leaves the current one.
-    const int64_t nblk = (n + kBlockRows - 1) / kBlockRows;
+    const int64_t BR = (int64_t)kThreads * a.rpl;
+    const int nch = a.rpl / kStages;
+    const int64_t nblk = (n + BR - 1) / BR;
     const unsigned myring_s = (unsigned)__cvta_generic_to_shared(ring + (size_t)tid * D);
     constexpr int SLOT = kThreads * D;
     constexpr int STEP = kThreads * D;                 // floats between a thread's consecutive rows
-    const float* pf = a.X + ((int64_t)blockIdx.x * kBlockRows + tid) * D;
-    int64_t pf_row = (int64_t)blockIdx.x * kBlockRows + tid;
+    const float* pf = a.X + ((int64_t)blockIdx.x * BR + tid) * D;
+    int64_t pf_row = (int64_t)blockIdx.x * BR + tid;
     auto fetch = [&](int slot, bool ok) {
         if (ok) {
             const unsigned dst = myring_s + (unsigned)(slot * SLOT * 4);
@@ -774,18 +782,18 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(PlainSmem<D, K>::total) 
     for (int s = 0; s < kStages - 1; s++) fetch(s, pf_row < n);
 
     for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
-        const int64_t base = blk * kBlockRows + tid;
-        const int64_t next = (blk + gridDim.x) * kBlockRows + tid;
+        const int64_t base = blk * BR + tid;
+        const int64_t next = (blk + gridDim.x) * BR + tid;
         // checks are needed only while this block or the prefetched part of the next one is ragged
-        const bool clean = (blk + gridDim.x + 1) * kBlockRows <= n;
+        const bool clean = (blk + gridDim.x + 1) * BR <= n;
 
         auto steps = [&](auto check) {
             constexpr bool CHECK = decltype(check)::value;
-            for (int ch = 0; ch < kRowsPerLane / kStages; ch++) {
+            for (int ch = 0; ch < nch; ch++) {
 #pragma unroll
                 for (int s = 0; s < kStages; s++) {
                     const int r = ch * kStages + s;
-                    if (s == 1 && ch == kRowsPerLane / kStages - 1) {   // step r + kStages - 1 == kRowsPerLane
+                    if (s == 1 && ch == nch - 1) {   // step r + kStages - 1 == rpl: the next block
                         pf = a.X + next * D;
                         pf_row = next;
                     }
@@ -862,13 +870,14 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
     const PackedShared<D, K> pk_s{(unsigned)__cvta_generic_to_shared(pks)};
     const bool bounded = prep.bvalid != 0;
 
-    // Row of thread tid at step r of block b: b * kBlockRows + r * kThreads + tid, as in the screening kernel.
+    // Row of thread tid at step r of block b: b * BR + r * kThreads + tid, as in the screening kernel.
     // Register slot r % P holds row r; it is refilled with row r + P once row r is done.  Steps run in chunks
     // of U; a refill reads from this chunk's or the next chunk's base (the next block's first chunk after the
     // last one) at a constant offset, so the loads carry immediate offsets and no per-row pointer arithmetic.
-    const int64_t nblk = (n + kBlockRows - 1) / kBlockRows;
+    const int64_t BR = (int64_t)kThreads * a.rpl;
+    const int64_t nblk = (n + BR - 1) / BR;
     constexpr int XSTEP = kThreads * D;                 // floats between a thread's consecutive rows
-    constexpr int NCH = kRowsPerLane / U;
+    const int nch = a.rpl / U;
     // rows in flight; an even number of columns is kept as packed pairs end to end (PK), so the packed float32
     // arithmetic needs no register moves
     constexpr bool PK = D % 2 == 0;
@@ -894,7 +903,7 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
         }
     };
     {
-        const int64_t r0 = (int64_t)blockIdx.x * kBlockRows + tid;
+        const int64_t r0 = (int64_t)blockIdx.x * BR + tid;
 #pragma unroll
         for (int q = 0; q < P; q++)
             fetch(xq[q], xq2[q], wq[q], a.X + (r0 + q * kThreads) * D, a.brows + r0 + q * kThreads,
@@ -913,10 +922,10 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
     int qhead = 0, qcount = 0;
 
     for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
-        const int64_t base = blk * kBlockRows + tid;
-        const int64_t blk0 = blk * kBlockRows;
-        const int64_t next = (blk + gridDim.x) * kBlockRows + tid;
-        const bool clean = (blk + gridDim.x + 1) * kBlockRows <= n;
+        const int64_t base = blk * BR + tid;
+        const int64_t blk0 = blk * BR;
+        const int64_t next = (blk + gridDim.x) * BR + tid;
+        const bool clean = (blk + gridDim.x + 1) * BR <= n;
 
         // screen `cnt` queued rows, one per lane
         auto flush = [&](int cnt) {
@@ -948,9 +957,9 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
         const uint32_t* wblk = a.brows + base;
         auto steps = [&](auto check) {
             constexpr bool CHECK = decltype(check)::value;
-            for (int ch = 0; ch < NCH; ch++) {
+            for (int ch = 0; ch < nch; ch++) {
                 // this chunk's rows and the next chunk's (the next block's first chunk after the last)
-                const bool last = ch == NCH - 1;
+                const bool last = ch == nch - 1;
                 const float* xc = xblk + (int64_t)ch * U * XSTEP;
                 const uint32_t* wc = wblk + ch * U * kThreads;
                 const float* xn = last ? a.X + next * D : xc + U * XSTEP;
@@ -1074,7 +1083,7 @@ cudaError_t launch_grid(Kern kern, size_t smem, unsigned long long& configured, 
     if (per_sm < 1) return cudaErrorNotSupported;
     // as many CTAs as fit, but no more than it takes to give every CTA the same number of blocks: with few
     // blocks per CTA (a shard of a multi-GPU run) an uneven last round would otherwise set the pass time
-    const int64_t nblk = (a.n + kBlockRows - 1) / kBlockRows;
+    const int64_t nblk = (a.n + (int64_t)kThreads * a.rpl - 1) / ((int64_t)kThreads * a.rpl);
     const int64_t max_grid = (int64_t)num_sms() * per_sm;
     const int64_t rounds = (nblk + max_grid - 1) / max_grid;
     int64_t grid = rounds > 0 ? (nblk + rounds - 1) / rounds : 1;
@@ -1122,12 +1131,13 @@ cudaError_t run_k(PassArgs a, cudaStream_t st) {
 
 }  // namespace
 
-int64_t lowd_block_rows() { return kBlockRows; }
+int64_t lowd_block_rows(int64_t n_total) { return (int64_t)kThreads * rows_per_lane(n_total); }
 
 bool lowd_supports(int d, int k) { return d >= 1 && d <= 8 && k >= 1 && k <= (d <= 2 ? 32 : d <= 5 ? 16 : 8); }
 
 cudaError_t launch_pass_lowd(PassArgs a, cudaStream_t st) {
     if (!lowd_supports(a.d, a.k)) return cudaErrorNotSupported;
+    a.rpl = rows_per_lane(a.n_total);
     switch (a.d) {
         case 1: return run_k<1>(a, st);
         case 2: return run_k<2>(a, st);

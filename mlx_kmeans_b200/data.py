@@ -60,7 +60,7 @@ def shard_range(n_total, rank, world, align=None):
     """Contiguous rows [lo, hi) of rank `rank` of `world`; every boundary a multiple of `align` (default: the
     library's row block, so the totals are bit-identical for any number of GPUs)."""
     if align is None:
-        align = int(_lib.load().kmc_row_block())
+        align = int(_lib.load().kmc_row_block(n_total))
     blocks = (n_total + align - 1) // align
     lo = min(n_total, (blocks * rank // world) * align)
     hi = min(n_total, (blocks * (rank + 1) // world) * align)

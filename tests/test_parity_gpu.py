@@ -258,7 +258,7 @@ def test_fused_is_deterministic_and_block_split_invariant(cuda_device):
     from mlx_kmeans_b200 import _lib
     from mlx_kmeans_b200.data import generate
     torch = _torch()
-    blk = int(_lib.load().kmc_row_block())
+    blk = int(_lib.load().kmc_row_block(0))
     n = 37 * blk + 1234
     X = generate(3, 0, n, cuda_device, rows_total=n)
     C = X[torch.arange(0, 16, device=cuda_device) * 997].contiguous()
@@ -269,6 +269,55 @@ def test_fused_is_deterministic_and_block_split_invariant(cuda_device):
     for u, v, w in zip(a, b, c):
         assert np.array_equal(np.asarray(u), np.asarray(v))
         assert np.array_equal(np.asarray(u), np.asarray(w))
+
+
+@pytest.mark.parametrize("bounded", [False, True])
+def test_large_blocks_are_split_invariant(bounded, cuda_device):
+    """From 64M rows in all the fused kernels fold 160 rows per lane (20480-row blocks, kmc_row_block): passes
+    over one slice and over three slices cut at block multiples, with the global row count of such a dataset,
+    give the same totals bit for bit (plain and bounded kernels, the bounded one after a pass that built its
+    bounds), and the labels of the 8192-row-block pass."""
+    import mlx_kmeans_b200 as km
+    from mlx_kmeans_b200 import _lib
+    from mlx_kmeans_b200.data import generate
+    torch = _torch()
+    L = _lib.load()
+    n_total = 64_000_000
+    blk = int(L.kmc_row_block(n_total))
+    assert blk == 20480 and int(L.kmc_row_block(n_total - 1)) == 8192
+    n = 37 * blk + 1234
+    X = generate(3, 0, n, cuda_device, rows_total=n)
+    C = X[torch.arange(0, 16, device=cuda_device) * 997].contiguous()
+    ds = km.Dataset([X])
+    ref_labels = ds.assign(C, return_labels=True)[3]
+    cm, b = ds.colmax, ds.buffers(16)
+    st = torch.cuda.current_stream().cuda_stream
+    lab = torch.empty(n, dtype=torch.int32, device=cuda_device)
+
+    def run(cuts):
+        tot = torch.zeros((16, 6), dtype=torch.int64, device=cuda_device)
+        for i, (lo, hi) in enumerate(zip(cuts[:-1], cuts[1:])):
+            flags = _lib.KMC_PASS_ACCUMULATE if i else 0
+            if bounded:
+                nb = int(L.kmc_bounds_bytes(hi - lo, 4, 16))
+                bb = torch.zeros(nb, dtype=torch.uint8, device=cuda_device)
+                for _ in range(2):          # the first pass writes the bounds, the second uses them
+                    t2 = torch.zeros_like(tot)
+                    _lib.call("kmc_pass_bounded", X[lo:hi].data_ptr(), hi - lo, 4, C.data_ptr(), 16, cm.data_ptr(),
+                              n_total, t2.data_ptr(), 0, bb.data_ptr(), nb, b["ws"].data_ptr(), b["wsb"], st)
+                tot += t2
+            else:
+                _lib.call("kmc_pass", X[lo:hi].data_ptr(), hi - lo, 4, C.data_ptr(), 16, cm.data_ptr(), n_total,
+                          tot.data_ptr(), lab[lo:hi].data_ptr(), None, flags, b["ws"].data_ptr(), b["wsb"], st)
+        torch.cuda.synchronize()
+        return tot.cpu().numpy()
+
+    one = run([0, n])
+    three = run([0, 5 * blk, 21 * blk, n])
+    assert np.array_equal(one, three)
+    assert one[:, 0].sum() == n
+    if not bounded:
+        assert np.array_equal(lab.cpu().numpy().astype(np.int64), ref_labels)
 
 
 def test_window_rows_are_rescored(cuda_device):
