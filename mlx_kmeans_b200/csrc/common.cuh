@@ -18,6 +18,13 @@
 
 namespace kmc {
 
+// Programmatic dependent launch: a kernel launched with launch_pdl may be scheduled while the kernel before it in
+// the stream is still finishing; it runs this first, which returns once that kernel has completed and its memory
+// writes are visible (at once when it was launched the ordinary way), so nothing the kernel does changes.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel of the stream be scheduled now (its pdl_wait still waits for this kernel to complete).
+__device__ __forceinline__ void pdl_launch_next() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 constexpr int kMaxDims = 4096;     // largest d the pass kernels accept
 
 // Per-pass constants, computed on device by k_prepare (no host round trip).

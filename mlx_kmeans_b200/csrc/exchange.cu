@@ -20,6 +20,7 @@ __global__ void __launch_bounds__(kExThreads) k_exchange_sum(long long* __restri
                                                             unsigned long long timeout_ns,
                                                             long long* __restrict__ counters) {
     __shared__ int s_fail;
+    pdl_wait();                                      // the pass's totals
     exchange_cta(totals, W, 0, W, 0, peers, world, rank, step, timeout_ns, counters, &s_fail);
 }
 
@@ -30,6 +31,7 @@ __global__ void __launch_bounds__(kExThreads) k_exchange_wide(long long* __restr
                                                              unsigned long long timeout_ns,
                                                              long long* __restrict__ counters) {
     __shared__ int s_fail;
+    pdl_wait();                                      // the pass's totals
     const int64_t per = (W + gridDim.x - 1) / gridDim.x;
     const int64_t e0 = (int64_t)blockIdx.x * per;
     const int64_t e1 = e0 + per < W ? e0 + per : W;
@@ -58,12 +60,11 @@ cudaError_t launch_exchange_sum(long long* totals, int k, int d, const unsigned 
         // ranges of at least 4096 values (32 KB per peer), at most one CTA per flag row
         int64_t g = (W + 4095) / 4096;
         if (g > kExchangeRows) g = kExchangeRows;
-        k_exchange_wide<<<(int)g, kExThreads, 0, st>>>(totals, W, peers, world, rank, step, exchange_timeout_ns(),
-                                                       counters);
-    } else {
-        k_exchange_sum<<<1, kExThreads, 0, st>>>(totals, W, peers, world, rank, step, exchange_timeout_ns(), counters);
+        return launch_pdl(k_exchange_wide, dim3((unsigned)g), dim3(kExThreads), 0, st, totals, W, peers, world, rank,
+                          step, exchange_timeout_ns(), counters);
     }
-    return cudaGetLastError();
+    return launch_pdl(k_exchange_sum, dim3(1), dim3(kExThreads), 0, st, totals, W, peers, world, rank, step,
+                      exchange_timeout_ns(), counters);
 }
 
 }  // namespace kmc

@@ -190,6 +190,7 @@ __global__ void __launch_bounds__(1024) k_finish(FinishArgs a) {
     __shared__ int s_bigi[32];
     __shared__ long long sh_n_empty, sh_inert, sh_nreloc;
     __shared__ int sh_big, sh_write, sh_xfail;
+    pdl_wait();                                        // the pass's totals (or the exchange's)
     if (a.loop && a.loop->state != kLoopRunning) {    // the device loop stopped: nothing to do (read before any
         if (tid == 0 && a.grid_centers) a.counters[4] = 0;   // thread writes the record, after the barriers below)
         return;
@@ -343,6 +344,7 @@ __global__ void __launch_bounds__(1024) k_finish(FinishArgs a) {
 // Steps 4 and 5 of k_finish over a grid (many center values): every value computed from the totals, an empty
 // cluster's from the largest cluster's, so no value waits for another thread's.
 __global__ void __launch_bounds__(256) k_finish_centers(FinishArgs a) {
+    pdl_wait();                                      // k_finish's record
     if (a.counters[4] == 0) return;                  // relocation pending: the centers are not written
     const int k = a.k, d = a.d, W = d + 2;
     const int big = (int)a.counters[3];
@@ -388,13 +390,14 @@ cudaError_t launch_finish(long long* totals, int k, int d, const uint32_t* cands
     a.timeout_ns = peers ? exchange_timeout_ns() : 0;
     const int64_t total = (int64_t)k * d;
     a.grid_centers = total > kFinishOneCta;
-    k_finish<<<1, 1024, 0, st>>>(a);
+    cudaError_t e = launch_pdl(k_finish, dim3(1), dim3(1024), 0, st, a);
+    if (e != cudaSuccess) return e;
     if (a.grid_centers) {
         int64_t blocks = (total + 255) / 256;
         if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
-        k_finish_centers<<<(int)blocks, 256, 0, st>>>(a);
+        e = launch_pdl(k_finish_centers, dim3((unsigned)blocks), dim3(256), 0, st, a);
     }
-    return cudaGetLastError();
+    return e;
 }
 
 // ---------------------------------------------------------------- unpack (assign_mlx's return values)

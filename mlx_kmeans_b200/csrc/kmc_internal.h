@@ -10,6 +10,23 @@ namespace kmc {
 
 int num_sms();
 
+// The launch of a kernel that begins with pdl_wait(): with programmatic stream serialisation it is scheduled as
+// the kernel before it in the stream finishes (its launch and set-up overlap that kernel's tail) instead of after.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // Arguments of the pass kernels.
 struct PassArgs {
     const float* X;

@@ -104,6 +104,7 @@ __global__ void k_prepare(const float* __restrict__ C, int k, int d, const unsig
     __shared__ float s_max[32];
     __shared__ float s_cmax2[32];
     __shared__ int s_bad;
+    pdl_wait();
     if (loop && loop->state != kLoopRunning) {        // the device loop stopped: this step does nothing
         if (threadIdx.x == 0) prep->skip = 1;
         return;
@@ -308,9 +309,8 @@ cudaError_t launch_prepare(const float* C, int k, int d, const unsigned int* col
         if (e != cudaSuccess) return e;
         zero_totals = nullptr;
     }
-    k_prepare<<<1, 1024, 0, st>>>(C, k, d, colmax, n_total, prep, scale_x, hc, zero_totals, (int)zn, zero_counters,
-                                  bmeta, bcprev, bhsep, rule, static_cast<const LoopState*>(loop));
-    return cudaGetLastError();
+    return launch_pdl(k_prepare, dim3(1), dim3(1024), 0, st, C, k, d, colmax, n_total, prep, scale_x, hc, zero_totals,
+                      (int)zn, zero_counters, bmeta, bcprev, bhsep, rule, static_cast<const LoopState*>(loop));
 }
 
 cudaError_t launch_pass_generic(PassArgs a, cudaStream_t st) {

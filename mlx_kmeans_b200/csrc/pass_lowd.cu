@@ -737,6 +737,7 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(PlainSmem<D, K>::total) 
     float* cs = reinterpret_cast<float*>(smem + L::ring + L::sums + L::cnts);
     long long* acc = reinterpret_cast<long long*>(smem + L::ring + L::sums + L::cnts + L::centers);
 
+    pdl_wait();                                        // k_prepare's constants
     if (a.prep->skip) return;                          // a device Lloyd loop has stopped
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int k = a.k;
@@ -812,6 +813,7 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(PlainSmem<D, K>::total) 
         st.fold_block(acc, a.scale_x, prep.scale_i);
     }
     cp_wait<0>();
+    pdl_launch_next();                                 // k_finish may be scheduled now
     __syncthreads();
     st.finish(acc, a, tid);
 }
@@ -850,6 +852,7 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
     int* queue_all = reinterpret_cast<int*>(smem + off);           off += L::queue;
     float* qrows_all = reinterpret_cast<float*>(smem + off);
 
+    pdl_wait();                                        // k_prepare's constants
     if (a.prep->skip) return;                          // a device Lloyd loop has stopped
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int k = a.k;
@@ -1044,6 +1047,7 @@ __global__ void __launch_bounds__(kThreads, bounded_ctas(D, BoundSmem<D, K>::tot
         st.chunk_done();
         st.fold_block(acc, a.scale_x, prep.scale_i);
     }
+    pdl_launch_next();                                 // k_finish may be scheduled now
     __syncthreads();
     st.finish(acc, a, tid);
 }
@@ -1088,8 +1092,7 @@ cudaError_t launch_grid(Kern kern, size_t smem, unsigned long long& configured, 
     const int64_t rounds = (nblk + max_grid - 1) / max_grid;
     int64_t grid = rounds > 0 ? (nblk + rounds - 1) / rounds : 1;
     if (grid < 1) grid = 1;
-    kern<<<(int)grid, kThreads, smem, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3((unsigned)grid), dim3(kThreads), smem, st, a);
 }
 
 template <int D, int K, bool OUT>
