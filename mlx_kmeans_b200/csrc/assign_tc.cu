@@ -15,7 +15,7 @@
 //
 // Kernel layout (one CTA per SM, persistent over 128-row tiles):
 //   warp 0   TMA producer: per (row tile, center tile, 64-column chunk) one stage = xh, xl (128 x 64 bf16)
-//            and ch, cl (BN x 64 bf16), 128-byte swizzled, two stages in flight.
+//            and ch, cl (BN x 64 bf16), 128-byte swizzled, 2 to 6 stages in flight (as many as fit).
 //   warp 1   MMA issuer: 3 x 4 tcgen05.mma (M=128, N=BN, K=16) per stage into one of two TMEM accumulators;
 //            tcgen05.commit frees the stage and, after the last chunk, hands the accumulator to the epilogue.
 //   warps 2-9  epilogue: two warps per TMEM lane quarter, one per half of the accumulator's columns; a thread
@@ -41,7 +41,6 @@ namespace {
 
 constexpr int BM = 128;                  // rows per tile (UMMA M)
 constexpr int BK = 64;                   // bf16 columns per chunk: one 128-byte swizzle row
-constexpr int kTcStages = 2;
 constexpr int kTcThreads = 320;          // producer warp, MMA warp, eight epilogue warps
 constexpr int kEpiWarps = 8;
 constexpr uint32_t kSpinLimit = 1u << 22;
@@ -59,7 +58,12 @@ struct TcSmem {
     static constexpr int STAGE = AR ? PARTS * B : PARTS * (A + B);   // the parts of each operand it carries
     static constexpr int BAR = 256;                   // barriers, TMEM address, abort flag
     static constexpr int EPI = 2 * 4 * 32 * 5 * 4;    // the column halves' trackers: [tile parity][quarter][lane]
-    static constexpr int total = AREG + kTcStages * STAGE + BAR + EPI + 1024;   // + slack to align to 1 KB
+    // as many stages as the shared memory holds, 2 to 6: the small stages of few centers (BN = 64: 48 KB) or of
+    // exact=False keep more loads in flight (a streaming shape: the operands are read once), the 96 KB stages
+    // of 256 centers get two
+    static constexpr int FREE = 227 * 1024 - AREG - BAR - EPI - 1024;
+    static constexpr int NS = FREE / STAGE < 2 ? 2 : FREE / STAGE > 6 ? 6 : FREE / STAGE;
+    static constexpr int total = AREG + NS * STAGE + BAR + EPI + 1024;   // + slack to align to 1 KB
     static_assert(A % 1024 == 0 && B % 1024 == 0, "swizzle atoms are 1024-byte aligned");
     static_assert(total <= 227 * 1024, "shared memory per CTA");
 };
@@ -349,17 +353,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t base = (raw + 1023u) & ~1023u;
     const uint32_t sbase = base + S::AREG;
     unsigned char* gbase = smem_raw + (base - raw);
-    const uint32_t bars = sbase + kTcStages * S::STAGE;
-    unsigned char* gbars = gbase + S::AREG + kTcStages * S::STAGE;
-    // barrier block: full[2] empty[2] accf[2] acce[2] (8 B each), TMEM base (4 B), abort flag (4 B), and for
-    // resident rows afull, aempty (8 B each)
+    constexpr int NS = S::NS;
+    const uint32_t bars = sbase + NS * S::STAGE;
+    unsigned char* gbars = gbase + S::AREG + NS * S::STAGE;
+    // barrier block (8 B each): full[NS] empty[NS] accf[2] acce[2], for resident rows afull, aempty; then the TMEM
+    // base (4 B) and the abort flag (4 B)
+    static_assert(8 * (2 * NS + 6) + 8 <= S::BAR, "barrier block");
     auto full = [&](int s) { return bars + 8u * s; };
-    auto empty = [&](int s) { return bars + 16u + 8u * s; };
-    auto accf = [&](int b) { return bars + 32u + 8u * b; };
-    auto acce = [&](int b) { return bars + 48u + 8u * b; };
-    const uint32_t afull = bars + 72u, aempty = bars + 80u;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbars + 64);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(gbars + 68);
+    auto empty = [&](int s) { return bars + 8u * (NS + s); };
+    auto accf = [&](int b) { return bars + 8u * (2 * NS + b); };
+    auto acce = [&](int b) { return bars + 8u * (2 * NS + 2 + b); };
+    const uint32_t afull = bars + 8u * (2 * NS + 4), aempty = bars + 8u * (2 * NS + 5);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbars + 8 * (2 * NS + 6));
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(gbars + 8 * (2 * NS + 6) + 4);
     float* epi = reinterpret_cast<float*>(gbars + S::BAR);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -367,7 +373,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int ntiles = a.kp / BN, kchunks = a.dp / BK;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kTcStages; s++) {
+        for (int s = 0; s < NS; s++) {
             mbar_init(full(s), 1);
             mbar_init(empty(s), 1);
         }
@@ -430,7 +436,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                 tma_load_2d(st + 2 * S::A + S::B, &mcl, kc * BK, nt * BN, full(stage));
                             }
                         }
-                        if (++stage == kTcStages) { stage = 0; phase ^= 1u; }
+                        if (++stage == NS) { stage = 0; phase ^= 1u; }
                     }
             }
         }
@@ -471,7 +477,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             }
                         }
                         mma_commit(empty(stage));          // the stage is free once these MMAs are done
-                        if (++stage == kTcStages) { stage = 0; phase ^= 1u; }
+                        if (++stage == NS) { stage = 0; phase ^= 1u; }
                     }
                     if (!ok) break;
                     mma_commit(accf(abuf));                // the accumulator is ready for the epilogue
