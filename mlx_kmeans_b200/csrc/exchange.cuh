@@ -2,7 +2,7 @@
 // the work of one CTA (k_exchange_sum launches it alone; k_finish runs it first when the step's tail is fused).
 //
 // The rank copies its totals into its own exchange buffer, raises its flag in every peer's buffer (a release
-// store over NVLink), waits for every peer's flag (acquire loads of its own buffer, for at most a set time), and sums all
+// store over NVLink, after a CTA barrier), waits for every peer's flag (acquire loads of its own buffer, for at most a set time), and sums all
 // ranks' totals with plain peer loads.  The sum of integers does not depend on the order, so the result is the
 // same as NCCL's and the same on every rank.
 //
@@ -50,7 +50,8 @@ __device__ inline void exchange_cta(long long* __restrict__ totals, int64_t W, i
     char* mine = reinterpret_cast<char*>(peers[rank]);
     long long* my_slot = reinterpret_cast<long long*>(mine + slot_off);
     for (int64_t e = e0 + tid; e < e1; e += nt) my_slot[e] = totals[e];
-    __threadfence_system();
+    // the barrier orders every thread's slot writes before the flag stores below, and a system-scope release store
+    // is cumulative: a peer that acquires the flag sees the whole range (no fence per thread)
     __syncthreads();
     const unsigned long long tag = step + 1;
     if (tid < world && tid != rank) {
