@@ -49,6 +49,11 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--generic", action="store_true", help="force the any-shape kernel (diagnostic)")
     p.add_argument("--no-bounds", action="store_true", help="compare every row with every center each pass")
+    p.add_argument("--cascade", action="store_true",
+                   help="the prefix-pruning cascade (kmc_pass_cascade; 128-256 dims, k >= 256)")
+    p.add_argument("--column-decay", type=float, default=None,
+                   help="scale column j's spread by R^p(j) (p a seeded permutation): data with variance structure, "
+                        "the cascade's case (SIFT-like)")
     p.add_argument("--approx", action="store_true",
                    help="exact=False: the approximate tensor-core pass (one bf16 product per score; d >= 64)")
     return p.parse_args()
@@ -216,7 +221,7 @@ def main():
     import torch
     import torch.distributed as dist
     from mlx_kmeans_b200 import _lib, core
-    from mlx_kmeans_b200.data import CONFIGS, DESCRIPTION, generate, shard_range
+    from mlx_kmeans_b200.data import CONFIGS, DESCRIPTION, column_scales, generate, shard_range
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -236,7 +241,10 @@ def main():
     n_total, d, k = c["rows"], c["dims"], c["k"]
     lo, hi = shard_range(n_total, rank, world)
     X = generate(cfg, lo, hi - lo, dev, rows_total=n_total, group=group)
+    if args.column_decay:
+        X.mul_(torch.from_numpy(column_scales(d, args.column_decay, c["seed"])).to(dev))
     ds = core.Dataset([X], group=group)
+    ds.cascade = args.cascade
 
     # identical initial centers on every rank: greedy k-means++ on the first rows, broadcast from rank 0
     m = min(n_total, c["pp_sample"] or 20_000, hi - lo if world == 1 else n_total)
@@ -248,7 +256,8 @@ def main():
 
     # warm-up: full Lloyd steps (relocation handled)
     for _ in range(max(args.warmup, 3)):
-        C_new, s = ds.step(C, generic=args.generic, bounded=not args.no_bounds, approx=args.approx)
+        C_new, s = ds.step(C, generic=args.generic, bounded=not args.no_bounds, approx=args.approx,
+                           cascade=args.cascade)
         C = C_new.clone()
 
     L = _lib.load()
@@ -265,6 +274,10 @@ def main():
     bb, bbytes = ds.bounds(k)[0] if bounded else (None, 0)
     approx = args.approx and tc and ds.uses_approx(True)
     elk = None
+    casc = None
+    if tc and args.cascade and ds.cascade_ok(k, forced=True):
+        casc = ds.cascade_state(k)                    # prefix split and state built by the warm-up steps
+        Cm = torch.empty((k, casc["m"]), dtype=torch.float32, device=dev)
     if tc:
         (spl, splb), (csp, cspb) = ds.split()[0], ds.csplit(k)
         # per-center bounds (kmc_pass_elkan) built by the warm-up steps, used by every timed step
@@ -292,7 +305,15 @@ def main():
     for i in range(K):
         Cin, Cout = Cs[i % 2], Cs[(i + 1) % 2]
         ev[i][0].record(st)
-        if elk is not None:
+        if casc is not None:
+            torch.index_select(Cin, 1, casc["cols"], out=Cm)
+            (ms, mb), (cbuf, cbytes) = casc["msplits"][0], casc["bufs"][0]
+            _lib.check(L.kmc_pass_cascade(X.data_ptr(), X.shape[0], d, Cin.data_ptr(), k, cm.data_ptr(), n_total,
+                                          b["totals"].data_ptr(), None, None, flags, spl.data_ptr(), splb,
+                                          csp.data_ptr(), cspb, Cm.data_ptr(), casc["m"], ms.data_ptr(), mb,
+                                          casc["mcsplit"][0].data_ptr(), casc["mcsplit"][1], cbuf.data_ptr(), cbytes,
+                                          b["ws"].data_ptr(), b["wsb"], sp))
+        elif elk is not None:
             _lib.check(L.kmc_pass_elkan(X.data_ptr(), X.shape[0], d, Cin.data_ptr(), k, cm.data_ptr(), n_total,
                                         b["totals"].data_ptr(), None, None, flags, spl.data_ptr(), splb,
                                         csp.data_ptr(), cspb, elk[0].data_ptr(), elk[1], b["ws"].data_ptr(),
@@ -378,6 +399,8 @@ def main():
     tpeak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
     tensor_bound = tc and flops_per_launch / (tpeak * 1e12) > bytes_per_launch / (pk["hbm_gbs"] * 1e9)
     mmas = 1 if approx else 3             # bf16 MMAs per product: the pass's own ceiling is peak / mmas
+    if casc is not None:
+        mmas = 3.0 * casc["m"] / d        # the cascade multiplies the prefix columns only
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
@@ -400,9 +423,15 @@ def main():
                    "per_row_bounds": bounded,
                    "per_center_bounds": elk is not None,
                    "fraction_of_rows_compared_with_every_center": screened if bounded else 1.0,
-                   "fraction_of_row_center_pairs_visited": (screened / k) if elk is not None else None,
-                   "kernel": "generic" if args.generic else (("tensor cores (kmc_pass_split" +
-                                                               (", exact=False)" if approx else ")")) if tc else "auto")},
+                   "fraction_of_row_center_pairs_visited": (screened / k) if (elk is not None or casc is not None)
+                                                           else None,
+                   "column_decay": args.column_decay,
+                   "kernel": "generic" if args.generic else (("tensor cores (" +
+                                                               ("kmc_pass_cascade, prefix of %d columns)" % casc["m"]
+                                                                if casc is not None else
+                                                                "kmc_pass_split" +
+                                                                (", exact=False)" if approx else ")")))
+                                                              if tc else "auto")},
         "roofline": ({"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                       "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
                       "kernel_ms": pass_ms, "algorithmic_bytes_per_launch": bytes_per_launch,

@@ -161,6 +161,28 @@ int kmc_pass_elkan(const float *X, int64_t n, int d, const float *C, int k, cons
                    void *csplit, size_t csplit_bytes, void *elkan, size_t elkan_bytes, void *workspace,
                    size_t ws_bytes, void *stream);
 
+/* The prefix-pruning cascade: replaces the reference's two-stage exact assignment `_cascade_nearest`
+ * (core.py:1212-1260; stage kernels core.py:1107-1196, engaged at core.py:2085-2109).  The squared distance over a
+ * subset of the columns is a lower bound on the full one, so a center whose prefix distance already exceeds the
+ * row's distance to its previous label (widened by the decision window) cannot be its label.  Each row's threshold
+ * comes from its previous label; the tensor-core pass over the prefix (the caller's m columns, highest variance
+ * first: msplit = kmc_split_rows of those columns, kmc_split_bytes(n, m) bytes, filled once per slice; Cm = the
+ * centers' same columns, k x m float32, device; mcsplit = kmc_csplit_bytes(m, k) bytes, refilled by every pass)
+ * marks one bit per (row, center) whose rigorous lower bound is within it; the marked centers are then scored in
+ * full and near ties go to the label rule's decision, so labels, best and totals are kmc_pass_split's, bit for
+ * bit, whatever the prefix prunes.  cascade: kmc_cascade_bytes(n, k) bytes of caller memory per slice (the
+ * thresholds and the survivor bits, rewritten by every call).  The previous pass's labels on the split are the
+ * starting guesses, so a kmc_pass_split (or kmc_pass_elkan) must have run on the split first.  The number of
+ * survivors is added to the statistics' `screened`; the reference stops offering the cascade once more than 15% of
+ * the (row, center) pairs survive (core.py:491, 2155-2156).  k a multiple of 8; exact passes only (no
+ * KMC_PASS_APPROX or KMC_PASS_ELKAN_BUILD). */
+size_t kmc_cascade_bytes(int64_t n, int k);
+int kmc_pass_cascade(const float *X, int64_t n, int d, const float *C, int k, const uint32_t *colmax,
+                     int64_t n_total, int64_t *totals, int32_t *labels, float *best, unsigned flags, void *split,
+                     size_t split_bytes, void *csplit, size_t csplit_bytes, const float *Cm, int m, void *msplit,
+                     size_t msplit_bytes, void *mcsplit, size_t mcsplit_bytes, void *cascade, size_t cascade_bytes,
+                     void *workspace, size_t ws_bytes, void *stream);
+
 /* The tensor-core pass's raw scores, for auditing its error window (no counterpart in the reference): out
  * (device, n x k float32) = x.c for every row of the split (kmc_split_rows) and every center, exactly as the
  * tcgen05 MMAs of kmc_pass_split accumulate them (xh.ch + xh.cl + xl.ch in float32), before any decision.

@@ -55,6 +55,9 @@ SIGNATURES = {
     "kmc_elkan_bytes": (_sz, [_i64, _int, _int]),
     "kmc_pass_elkan": (_int, [_vp, _i64, _int, _vp, _int, _vp, _i64, _vp, _vp, _vp, _u, _vp, _sz, _vp, _sz, _vp, _sz,
                               _vp, _sz, _vp]),
+    "kmc_cascade_bytes": (_sz, [_i64, _int]),
+    "kmc_pass_cascade": (_int, [_vp, _i64, _int, _vp, _int, _vp, _i64, _vp, _vp, _vp, _u, _vp, _sz, _vp, _sz, _vp,
+                                _int, _vp, _sz, _vp, _sz, _vp, _sz, _vp, _sz, _vp]),
     "kmc_tc_dot": (_int, [_vp, _i64, _int, _int, _vp, _sz, _vp, _sz, _vp, _vp, _vp]),
     "kmc_loop_init": (_int, [_vp, ctypes.c_double, _i64, _i64, ctypes.c_double, _int, _vp]),
     "kmc_lloyd": (_int, [_vp, _i64, _int, _vp, _vp, _int, _vp, _i64, _vp, _u, _vp, _sz, _vp, _vp, _int, _vp, _sz,

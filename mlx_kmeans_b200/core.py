@@ -92,6 +92,15 @@ class Dataset:
     # 4.1 ms for the dense pass there)
     ELKAN_MAX_BYTES = 16 << 30
     ELKAN_MAX_VISITED = 0.05
+    # the prefix-pruning cascade (kmc_pass_cascade) where the reference offers it (core.py:486-491: 128 to 256 dims,
+    # k >= 256) and while its bounds fit; dropped once more than 15% of the (row, center) pairs survive.  Offered
+    # when Dataset.cascade is True, or for one call by method="cascade" (the reference's accuracy suite forces it
+    # that way); not by default: the dense tensor-core pass is faster on B200 at the shapes measured
+    CASCADE_MIN_DIMS = 128
+    CASCADE_MAX_DIMS = 256
+    CASCADE_MIN_K = 256
+    CASCADE_MAX_SURVIVORS = 0.15
+    CASCADE_MAX_BYTES = 48 << 30    # the survivor bits, one per (row, center)
 
     def __init__(self, parts, group=None, device=None, tensor_cores=None, label_rule="float64"):
         if isinstance(parts, (torch.Tensor, np.ndarray)) or not isinstance(parts, (list, tuple)):
@@ -126,6 +135,9 @@ class Dataset:
         self._xch = {}                  # per k: peer-memory exchange of the totals (multi-GPU), or False: NCCL
         self._elkan = {}                # per k: per-center bounds of the tensor-core pass and their policy state
         self.elkan = False              # True: per-center bounds between bounded tensor-core passes
+        self._cascade = {}              # per k: the cascade's prefix, bounds and policy state
+        self.cascade = False            # True: the prefix-pruning cascade where it applies
+        self._split_ready = False       # a tensor-core pass has left labels and the grouped order in the splits
 
     # -- per-dataset state
     @property
@@ -242,6 +254,59 @@ class Dataset:
         else:
             e["cool"] = 0
 
+    # -- the prefix-pruning cascade (kmc_pass_cascade): core.py:1198-1210 and 2085-2109
+    def cascade_m(self):
+        """Prefix width: half the dimensions in multiples of 8, 8 to 96 (core.py:1198-1200)."""
+        return min(96, max(8, (self.d // 2) // 8 * 8))
+
+    def cascade_ok(self, k, forced=False):
+        """Whether a pass with k centers takes the cascade: the reference's shape rule (core.py:1203-1204) even when
+        forced (core.py:2086, 2110: a forced cascade that does not apply falls through to the usual pass)."""
+        if not (self.tensor_cores and k % 8 == 0 and self.n_local * k // 8 <= self.CASCADE_MAX_BYTES and
+                self.CASCADE_MIN_DIMS <= self.d <= self.CASCADE_MAX_DIMS and k >= self.CASCADE_MIN_K):
+            return False
+        if forced:
+            return True
+        if self.cascade is not True:
+            return False
+        st = self._cascade.get(k)
+        return st is None or st["ok"]
+
+    def cascade_state(self, k):
+        """The columns by decreasing variance (on a strided sample of the first slice, as core.py:2096-2098), the
+        prefix of every slice split for the tensor cores, and the bounds buffers; built once per (dataset, k)."""
+        st = self._cascade.get(k)
+        if st is not None:
+            return st
+        L = _lib.load()
+        m = self.cascade_m()
+        step = max(1, self.parts[0].shape[0] // 65536)
+        var = self.parts[0][::step].var(dim=0, unbiased=False)
+        order = np.argsort(-var.cpu().numpy(), kind="stable").astype(np.int64)
+        cols = torch.from_numpy(order[:m].copy()).to(self.device)
+        msplits, bufs = [], []
+        for p in self.parts:
+            xm = p.index_select(1, cols).contiguous()
+            nb = int(L.kmc_split_bytes(p.shape[0], m))
+            t = torch.empty(nb, dtype=torch.uint8, device=self.device)
+            _lib.call("kmc_split_rows", _ptr(xm), p.shape[0], m, _ptr(t), nb, _stream())
+            msplits.append((t, nb))
+            eb = int(L.kmc_cascade_bytes(p.shape[0], k))
+            bufs.append((torch.empty(eb, dtype=torch.uint8, device=self.device), eb))
+        del xm
+        mcb = int(L.kmc_csplit_bytes(m, k))
+        st = dict(m=m, order=order, cols=cols, msplits=msplits, bufs=bufs,
+                  mcsplit=(torch.empty(mcb, dtype=torch.uint8, device=self.device), mcb), ok=True, used=False)
+        self._cascade[k] = st
+        return st
+
+    def cascade_after(self, k, stats):
+        """After a step: stop offering the cascade once a pass kept more than CASCADE_MAX_SURVIVORS of the pairs
+        (core.py:2155-2156: the data has no variance structure the prefix can use)."""
+        st = self._cascade.get(k)
+        if st is not None and st["used"] and stats["screened"] > self.CASCADE_MAX_SURVIVORS * self.n_local * k:
+            st["ok"] = False
+
     # -- the all-reduce of the totals over the ranks
     def _exchange(self, k):
         """Peer-memory exchange buffers for k centers: one per rank, mapped by every peer through CUDA IPC
@@ -314,11 +379,13 @@ class Dataset:
         APPROX_MIN_DIMS dims up; elsewhere it runs exactly, as the reference does below its crossover)."""
         return bool(approx) and self.tensor_cores and self.d >= self.APPROX_MIN_DIMS
 
-    def run_pass(self, C, labels=False, generic=False, bounded=False, reduce=True, rule=None, approx=False):
+    def run_pass(self, C, labels=False, generic=False, bounded=False, reduce=True, rule=None, approx=False,
+                 cascade=False):
         """kmc_pass over every local slice, then (reduce) the all-reduce of the totals. C: (k, d) float32 CUDA.
         bounded: use and refresh the per-row bounds (kmc_pass_bounded; no labels). rule: the label rule ("float64"
         or "float32"; None: the Dataset's). approx: exact=False (one bf16 product per score, no window) where
-        uses_approx allows it."""
+        uses_approx allows it. cascade: force the prefix-pruning cascade for this pass (method="cascade") where the
+        tensor-core pass runs; the Dataset's `cascade` attribute offers it to every exact pass."""
         k = C.shape[0]
         b = self.buffers(k)
         lab, bst = self._label_buffers(b) if labels else (None, None)
@@ -333,9 +400,24 @@ class Dataset:
         tc = self.tensor_cores and not generic
         bb = self.bounds(k) if want_bounds and not tc else None
         eb = None
+        casc = None
         if tc:
             sp, cs = self.split(), self.csplit(k)
-            if want_bounds and self.elkan_ok(k) and not (flags & _lib.KMC_PASS_APPROX):
+            if not (flags & _lib.KMC_PASS_APPROX) and self.cascade_ok(k, forced=cascade):
+                casc = self.cascade_state(k)
+                casc["used"] = False
+                if not self._split_ready:
+                    # the cascade prunes against each row's previous label: a plain pass leaves them first
+                    # (core.py:2104-2107 bootstraps a forced cascade the same way); the cascade below overwrites
+                    # its totals
+                    f0 = flags
+                    for i, p in enumerate(self.parts):
+                        _lib.call("kmc_pass_split", _ptr(p), p.shape[0], self.d, _ptr(C), k, _ptr(cm), self.n_total,
+                                  _ptr(b["totals"]), None, None, f0, _ptr(sp[i][0]), sp[i][1], _ptr(cs[0]), cs[1],
+                                  _ptr(b["ws"]), b["wsb"], st)
+                        f0 |= _lib.KMC_PASS_ACCUMULATE
+                Cm = C.index_select(1, casc["cols"]).contiguous()
+            elif want_bounds and self.elkan_ok(k) and not (flags & _lib.KMC_PASS_APPROX):
                 eb = self.elkan_state(k)
                 eb["used"] = False
                 if not eb["valid"] and eb["wait"] > 0:
@@ -343,7 +425,15 @@ class Dataset:
                     eb = None
             bb = None
         for i, p in enumerate(self.parts):
-            if tc and eb is not None:
+            if tc and casc is not None:
+                ebuf, ebytes = casc["bufs"][i]
+                ms, mb = casc["msplits"][i]
+                _lib.call("kmc_pass_cascade", _ptr(p), p.shape[0], self.d, _ptr(C), k, _ptr(cm), self.n_total,
+                          _ptr(b["totals"]), _ptr(lab[i]) if labels else None, _ptr(bst[i]) if labels else None,
+                          flags, _ptr(sp[i][0]), sp[i][1], _ptr(cs[0]), cs[1], _ptr(Cm), casc["m"], _ptr(ms), mb,
+                          _ptr(casc["mcsplit"][0]), casc["mcsplit"][1], _ptr(ebuf), ebytes, _ptr(b["ws"]), b["wsb"],
+                          st)
+            elif tc and eb is not None:
                 ebuf, ebytes = eb["bufs"][i]
                 _lib.call("kmc_pass_elkan", _ptr(p), p.shape[0], self.d, _ptr(C), k, _ptr(cm), self.n_total,
                           _ptr(b["totals"]), _ptr(lab[i]) if labels else None, _ptr(bst[i]) if labels else None,
@@ -364,6 +454,10 @@ class Dataset:
         if eb is not None:
             eb["used"] = eb["valid"]              # this pass used the bounds (a build pass visits nothing)
             eb["valid"] = True
+        if casc is not None:
+            casc["used"] = True
+        if tc:
+            self._split_ready = True
         if reduce:
             self.allreduce_totals(b, k)
         return b
@@ -374,7 +468,7 @@ class Dataset:
         return dict(inertia=float(host[:1].view(np.float64)[0]), n_empty=int(host[1]), n_relocated=int(host[2]),
                     needs_reloc=int(host[3]), flags=int(host[4]), rescored=int(host[5]), screened=int(host[6]))
 
-    def step(self, C, generic=False, bounded=True, rule=None, approx=False):
+    def step(self, C, generic=False, bounded=True, rule=None, approx=False, cascade=False):
         """One Lloyd iteration on the device: C (k, d) CUDA -> (C_new CUDA tensor (a buffer reused by the
         next step with the same k; copy it to keep it), stats dict).  bounded: keep per-row bounds between
         steps so rows whose label cannot have changed skip the comparison with every center (the labels are
@@ -382,7 +476,8 @@ class Dataset:
         label rule (None: the Dataset's). approx: exact=False (see run_pass)."""
         k = C.shape[0]
         x = self._exchange(k) if self.group is not None else False
-        b = self.run_pass(C, generic=generic, bounded=bounded, reduce=not x, rule=rule, approx=approx)
+        b = self.run_pass(C, generic=generic, bounded=bounded, reduce=not x, rule=rule, approx=approx,
+                          cascade=cascade)
         if x:
             # the all-reduce over peer memory and the finish in one launch
             _lib.call("kmc_exchange_finish", _ptr(b["totals"]), k, self.d, _ptr(x["dev"]), self.world, self.rank,
@@ -395,8 +490,9 @@ class Dataset:
         if s["flags"] & 2:
             raise RuntimeError("the all-reduce of the totals timed out waiting for a peer GPU")
         self.elkan_after(k, s)
+        self.cascade_after(k, s)
         if s["needs_reloc"]:
-            s = self._relocate(C, b, s["n_empty"], generic, rule, approx)
+            s = self._relocate(C, b, s["n_empty"], generic, rule, approx, cascade)
         return b["C_new"], s
 
     def device_loop_ok(self, generic=False):
@@ -451,11 +547,11 @@ class Dataset:
                 return bufs[cur], inertia, done, s["flags"]
             prev, have = inertia, 1
 
-    def _relocate(self, C, b, n_empty, generic, rule=None, approx=False):
+    def _relocate(self, C, b, n_empty, generic, rule=None, approx=False, cascade=False):
         """Empty clusters: recompute the pass with labels and best, gather the farthest rows of every slice
         and rank, and finish again with them (core.py:2224-2236)."""
         k = C.shape[0]
-        b = self.run_pass(C, labels=True, generic=generic, rule=rule, approx=approx)
+        b = self.run_pass(C, labels=True, generic=generic, rule=rule, approx=approx, cascade=cascade)
         E = int(n_empty)
         R = self.d + 4
         fwb = int(_lib.load().kmc_far_workspace_bytes(E))
@@ -478,10 +574,10 @@ class Dataset:
                   _ptr(b["stats"]), _ptr(b["ws"]), b["wsb"], _stream())
         return self.read_stats(b)
 
-    def assign(self, C, return_labels=False, generic=False, rule=None, approx=False):
+    def assign(self, C, return_labels=False, generic=False, rule=None, approx=False, cascade=False):
         """One pass -> (sums float64 (k, d), counts int64 (k), inertia float[, labels int64 (n_local)])."""
         k = C.shape[0]
-        b = self.run_pass(C, labels=return_labels, generic=generic, rule=rule, approx=approx)
+        b = self.run_pass(C, labels=return_labels, generic=generic, rule=rule, approx=approx, cascade=cascade)
         sums = torch.empty((k, self.d), dtype=torch.float64, device=self.device)
         counts = torch.empty(k, dtype=torch.int64, device=self.device)
         inertia = torch.empty(1, dtype=torch.float64, device=self.device)
@@ -611,7 +707,7 @@ def lloyd_step(parts, C, method="auto", accumulate="auto", label_rule=None):
     Cd = _centers(C, ds)
     _check_method(method, accumulate, Cd.shape[0], ds.d)
     C_new, s = ds.step(Cd, generic=(method == "generic"), rule=label_rule and _check_rule(label_rule),
-                       approx=(method == "approx"))
+                       approx=(method == "approx"), cascade=(method == "cascade"))
     inertia = float("nan") if s["flags"] & 1 else s["inertia"]
     return C_new.cpu().numpy(), inertia, s["n_empty"]
 
@@ -622,7 +718,8 @@ def assign_mlx(parts, C, method="auto", return_labels=False, accumulate="auto", 
     Cd = _centers(C, ds)
     _check_method(method, accumulate, Cd.shape[0], ds.d)
     out = ds.assign(Cd, return_labels=return_labels, generic=(method == "generic"),
-                    rule=label_rule and _check_rule(label_rule), approx=(method == "approx"))
+                    rule=label_rule and _check_rule(label_rule), approx=(method == "approx"),
+                    cascade=(method == "cascade"))
     return out
 
 

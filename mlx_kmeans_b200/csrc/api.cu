@@ -351,12 +351,22 @@ int kmc_split_rows(const float* X, int64_t n, int d, void* split, size_t split_b
 
 }  // extern "C"
 
-// kmc_pass_split and kmc_pass_elkan: elkan == nullptr for a plain tensor-core pass; else the per-center bounds,
-// built by the tensor-core pass (flags & KMC_PASS_ELKAN_BUILD) or used by the bounded pass.
+// The cascade's prefix (kmc_pass_cascade): the first m columns in the caller's order, as rows split once per slice
+// (msplit) and as centers (Cm, k x m, split into mcsplit by every pass).
+struct Prefix {
+    const float* Cm;
+    int m;
+    void* msplit;
+    void* mcsplit;
+};
+
+// kmc_pass_split, kmc_pass_elkan and kmc_pass_cascade: elkan == nullptr for a plain tensor-core pass; else the
+// per-center bounds, built by the tensor-core pass (flags & KMC_PASS_ELKAN_BUILD) or used by the bounded pass; or,
+// with pre, the cascade's state (threshold and survivor bits).
 static int tc_pass_impl(const char* who, const float* X, int64_t n, int d, const float* C, int k,
                         const uint32_t* colmax, int64_t n_total, int64_t* totals, int32_t* labels, float* best,
                         unsigned flags, void* split, size_t split_bytes, void* csplit, size_t csplit_bytes,
-                        void* elkan, void* workspace, size_t ws_bytes, void* stream) {
+                        void* elkan, void* workspace, size_t ws_bytes, void* stream, const Prefix* pre = nullptr) {
     if (int s = check_shape(n, d, k)) return s;
     if (!C || !colmax || !totals || !workspace || !split || !csplit || (n > 0 && !X))
         return fail(KMC_ERR_INVALID, "%s: null pointer", who);
@@ -403,7 +413,42 @@ static int tc_pass_impl(const char* who, const float* X, int64_t n, int d, const
     ts.approx = (flags & KMC_PASS_APPROX) ? 1 : 0;
     ts.lb = nullptr;
     ts.xsq_lo = rs.xsq_lo;
-    if (elkan) {
+    if (pre) {
+        // The cascade (elkan: its state, kmc_cascade_bytes).  Each row's threshold from its previous label; then
+        // the tensor-core pass over the prefix columns marks, per (row, center), whether a lower bound on the
+        // prefix's distance -- a lower bound on the full distance too, the other columns' terms being nonnegative
+        // -- is within it (that pass's own labels go to the prefix split and are not used; a barrier timeout in it
+        // sets the full pass's error flag, which sends every row to the float64 decision, the marks untrusted);
+        // then the marked centers are scored in full.
+        const CascadeState cst = carve_cascade(elkan, n, k);
+        const RowSplit prs = carve_rows(pre->msplit, n, pre->m);
+        const CenterSplit pcs = carve_centers(pre->mcsplit, pre->m, k);
+        e = launch_cascade_ub(X, n, d, C, k, cst, rs.lab, ws.prep, st);
+        if (e == cudaSuccess) e = launch_split_centers(pre->Cm, k, pre->m, pcs, st);
+        if (e == cudaSuccess) {
+            TcSplit tp = ts;
+            tp.dp = split_dp(pre->m);
+            tp.xh = prs.xh;
+            tp.xl = prs.xl;
+            tp.ch = pcs.ch;
+            tp.cl = pcs.cl;
+            tp.hs = pcs.hs;
+            tp.xn = prs.xn;
+            tp.cmax = reinterpret_cast<const float*>(pcs.cmax_bits);
+            tp.lab = prs.lab;
+            tp.cands = prs.cands;
+            tp.error = cs.error;
+            tp.approx = 0;
+            tp.xsq_lo = prs.xsq_lo;
+            tp.mask = cst.mask;
+            tp.ub = cst.ub;
+            tp.plab = rs.lab;
+            tp.srows = cst.srows;
+            tp.nsrows = cst.nsrows;
+            e = launch_assign_tc(tp, st);
+        }
+        if (e == cudaSuccess) e = launch_cascade(X, n, d, C, k, cst, rs.lab, rs.cands, ws.prep, ws.counters, st);
+    } else if (elkan) {
         const ElkanState es = carve_elkan(elkan, n, d, k);
         if (flags & KMC_PASS_ELKAN_BUILD) {            // a full pass that also writes every bound
             ts.lb = es.lb;
@@ -471,6 +516,35 @@ int kmc_pass_elkan(const float* X, int64_t n, int d, const float* C, int k, cons
     return tc_pass_impl(who, X, n, d, C, k, colmax, n_total, totals, labels, best, flags, split, split_bytes, csplit,
                         csplit_bytes, elkan, workspace, ws_bytes, stream);
 }
+
+int kmc_pass_cascade(const float* X, int64_t n, int d, const float* C, int k, const uint32_t* colmax,
+                     int64_t n_total, int64_t* totals, int32_t* labels, float* best, unsigned flags, void* split,
+                     size_t split_bytes, void* csplit, size_t csplit_bytes, const float* Cm, int m, void* msplit,
+                     size_t msplit_bytes, void* mcsplit, size_t mcsplit_bytes, void* cascade, size_t cascade_bytes_,
+                     void* workspace, size_t ws_bytes, void* stream) {
+    const char* who = "kmc_pass_cascade";
+    if (int s = check_shape(n, d, k)) return s;
+    if (!cascade || !Cm || !msplit || !mcsplit) return fail(KMC_ERR_INVALID, "%s: null pointer", who);
+    if (m < 1 || m > d) return fail(KMC_ERR_INVALID, "%s: prefix of %d columns out of 1..%d", who, m, d);
+    if (k % 8) return fail(KMC_ERR_UNSUPPORTED, "%s: k = %d, the bounds need k to be a multiple of 8", who, k);
+    if (flags & (KMC_PASS_APPROX | KMC_PASS_ELKAN_BUILD))
+        return fail(KMC_ERR_INVALID, "%s: flags 0x%x (the cascade is an exact pass that builds its own bounds)", who,
+                    flags);
+    if (cascade_bytes_ < cascade_bytes(n, k))
+        return fail(KMC_ERR_INVALID, "%s: cascade state of %zu bytes, need %zu", who, cascade_bytes_,
+                    cascade_bytes(n, k));
+    if (msplit_bytes < split_rows_bytes(n, m))
+        return fail(KMC_ERR_INVALID, "%s: prefix split of %zu bytes, need %zu", who, msplit_bytes,
+                    split_rows_bytes(n, m));
+    if (mcsplit_bytes < split_centers_bytes(m, k))
+        return fail(KMC_ERR_INVALID, "%s: prefix center split of %zu bytes, need %zu", who, mcsplit_bytes,
+                    split_centers_bytes(m, k));
+    const Prefix pre{Cm, m, msplit, mcsplit};
+    return tc_pass_impl(who, X, n, d, C, k, colmax, n_total, totals, labels, best, flags, split, split_bytes, csplit,
+                        csplit_bytes, cascade, workspace, ws_bytes, stream, &pre);
+}
+
+size_t kmc_cascade_bytes(int64_t n, int k) { return cascade_bytes(n, k); }
 
 int kmc_tc_dot(const float* C, int64_t n, int d, int k, void* split, size_t split_bytes, void* csplit,
                size_t csplit_bytes, float* out, int* error, void* stream) {

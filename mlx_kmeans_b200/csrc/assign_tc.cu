@@ -192,6 +192,21 @@ struct Top3 {
     }
 };
 
+// two float32 values as one packed pair (low = a), the packed subtraction rounded down, a three-way minimum
+__device__ __forceinline__ unsigned long long pack2f(float a, float b) {
+    return ((unsigned long long)__float_as_uint(b) << 32) | __float_as_uint(a);
+}
+__device__ __forceinline__ unsigned long long sub2_rd(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("sub.rm.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float fmin3f(float a, float b, float c) {
+    float d;
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 struct TcArgs {
     int64_t n;
     int dp;                  // padded dims (multiple of 64)
@@ -206,7 +221,13 @@ struct TcArgs {
     float* dump;             // (kmc_tc_dot) n x k: every accumulated x.c as read from TMEM, or nullptr
     float wr;                // window term per (|x| + max|c|)^2: the rounding of the label rule's distance
     __half* lb;              // (Elkan bounds, built here) n x k: a lower bound on every row-center distance, or nullptr
-    const float* xsq_lo;     // n: |x|^2 rounded down (with lb)
+    const float* xsq_lo;     // n: |x|^2 rounded down (with lb or mask)
+    uint32_t* mask;          // (cascade, built here) n x kw: bit c set where c's lower bound is <= ub[row], or nullptr
+    const float* ub;         // n: the cascade's threshold on the squared distance (with mask)
+    int kw;                  // 32-bit words per row of mask
+    const int32_t* plab;     // n: (with mask) each row's previous label
+    uint32_t* srows;         // (with mask) the rows with a survivor besides that label, in any order ...
+    unsigned int* nsrows;    // ... and their count (zero before the pass)
 };
 
 // 1 if x != 0 (or infinite), 0 if x == 0: x * 2^127 is at least 2^-22 for any nonzero float, and the second
@@ -510,12 +531,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         int it = 0;                                       // tiles done: the hand-over slot alternates with it
         for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, it++) {
             const int64_t row = t * BM + 32 * q + lane;
-            const float xr = ((h == 0 || a.lb) && row < a.n) ? __ldg(a.xn + row) : 0.0f;   // in flight meanwhile
+            const bool lbm = a.lb != nullptr || a.mask != nullptr;
+            const float xr = ((h == 0 || lbm) && row < a.n) ? __ldg(a.xn + row) : 0.0f;   // in flight meanwhile
             // Elkan bounds of this row (a.lb): |x - c|^2 = |x|^2 + 2 (|c|^2/2 - x.c) >= xsq_lo + 2 (score - err), err
             // the score's error bound of the window below (E |x| max|c| + 2^-24 max|c|^2, with a margin), every
             // step rounded down, then the square root rounded down and stored as half rounded toward zero
-            float lb_x = 0.0f, lb_err = 0.0f;
-            if (a.lb && row < a.n) {
+            // The cascade's survivor bits (a.mask) come from the same lower bound, squared, against the row's
+            // threshold: bit c set unless the bound exceeds ub[row].
+            float lb_x = 0.0f, lb_err = 0.0f, ubr = 0.0f;
+            int plab = -1;                                // (mask) the row's previous label: its own bit
+            uint32_t others = 0u;                         // (mask) any surviving center but the previous label
+            if (a.mask && row < a.n) {
+                ubr = __ldg(a.ub + row);
+                plab = __ldg(a.plab + row);
+                if (plab < 0 || plab >= a.k) {            // not a final label of this k: listed for the full scoring
+                    plab = 0;
+                    others = 1u;
+                }
+            }
+            if (lbm && row < a.n) {
                 const float cm = *a.cmax;
                 lb_x = __ldg(a.xsq_lo + row);
                 lb_err = __fmul_ru(__fadd_ru(__fmul_ru(__fmul_ru((float)(3.1 / 65536.0 + 3.0 * a.dp / 16777216.0), xr), cm),
@@ -554,6 +588,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                 if (c0 + j < a.k) dst[j] = hv[j];
                         }
                     }
+                    if (a.mask != nullptr && row < a.n && c0 < a.k) {   // the cascade's survivors of these 32 centers
+                        // hs - x.c rounded down, two at a time, and its minimum over the chunk: the bound of that
+                        // minimum (every step rounded down, so no bound of the chunk is below it) rules out the
+                        // whole chunk at once, as it does for almost every chunk of a row; the others are tested
+                        // center by center, from the same values
+                        float sv[32];
+#pragma unroll
+                        for (int g = 0; g < 8; g++) {
+                            const float4 hq = __ldg(reinterpret_cast<const float4*>(a.hs + c0) + g);
+                            const unsigned long long d01 = sub2_rd(pack2f(hq.x, hq.y), pack2f(v[4 * g], v[4 * g + 1]));
+                            const unsigned long long d23 = sub2_rd(pack2f(hq.z, hq.w), pack2f(v[4 * g + 2], v[4 * g + 3]));
+                            sv[4 * g] = __uint_as_float((unsigned)d01);
+                            sv[4 * g + 1] = __uint_as_float((unsigned)(d01 >> 32));
+                            sv[4 * g + 2] = __uint_as_float((unsigned)d23);
+                            sv[4 * g + 3] = __uint_as_float((unsigned)(d23 >> 32));
+                        }
+                        float mn[11];
+#pragma unroll
+                        for (int j = 0; j < 10; j++) mn[j] = fmin3f(sv[3 * j], sv[3 * j + 1], sv[3 * j + 2]);
+                        mn[10] = fminf(sv[30], sv[31]);
+                        const float m4 = fmin3f(fmin3f(mn[0], mn[1], mn[2]), fmin3f(mn[3], mn[4], mn[5]),
+                                                fmin3f(fmin3f(mn[6], mn[7], mn[8]), mn[9], mn[10]));
+                        uint32_t bits = 0u;
+                        if (!(__fmaf_rd(2.0f, __fsub_rd(m4, lb_err), lb_x) > ubr)) {
+#pragma unroll
+                            for (int j = 0; j < 32; j++) {
+                                const float d2 = __fmaf_rd(2.0f, __fsub_rd(sv[j], lb_err), lb_x);
+                                bits |= (!(d2 > ubr) && c0 + j < a.k) ? (1u << j) : 0u;
+                            }
+                        }
+                        a.mask[row * a.kw + (c0 >> 5)] = bits;
+                        others |= (plab >> 5) == (c0 >> 5) ? bits & ~(1u << (plab & 31)) : bits;
+                    }
+                    if (a.mask != nullptr) continue;               // the cascade's prefix pass needs no label
                     if (a.dump != nullptr && row < a.n) {          // diagnostic copy of the raw scores
 #pragma unroll
                         for (int j = 0; j < 32; j++)
@@ -585,6 +653,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             if constexpr (!CHUNK) ev.merge(od.m0, od.l0, od.m1, od.l1, od.m2);
             float* slot = epi + ((((it & 1) * 4 + q) * 32 + lane) * 5);
+            if (a.mask != nullptr) {
+                // the cascade: a row with a surviving center besides its previous label is listed for the full
+                // scoring (the two halves' columns combined through the hand-over slot); the others keep it
+                if (h == 1) slot[0] = __uint_as_float(others);
+                asm volatile("bar.sync %0, %1;" ::"r"(1 + q), "r"(64) : "memory");
+                if (h == 0 && ok && row < a.n && (others | __float_as_uint(slot[0])) != 0u)
+                    a.srows[atomicAdd(a.nsrows, 1u)] = (uint32_t)row;
+                continue;
+            }
             if (h == 1) {
                 slot[0] = ev.m0;
                 slot[1] = ev.m1;
@@ -597,7 +674,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             ev.merge(slot[0], __float_as_int(slot[3]), slot[1], __float_as_int(slot[4]), slot[2]);
             const float m0 = ev.m0, m1 = ev.m1, m2 = ev.m2;
             const int l0 = ev.l0, l1 = ev.l1;
-            if (row < a.n) {
+            if (row < a.n && a.mask == nullptr) {
                 const float r = xr + cmax;
                 const float win = (E2 * xr * cmax + cmax * (cmax + xr) * (1.0f / 8388608.0f)) * (1.0f + 1.0f / 1024.0f) +
                                   r * r * a.wr;
@@ -687,6 +764,12 @@ cudaError_t run_tc(const TcSplit& s, cudaStream_t st) {
     a.wr = (float)(1.0 / 1099511627776.0 + (s.rule ? rule32_coef(s.dp) : 0.0));
     a.lb = static_cast<__half*>(s.lb);
     a.xsq_lo = s.xsq_lo;
+    a.mask = static_cast<uint32_t*>(s.mask);
+    a.ub = s.ub;
+    a.plab = s.plab;
+    a.srows = s.srows;
+    a.nsrows = s.nsrows;
+    a.kw = (s.k + 31) / 32;
     const int64_t tiles = (s.n + BM - 1) / BM;
     int64_t grid = num_sms();
     if (grid > tiles) grid = tiles;

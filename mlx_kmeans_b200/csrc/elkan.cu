@@ -15,6 +15,11 @@
 //     full pass's, bit for bit, and the totals (grouped reduction, split.cu) too.
 // Every visited center's bound is replaced by its computed distance, rounded down; the others keep the lowered
 // bound.
+//
+// The prefix-pruning cascade (kmc_pass_cascade; the reference's two-stage exact assignment, core.py:1091-1260)
+// shares the bounded pass's scoring and decision: k_cascade_ub sets each row's threshold from its previous label,
+// the tensor-core pass over the prefix columns marks the centers whose prefix lower bound does not exceed it (one
+// bit per (row, center), assign_tc.cu), and k_cascade scores the marked centers in full.
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -89,6 +94,34 @@ __device__ __forceinline__ float warp_dist(const float (&xv)[XR > 0 ? XR : 1], c
     return s;
 }
 
+// A computed squared distance is within g of the exact one (a subtraction and a square per term, an fma chain of
+// ceil(d/32) terms per lane, a five-level tree: nonnegative terms, taken twice over).  A center can be the label
+// only if its computed distance is within W of the smallest: (1 + g) / (1 - g), the label rule's own rounding
+// (float64: 2^-40 of margin; the float32 rule: rule32_coef(d)), and a 2^-20 margin.
+struct Window {
+    float g, W;
+    __device__ Window(int d, int rule) {
+        const int mcols = (d + 31) / 32;
+        const double gd = (mcols + 8) / 8388608.0;
+        g = (float)gd;
+        W = (float)((1.0 + gd) / (1.0 - gd) * (1.0 + (rule ? rule32_coef(d) : 1.0 / 1099511627776.0)) *
+                    (1.0 + 1.0 / 1048576.0));
+    }
+};
+
+// A row's label from the distances computed for it: decided when no other center is within the window of the
+// smallest, else flagged (bit 31) with its candidates for the label rule's decision (split.cu).
+__device__ __forceinline__ void decide(const Best3& b, float W, int k, int64_t row, int32_t* lab, int4* cands) {
+    const float hi = __fmul_ru(b.m0, W);
+    if (!(b.m1 <= hi) && b.m0 <= 3.0e38f) {
+        lab[row] = b.l0;
+    } else {
+        const bool many = b.m2 <= hi || !(b.m0 <= 3.0e38f) || b.l1 == 0x7fffffff;
+        lab[row] = (int32_t)((uint32_t)(b.l0 < k ? b.l0 : 0) | 0x80000000u);
+        cands[row] = make_int4(b.l0 < k ? b.l0 : 0, b.l1 < k ? b.l1 : -1, -1, many ? -2 : -1);
+    }
+}
+
 template <int XR>
 __global__ void __launch_bounds__(kElkanThreads) k_elkan(const float* __restrict__ X, int64_t n, int d,
                                                         const float* __restrict__ C, int k,
@@ -99,16 +132,8 @@ __global__ void __launch_bounds__(kElkanThreads) k_elkan(const float* __restrict
                                                         long long* __restrict__ counters) {
     const int lane = threadIdx.x & 31;
     const int64_t nw = (int64_t)gridDim.x * kElkanWarps;
-    // A computed squared distance is within g of the exact one (a subtraction and a square per term, an fma chain
-    // of ceil(d/32) terms per lane, a five-level tree: nonnegative terms, taken twice over).  A center can be the
-    // label only if its computed distance is within W of the smallest: (1 + g) / (1 - g), the label rule's own
-    // rounding (float64: 2^-40 of margin; the float32 rule: rule32_coef(d)), and a 2^-20 margin.
-    const int mcols = (d + 31) / 32;
-    const double gd = (mcols + 8) / 8388608.0;
-    const int rule = prep->rule;
-    const float g = (float)gd;
-    const float W = (float)((1.0 + gd) / (1.0 - gd) * (1.0 + (rule ? rule32_coef(d) : 1.0 / 1099511627776.0)) *
-                            (1.0 + 1.0 / 1048576.0));
+    const Window wn(d, prep->rule);
+    const float g = wn.g, W = wn.W;
     long long visited = 0;
     // rows in the order of the previous pass's grouping by label (a permutation of the rows): neighbouring warps
     // take rows of the same cluster, which visit the same few centers, so those centers' vectors stay in L1
@@ -152,16 +177,100 @@ __global__ void __launch_bounds__(kElkanThreads) k_elkan(const float* __restrict
             }
             if (valid) *const_cast<__half*>(bp) = __float2half_rz(out);
         }
-        if (lane == 0) {
-            const float hi = __fmul_ru(b.m0, W);
-            if (!(b.m1 <= hi) && b.m0 <= 3.0e38f) {
-                lab[row] = b.l0;                       // decided: no other center within the window
-            } else {                                   // to the label rule's decision (split.cu)
-                const bool many = b.m2 <= hi || !(b.m0 <= 3.0e38f) || b.l1 == 0x7fffffff;
-                lab[row] = (int32_t)((uint32_t)(b.l0 < k ? b.l0 : 0) | 0x80000000u);
-                cands[row] = make_int4(b.l0 < k ? b.l0 : 0, b.l1 < k ? b.l1 : -1, -1, many ? -2 : -1);
+        if (lane == 0) decide(b, W, k, row, lab, cands);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) visited += __shfl_xor_sync(0xffffffffu, visited, o);
+    if (lane == 0 && visited) atomicAdd(reinterpret_cast<unsigned long long*>(&counters[2]), (unsigned long long)visited);
+}
+
+// The cascade's threshold (kmc_pass_cascade, before its prefix pass): each row's float32 squared distance to its
+// previous label, times (1 + g) W, rounded up.  A center that can be the row's label, or tie with it, has an exact
+// distance within W of the smallest, which is at most the exact distance to the previous label, which is at most
+// the computed one times (1 + g); so its prefix lower bound cannot exceed this.  A warp per row.
+template <int XR>
+__global__ void __launch_bounds__(kElkanThreads) k_cascade_ub(const float* __restrict__ X, int64_t n, int d,
+                                                             const float* __restrict__ C, int k,
+                                                             const int32_t* __restrict__ lab,
+                                                             const Prep* __restrict__ prep, float* __restrict__ ub) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t)gridDim.x * kElkanWarps;
+    const Window wn(d, prep->rule);
+    for (int64_t row = (int64_t)blockIdx.x * kElkanWarps + (threadIdx.x >> 5); row < n; row += nw) {
+        const float* x = X + row * d;
+        float xv[XR > 0 ? XR : 1];
+        if constexpr (XR > 0) {
+#pragma unroll
+            for (int m = 0; m < XR; m++) {
+                const int j = lane + 32 * m;
+                xv[m] = j < d ? __ldg(x + j) : 0.0f;
             }
         }
+        int l = lab[row] & 0x7fffffff;
+        if (l >= k) l = 0;
+        const float Dl = warp_dist<XR>(xv, x, C + (int64_t)l * d, d, lane);
+        if (lane == 0) ub[row] = __fmul_ru(__fmul_ru(Dl, 1.0f + wn.g), wn.W);
+    }
+}
+
+// The cascade's second stage: every row the prefix pass listed (a surviving center besides its previous label) has
+// its surviving centers (its bits in the prefix pass's mask) scored in full, as k_elkan scores the centers its bounds
+// leave, with the previous label first; the same decision.  A row not listed keeps its previous label: every other
+// center's distance is more than the window above it (its threshold was finite, or every bit would be set).  The
+// list's order does not matter: each row's result is its own.
+template <int XR>
+__global__ void __launch_bounds__(kElkanThreads) k_cascade(const float* __restrict__ X, int64_t n, int d,
+                                                          const float* __restrict__ C, int k,
+                                                          const uint32_t* __restrict__ mask,
+                                                          const uint32_t* __restrict__ srows,
+                                                          const unsigned int* __restrict__ nsrows,
+                                                          int32_t* __restrict__ lab, int4* __restrict__ cands,
+                                                          const Prep* __restrict__ prep,
+                                                          long long* __restrict__ counters) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t)gridDim.x * kElkanWarps;
+    const int kw = (k + 31) / 32;
+    const float W = Window(d, prep->rule).W;
+    const int64_t count = *nsrows;
+    long long visited = 0;
+    for (int64_t idx = (int64_t)blockIdx.x * kElkanWarps + (threadIdx.x >> 5); idx < count; idx += nw) {
+        const int64_t row = srows[idx];
+        if (row >= n) continue;
+        int l = lab[row] & 0x7fffffff;
+        if (l >= k) l = 0;
+        const float* x = X + row * d;
+        float xv[XR > 0 ? XR : 1];
+        if constexpr (XR > 0) {
+#pragma unroll
+            for (int m = 0; m < XR; m++) {
+                const int j = lane + 32 * m;
+                xv[m] = j < d ? __ldg(x + j) : 0.0f;
+            }
+        }
+        const float Dl = warp_dist<XR>(xv, x, C + (int64_t)l * d, d, lane);
+        Best3 b;
+        b.init();
+        b.push(Dl, l);
+        // the row's survivor words, 32 at a time (one per lane); only the nonzero ones are walked
+        const uint32_t* mrow = mask + row * (int64_t)kw;
+        for (int w0 = 0; w0 < kw; w0 += 32) {
+            const int w = w0 + lane;
+            uint32_t word = w < kw ? __ldg(mrow + w) : 0u;
+            if ((l >> 5) == w) word &= ~(1u << (l & 31));
+            visited += __popc(word);
+            unsigned nz = __ballot_sync(0xffffffffu, word != 0u);
+            while (nz) {
+                const int src = __ffs(nz) - 1;
+                nz &= nz - 1;
+                uint32_t bits = __shfl_sync(0xffffffffu, word, src);
+                while (bits) {
+                    const int c = (w0 + src) * 32 + __ffs(bits) - 1;
+                    bits &= bits - 1;
+                    b.push(warp_dist<XR>(xv, x, C + (int64_t)c * d, d, lane), c);
+                }
+            }
+        }
+        if (lane == 0) decide(b, W, k, row, lab, cands);
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) visited += __shfl_xor_sync(0xffffffffu, visited, o);
@@ -181,9 +290,66 @@ cudaError_t run_elkan(const float* X, int64_t n, int d, const float* C, int k, c
     return cudaGetLastError();
 }
 
+template <int XR>
+cudaError_t run_cascade(const float* X, int64_t n, int d, const float* C, int k, const CascadeState& cs,
+                        int32_t* lab, int4* cands, const Prep* prep, long long* counters, bool threshold,
+                        cudaStream_t st) {
+    int64_t blocks = (n + kElkanWarps - 1) / kElkanWarps;
+    const int64_t cap = (int64_t)num_sms() * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    if (threshold)
+        k_cascade_ub<XR><<<(int)blocks, kElkanThreads, 0, st>>>(X, n, d, C, k, lab, prep, cs.ub);
+    else
+        k_cascade<XR><<<(int)blocks, kElkanThreads, 0, st>>>(X, n, d, C, k, cs.mask, cs.srows, cs.nsrows, lab,
+                                                             cands, prep, counters);
+    return cudaGetLastError();
+}
+
+cudaError_t cascade_dispatch(const float* X, int64_t n, int d, const float* C, int k, const CascadeState& cs,
+                             int32_t* lab, int4* cands, const Prep* prep, long long* counters, bool threshold,
+                             cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    const int m = (d + 31) / 32;
+#define KMC_CASCADE(XR) run_cascade<XR>(X, n, d, C, k, cs, lab, cands, prep, counters, threshold, st)
+    if (m <= 4) return KMC_CASCADE(4);
+    if (m <= 8) return KMC_CASCADE(8);
+    if (m <= 16) return KMC_CASCADE(16);
+    return KMC_CASCADE(0);
+#undef KMC_CASCADE
+}
+
 }  // namespace
 
 int64_t a256e(int64_t v) { return (v + 255) / 256 * 256; }
+
+size_t cascade_bytes(int64_t n, int k) {
+    const int64_t nn = n > 0 ? n : 1;
+    return (size_t)(256 + a256e(nn * 4) + a256e(nn * ((k + 31) / 32) * 4) + a256e(nn * 4));
+}
+
+CascadeState carve_cascade(void* base, int64_t n, int k) {
+    const int64_t nn = n > 0 ? n : 1;
+    CascadeState c;
+    char* p = static_cast<char*>(base);
+    c.nsrows = reinterpret_cast<unsigned int*>(p);
+    c.ub = reinterpret_cast<float*>(p + 256);
+    c.mask = reinterpret_cast<uint32_t*>(p + 256 + a256e(nn * 4));
+    c.srows = reinterpret_cast<uint32_t*>(p + 256 + a256e(nn * 4) + a256e(nn * ((k + 31) / 32) * 4));
+    return c;
+}
+
+cudaError_t launch_cascade_ub(const float* X, int64_t n, int d, const float* C, int k, const CascadeState& cs,
+                              const int32_t* lab, const Prep* prep, cudaStream_t st) {
+    cudaError_t e = cudaMemsetAsync(cs.nsrows, 0, sizeof(unsigned int), st);
+    if (e != cudaSuccess) return e;
+    return cascade_dispatch(X, n, d, C, k, cs, const_cast<int32_t*>(lab), nullptr, prep, nullptr, true, st);
+}
+
+cudaError_t launch_cascade(const float* X, int64_t n, int d, const float* C, int k, const CascadeState& cs,
+                           int32_t* lab, int4* cands, const Prep* prep, long long* counters, cudaStream_t st) {
+    return cascade_dispatch(X, n, d, C, k, cs, lab, cands, prep, counters, false, st);
+}
 
 size_t elkan_bytes(int64_t n, int d, int k) {
     const int64_t nn = n > 0 ? n : 1;

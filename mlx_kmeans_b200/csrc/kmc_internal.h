@@ -134,7 +134,12 @@ struct TcSplit {
     int rule;                 // label rule (Prep::rule): widens the window
     int approx;               // exact=False: one bf16 MMA per product (hi parts), no window
     void* lb;                 // Elkan bounds to build (n x k half), or nullptr
-    const float* xsq_lo;      // n: |x|^2 rounded down (with lb)
+    const float* xsq_lo;      // n: |x|^2 rounded down (with lb or mask)
+    void* mask = nullptr;     // the cascade's survivor bits to build (n x ceil(k/32) words), or nullptr
+    const float* ub = nullptr;   // n: the cascade's per-row threshold (with mask)
+    const int32_t* plab = nullptr;   // n: the previous labels (with mask)
+    uint32_t* srows = nullptr;       // the rows with survivors besides that label (with mask), and their count
+    unsigned int* nsrows = nullptr;
 };
 int split_dp(int d);
 int split_kp(int k);
@@ -150,6 +155,21 @@ cudaError_t launch_accum_split(PassArgs a, const RowSplit& rs, const CenterSplit
 
 // Per-center lower bounds between passes for the tensor-core shapes (elkan.cu): caller memory
 // [centers the bounds refer to: k x d float][drift: k float][bounds: n x k half].
+// The prefix-pruning cascade's per-slice state (elkan.cu): caller memory [count of listed rows][threshold: n float]
+// [survivors: n x ceil(k/32) 32-bit words][listed rows: n].
+struct CascadeState {
+    unsigned int* nsrows;
+    float* ub;
+    uint32_t* mask;
+    uint32_t* srows;
+};
+size_t cascade_bytes(int64_t n, int k);
+CascadeState carve_cascade(void* base, int64_t n, int k);
+cudaError_t launch_cascade_ub(const float* X, int64_t n, int d, const float* C, int k, const CascadeState& cs,
+                              const int32_t* lab, const Prep* prep, cudaStream_t st);
+cudaError_t launch_cascade(const float* X, int64_t n, int d, const float* C, int k, const CascadeState& cs,
+                           int32_t* lab, int4* cands, const Prep* prep, long long* counters, cudaStream_t st);
+
 struct ElkanState {
     float* cprev;
     float* drift;

@@ -56,6 +56,14 @@ def mixture_params(cfg):
     raise ValueError(f"unknown configuration {cfg}")
 
 
+def column_scales(d, r, seed):
+    """Per-column factors r^p(j), p a permutation from default_rng(seed): applied to a configuration's rows they
+    give data whose column spread falls off geometrically in an unordered way (the variance structure of SIFT-like
+    descriptors), the case the prefix-pruning cascade is for."""
+    p = np.random.default_rng(seed + 0x5C).permutation(d)
+    return (float(r) ** p).astype(np.float32)
+
+
 def shard_range(n_total, rank, world, align=None):
     """Contiguous rows [lo, hi) of rank `rank` of `world`; every boundary a multiple of `align` (default: the
     library's row block, so the totals are bit-identical for any number of GPUs)."""
