@@ -73,17 +73,32 @@ __device__ inline void exchange_cta(long long* __restrict__ totals, int64_t W, i
         __syncthreads();
         return;
     }
-    // four values per thread per round: 4 x world independent loads in flight over NVLink
-    for (int64_t e = e0 + tid; e < e1; e += 4 * (int64_t)nt) {
-        long long s[4] = {0, 0, 0, 0};
-        for (int r = 0; r < world; r++) {
-            const long long* slot = reinterpret_cast<const long long*>(reinterpret_cast<const char*>(peers[r]) + slot_off);
+    // Two values per thread per round, and the values of up to eight ranks requested before any is added: all of
+    // those loads are in flight over NVLink together, so the sum costs one round trip per eight ranks rather than
+    // one per rank (an add that waits on each load before the next is issued serialises the ranks)
+    constexpr int R = 8, U = 2;
+    for (int64_t e = e0 + tid; e < e1; e += U * (int64_t)nt) {
+        long long s[U] = {};
+        for (int r0 = 0; r0 < world; r0 += R) {
+            const long long* slot[R];
 #pragma unroll
-            for (int u = 0; u < 4; u++)
-                if (e + (int64_t)u * nt < e1) s[u] += slot[e + (int64_t)u * nt];
+            for (int j = 0; j < R; j++)
+                slot[j] = r0 + j < world
+                              ? reinterpret_cast<const long long*>(reinterpret_cast<const char*>(peers[r0 + j]) + slot_off)
+                              : nullptr;
+            long long v[R][U];
+#pragma unroll
+            for (int j = 0; j < R; j++)
+#pragma unroll
+                for (int u = 0; u < U; u++)
+                    v[j][u] = (slot[j] != nullptr && e + (int64_t)u * nt < e1) ? slot[j][e + (int64_t)u * nt] : 0;
+#pragma unroll
+            for (int j = 0; j < R; j++)
+#pragma unroll
+                for (int u = 0; u < U; u++) s[u] += v[j][u];
         }
 #pragma unroll
-        for (int u = 0; u < 4; u++)
+        for (int u = 0; u < U; u++)
             if (e + (int64_t)u * nt < e1) totals[e + (int64_t)u * nt] = s[u];
     }
     __syncthreads();
